@@ -1,0 +1,362 @@
+#!/usr/bin/env python3
+"""Benchmark of the PLaMo-3 token loop on B200.
+
+Metric: batch-1 greedy decode tok/s of the 8B-shaped model
+(profile 8b: hidden 4096, 32 layers, 32/4 heads x 128, intermediate 16384,
+vocab 107520) after a 455-token prompt, with the fraction of the HBM roofline;
+prefill tok/s; and aggregate tok/s of data-parallel replicas at N GPUs.
+
+One step = one decode token through every layer (one CUDA-graph launch).
+Weights are seeded synthetic BF16 (N(0, 0.02) stand-in, norms 1.0) generated
+in HBM; every step streams 16.2 GB of weights, far above the 126 MB L2, so no
+L2 flush is needed between steps. At N > 1 every rank runs an independent
+replica (own prompt) with no collective on the data path; rank 0 prints the
+aggregate (N x steps / max-over-ranks device time).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import ctypes
+import datetime
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "plamo-3-translate.c_b200")
+ORACLE = os.path.join(ROOT, "oracle", "liboracle.so")
+PROMPT = 455
+METRIC = "bs1 decode tok/s (8B-shaped)"
+
+
+def load_package():
+    spec = importlib.util.spec_from_file_location(
+        "plamo_b200", os.path.join(PKG_DIR, "__init__.py"), submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["plamo_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM-style copy)"
+    return 6650.0, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != self.gpu:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sms)) if sms else None,
+                "sm_max_mhz": max(maxes) if maxes else None, "samples": len(sms),
+                "reasons": sorted(reasons)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local, dist
+
+
+def reduce_max(dist, value):
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def oracle_lib():
+    if not os.path.exists(ORACLE):
+        subprocess.run(["make", "-C", os.path.join(ROOT, "oracle")], check=True,
+                       capture_output=True)
+    lib = ctypes.CDLL(ORACLE)
+    P, U64 = ctypes.c_void_p, ctypes.c_uint64
+    lib.plamo_forward.restype, lib.plamo_forward.argtypes = ctypes.c_int, [P, U64]
+    lib.plamo_prefill.restype, lib.plamo_prefill.argtypes = ctypes.c_int, [P, P, U64, P]
+    lib.plamo_argmax.restype, lib.plamo_argmax.argtypes = U64, [P, U64]
+    lib.oracle_set_threads.argtypes = [ctypes.c_int]
+    lib.oracle_synthetic_bf16.argtypes = [P, U64, U64, ctypes.c_float, ctypes.c_float, ctypes.c_int]
+    return lib
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def oracle_decode_rate(pkg, hm, tokens, prompt_tokens, threads):
+    """C oracle (restatement of the reference CPU path) decode tok/s on `hm`."""
+    lib = oracle_lib()
+    lib.oracle_set_threads(threads)
+    ids = np.random.default_rng(1).integers(3, 100000, size=prompt_tokens).astype(np.uint32)
+    states = np.zeros((prompt_tokens, hm.profile.hidden), dtype=np.float32)
+    assert lib.plamo_prefill(hm.ptr, ids.ctypes.data, prompt_tokens, states.ctypes.data) == 1
+    tok = int(lib.plamo_argmax(hm.model.logits, hm.profile.vocab))
+    t0 = time.perf_counter()
+    for _ in range(tokens):
+        assert lib.plamo_forward(hm.ptr, tok) == 1
+        tok = int(lib.plamo_argmax(hm.model.logits, hm.profile.vocab))
+    return tokens / (time.perf_counter() - t0)
+
+
+def host_model_for_oracle(pkg, profile, seed, threads):
+    """Weights generated on the host by the oracle's copy of the generator."""
+    lib = oracle_lib()
+    hm = pkg.HostModel(profile, full_capacity=8208)
+    for k, (addr, count, name) in enumerate(hm.tensor_ranges()):
+        mean, std = pkg.synthetic_parameters(name)
+        lib.oracle_synthetic_bf16(addr, count, seed * 1000003 + k, mean, std, threads)
+    return hm
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the reference CPU path of this loop (its C oracle
+    restatement; the AArch64/Darwin original cannot run on this host) timed on
+    the host cores, same metric and workload."""
+    if rank != 0:
+        return
+    pkg = load_package()
+    threads = host_threads()
+    profile = pkg.PROFILES["8b"]
+    hm = host_model_for_oracle(pkg, profile, seed=4, threads=threads)
+    sample_prompt = 4
+    lib = oracle_lib()
+    lib.oracle_set_threads(threads)
+    ids = np.random.default_rng(1).integers(3, 100000, size=sample_prompt).astype(np.uint32)
+    states = np.zeros((sample_prompt, profile.hidden), dtype=np.float32)
+    assert lib.plamo_prefill(hm.ptr, ids.ctypes.data, sample_prompt, states.ctypes.data) == 1
+    tok = int(lib.plamo_argmax(hm.model.logits, profile.vocab))
+    for _ in range(args.warmup):
+        assert lib.plamo_forward(hm.ptr, tok) == 1
+        tok = int(lib.plamo_argmax(hm.model.logits, profile.vocab))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        assert lib.plamo_forward(hm.ptr, tok) == 1
+        tok = int(lib.plamo_argmax(hm.model.logits, profile.vocab))
+    seconds = time.perf_counter() - t0
+    value = args.steps / seconds
+    sample = (f"8B-shaped decode, {args.steps} tokens after a {sample_prompt}-token prompt "
+              f"(+{args.warmup} warm-up); KV context {sample_prompt + args.warmup}.."
+              f"{sample_prompt + args.warmup + args.steps} instead of 455..519 (KV is <0.5% of "
+              "the bytes per token)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * seconds / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("reference CPU path = C restatement of the reference's AArch64 assembly "
+                 "(oracle/); the original is Darwin/AArch64 and cannot run on this x86 host"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(world):
+    return {"workload": "8b-decode: plamo-3 profile 8b, 455-token prompt then greedy decode, batch 1",
+            "model": "plamo-3-8b-shaped (random init)", "global_batch": world, "seq_len": PROMPT,
+            "parallelism": f"dp{world} (independent replicas)",
+            "l2": "inputs larger than L2 (16.2 GB of weights streamed per step)"}
+
+
+def run_ours(args, world, rank, local, dist):
+    pkg = load_package()
+    lib = pkg.load()
+    profile = pkg.PROFILES["8b"]
+    be = pkg.Backend(device=local, max_context=8192 + 16, max_prefill=4096)
+    ctx = be.ctx
+    hm = pkg.HostModel(profile, weights="synthetic", full_capacity=8208)
+    be.preload_synthetic(hm, seed=4)
+    be.prepare(hm)
+    ids = np.random.default_rng(1 + rank).integers(3, 100000, size=PROMPT).astype(np.uint32)
+
+    # Prefill (timed on the device; second run after a warm-up run).
+    nxt = ctypes.c_uint32()
+    prefill_s = None
+    for _ in range(2):
+        lib.plamo_cuda_reset_request(ctx, hm.ptr)
+        before = be.info().gpu_seconds
+        assert lib.plamo_cuda_prefill_greedy(ctx, hm.ptr, ids.ctypes.data, PROMPT,
+                                             ctypes.byref(nxt)) == 1, be.info().note
+        prefill_s = be.info().gpu_seconds - before
+    prefill_rate = world * PROMPT / reduce_max(dist, prefill_s)
+
+    # Decode: warm-up, then exactly K graph launches between barriers.
+    assert lib.plamo_cuda_time_decode(ctx, hm.ptr, args.warmup) > 0, be.info().note
+    barrier(dist)
+    lib.plamo_cuda_synchronize(ctx)
+    clocks = ClockSampler(local)
+    launches0 = lib.plamo_cuda_kernel_launches(ctx)
+    ms = lib.plamo_cuda_time_decode(ctx, hm.ptr, args.steps)
+    launches = lib.plamo_cuda_kernel_launches(ctx) - launches0
+    clock_info = clocks.stop()
+    assert ms > 0, be.info().note
+    lib.plamo_cuda_synchronize(ctx)
+    barrier(dist)
+    ms_max = reduce_max(dist, ms)
+    ms_per_step = ms_max / args.steps
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # Algorithmic bytes of one step: weights, norms, one embedding row, and
+    # the K/V rows read by attention at the mean context of the timed steps.
+    ctx_mean = PROMPT + args.warmup + (args.steps + 1) / 2.0
+    kv_bytes = profile.layers * ctx_mean * profile.kh * profile.dim * 4 * 2
+    step_bytes = (profile.weight_bytes_per_token() + profile.norm_bytes_per_token() +
+                  2 * profile.hidden + kv_bytes)
+    peak, peak_src = measured_peaks()
+    achieved = step_bytes / (ms_per_step / 1000.0) / 1e9
+
+    # Standalone projection kernel at the largest layer shape (gate_up,
+    # 32768 x 4096, 268 MB > L2): CUDA events around back-to-back launches.
+    rows, cols = 2 * profile.inter, profile.hidden
+    dw = lib.plamo_cuda_device_alloc(ctx, rows * cols * 2)
+    dx = lib.plamo_cuda_device_alloc(ctx, cols * 4)
+    dy = lib.plamo_cuda_device_alloc(ctx, rows * 4)
+    lib.plamo_cuda_fill_synthetic_bf16(ctx, dw, rows * cols, 99, 0.0, 0.02)
+    lib.plamo_cuda_fill_synthetic_f32(ctx, dx, cols, 98, 0.0, 1.0)
+    lib.plamo_cuda_time_gemv(ctx, dw, dx, dy, rows, cols, 5)
+    gemv_ms = lib.plamo_cuda_time_gemv(ctx, dw, dx, dy, rows, cols, 50) / 50
+    gemv_bytes = rows * cols * 2 + cols * 4 + rows * 4
+    for p in (dw, dx, dy):
+        lib.plamo_cuda_device_free(ctx, p)
+
+    # End to end through the public request API: host ids in, each token's
+    # id back on the host (pinned H2D of the token, D2H of the next id).
+    lib.plamo_cuda_reset_request(ctx, hm.ptr)
+    out = np.zeros(args.steps + 1, dtype=np.uint32)
+    timing = pkg._abi.CudaTiming()
+    barrier(dist)
+    n = lib.plamo_cuda_generate(ctx, hm.ptr, ids.ctypes.data, PROMPT, args.steps + 1,
+                                out.ctypes.data, pkg._abi.TOKEN_CALLBACK(), None,
+                                ctypes.byref(timing))
+    assert n > 0, be.info().note
+    steps_e2e = max(int(timing.decode_steps), 1)
+    e2e_s = reduce_max(dist, timing.decode_seconds / steps_e2e)
+    e2e_value = world / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        blob = np.empty(hm.blob_bytes // 2, dtype=np.uint16)
+        host = pkg.HostModel(profile, weights=blob, full_capacity=8208)
+        for (ka, count, _), (kb, _, _) in zip(hm.tensor_ranges(), host.tensor_ranges()):
+            assert lib.plamo_cuda_read_weights(ctx, ka, kb, 2 * count) == 1
+        tokens, prompt = 3, 4
+        rate = oracle_decode_rate(pkg, host, tokens, prompt, threads)
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"8B-shaped decode, {tokens} tokens after a {prompt}-token prompt "
+                         "(same weights; C restatement of the reference CPU path, row-split "
+                         "threads)"}
+        del host, blob
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(world),
+            "prefill_tok_s": prefill_rate,
+            "roofline": {"bound": "hbm", "kernel": "decode step (one CUDA graph launch per token)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "algorithmic_bytes": step_bytes, "peak_source": peak_src},
+            "gemv_roofline": {"bound": "hbm", "kernel": "gemv 32768x4096 bf16 (gate_up shape)",
+                              "achieved": gemv_bytes / (gemv_ms / 1000) / 1e9, "peak": peak,
+                              "unit": "GB/s", "frac": gemv_bytes / (gemv_ms / 1000) / 1e9 / peak,
+                              "ms": gemv_ms},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4, "api": "plamo_cuda_generate (per-token host round trip)"},
+            "gpu_launches": int(launches),
+            "clocks": clock_info,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    be.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 1 or args.steps < 1:
+        ap.error("steps and warmup must be positive")
+    if args.impl == "reference":
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
+    world, rank, local, dist = dist_setup(args.gpus)
+    try:
+        run_ours(args, world, rank, local, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,168 @@
+/* B200 (sm_100a) backend of the PLaMo-3 token loop: C ABI.
+ *
+ * Drop-in for the reference's GPU backend interface (reference
+ * runtime/metal.h:48-88). Each plamo_cuda_* entry replaces the plamo_metal_*
+ * entry of the same suffix with the same arguments, return convention and
+ * ownership rules, so the reference's engine (runtime/engine.c call sites
+ * :180,187,234,243,264,302,304,369,462,481,495,540,562,597) binds to it by a
+ * rename. The remaining entries are additions a CUDA device needs (explicit
+ * host/device KV synchronisation, on-device greedy selection, the request
+ * loop over token ids, timing and synthetic weights for benchmarks).
+ *
+ * Return convention of forward/prefill/verify/commit/linear/mlp, as
+ * reference runtime/metal.h:63-74: 1 success; 0 declined with no state
+ * changed (the caller may use another path); -1 executed and failed (do not
+ * retry: KV may have advanced).
+ *
+ * Threading: one context is owned by one host thread; calls are serialised.
+ */
+#ifndef PLAMO_CUDA_H
+#define PLAMO_CUDA_H
+#include "plamo_model.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Largest candidate block of one verification (reference runtime/metal.h:75). */
+enum { PLAMO_CUDA_VERIFY_MAX = 16 };
+
+struct plamo_cuda_config {
+    int device;               /* CUDA device ordinal */
+    uint64_t max_context;     /* KV rows kept per full-attention layer; 0 = 8192 + 16 */
+    uint64_t max_prefill;     /* largest prompt of one prefill call; 0 = 4096 */
+    uint64_t reserve;         /* HBM bytes left unallocated; 0 = 1 GiB */
+    unsigned copy_kv_to_host; /* 1: keep the host K/V/rotated-K arrays current after
+                                 every call (reference semantics, slower); 0: device
+                                 KV is canonical and plamo_cuda_sync_host copies it */
+};
+
+struct plamo_cuda_info {
+    char device[128], note[256];
+    uint64_t launches, graph_launches, forwards, prefills, verification_batches,
+        verified_tokens, committed_tokens, declines, errors;
+    uint64_t weight_bytes, kv_bytes, workspace_bytes, allocated_bytes;
+    uint64_t sm_count;
+    double gpu_seconds; /* device time of completed forward/prefill/verify calls */
+};
+
+struct plamo_cuda;
+
+/* reference runtime/metal.h:48: NULL + message in error[cap] on failure. */
+struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *, char *error, size_t cap);
+/* reference runtime/metal.h:49 */
+void plamo_cuda_close(struct plamo_cuda *);
+/* reference runtime/metal.h:50: releases scratch not needed by prepared models. */
+void plamo_cuda_maintain(struct plamo_cuda *);
+/* reference runtime/metal.h:51 */
+void plamo_cuda_get_info(const struct plamo_cuda *, struct plamo_cuda_info *);
+/* reference runtime/metal.h:55: copy host BF16 bytes [src, src+bytes) into HBM
+   and remember the mapping. 0 on allocation or copy failure. */
+int plamo_cuda_preload(struct plamo_cuda *, const void *src, uint64_t bytes);
+/* reference runtime/metal.h:58: touch every resident byte once on the device. */
+int plamo_cuda_warm_cache(struct plamo_cuda *);
+/* reference runtime/metal.h:62: allocate device KV, RoPE tables and workspace for
+   `model` and resolve each weight pointer to its HBM copy (uploading any weight
+   not preloaded). Must precede forward/prefill/verify on that model. */
+int plamo_cuda_prepare_model(struct plamo_cuda *, struct model *);
+/* reference runtime/metal.h:67: one complete decode step of `token`. On success
+   model->state, ->normalized and ->logits are current on the host. */
+int plamo_cuda_forward(struct plamo_cuda *, struct model *, uint64_t token);
+/* reference runtime/metal.h:73: layer-major prompt. states (tokens x hidden, may
+   be NULL) receives every prompt state; model state/logits are for the last. */
+int plamo_cuda_prefill(struct plamo_cuda *, struct model *, const uint32_t *ids,
+                       uint64_t tokens, float *states);
+/* reference runtime/metal.h:79: run candidates ids[0..tokens) without changing
+   the committed state; next[j] = greedy token after ids[0..j]. */
+int plamo_cuda_verify(struct plamo_cuda *, struct model *, const uint32_t *ids,
+                      uint64_t tokens, uint32_t *next);
+/* reference runtime/metal.h:81: commit candidate `index` of the last verify; indices
+   must be committed in order 0,1,2,... */
+int plamo_cuda_commit(struct plamo_cuda *, struct model *, uint64_t index);
+/* reference runtime/metal.h:85: synchronous dense projection of host buffers. */
+int plamo_cuda_linear(struct plamo_cuda *, const struct plamo_matmul *);
+/* reference runtime/metal.h:88: complete MLP branch (norm, gate_up, SwiGLU, down,
+   norm, residual) applied in place to states[tokens x hidden]. */
+int plamo_cuda_mlp(struct plamo_cuda *, const struct mlp *, float *states, uint64_t tokens);
+
+/* ---- additions a discrete GPU needs ---- */
+
+/* Copy the device-canonical KV rows, rotated keys (local positions, as the
+   reference's rotation cache holds them), state, normalized and logits of
+   `model` into its host arrays, and set the host counters. */
+int plamo_cuda_sync_host(struct plamo_cuda *, struct model *);
+/* Declare the host K/V arrays of `model` canonical: the next call uploads
+   rows [0, count) of every layer (use after writing host KV directly, e.g. by
+   a CPU path or a prompt-cache restore that kept the same counts). A host
+   count that differs from the device's is detected without this call. */
+int plamo_cuda_invalidate(struct plamo_cuda *, struct model *);
+/* Decode `token` and select the next token on the device (first maximal
+   logit, reference src/token.s:35-63). Host state/logits are not copied.
+   *next = UINT32_MAX when a logit is NaN. */
+int plamo_cuda_forward_greedy(struct plamo_cuda *, struct model *, uint64_t token,
+                              uint32_t *next);
+/* Prefill and select the first generated token on the device. */
+int plamo_cuda_prefill_greedy(struct plamo_cuda *, struct model *, const uint32_t *ids,
+                              uint64_t tokens, uint32_t *next);
+/* Greedy request loop over token ids (reference runtime/engine.c:428-617 without
+   the tokenizer): prefill, then decode until max_tokens or a stop id (1, 16).
+   out[] receives the emitted ids; returns their count, or -1 on failure.
+   on_token (may be NULL) sees each id as soon as it is on the host; a zero
+   return cancels. */
+struct plamo_cuda_timing {
+    double prefill_seconds, decode_seconds, first_token_seconds;
+    uint64_t prompt_tokens, completion_tokens, decode_steps;
+    const char *finish_reason;
+};
+int64_t plamo_cuda_generate(struct plamo_cuda *, struct model *, const uint32_t *ids,
+                            uint64_t tokens, uint64_t max_tokens, uint32_t *out,
+                            int (*on_token)(uint32_t id, void *context), void *context,
+                            struct plamo_cuda_timing *timing);
+/* One decoder layer of one decode step on a host hidden vector, in place
+   (reference src/layer.s:8-48 plamo_layer): appends one KV row to layer
+   `index` and advances only that layer. */
+int plamo_cuda_layer(struct plamo_cuda *, struct model *, uint64_t index, float *state);
+/* Reset the request state of `model` (all KV counts to zero) on host and device,
+   like the reference's plamo_reset_request (runtime/engine.c:46-55). */
+void plamo_cuda_reset_request(struct plamo_cuda *, struct model *);
+
+/* Standalone BF16 GEMV on device buffers: y[rows] = W[rows, cols] . x[cols]
+   with FP32 accumulation (the decode projection kernel). Asynchronous on the
+   context's stream. */
+int plamo_cuda_gemv_device(struct plamo_cuda *, const uint16_t *w, const float *x, float *y,
+                           uint64_t rows, uint64_t cols);
+
+/* ---- device memory and timing helpers for tests and benchmarks ---- */
+void *plamo_cuda_device_alloc(struct plamo_cuda *, uint64_t bytes);
+void plamo_cuda_device_free(struct plamo_cuda *, void *);
+int plamo_cuda_copy_to_device(struct plamo_cuda *, void *dst, const void *src, uint64_t bytes);
+int plamo_cuda_copy_to_host(struct plamo_cuda *, void *dst, const void *src, uint64_t bytes);
+int plamo_cuda_synchronize(struct plamo_cuda *);
+/* Device time in milliseconds of `repeats` launches of the decode step graph
+   of `model` (tokens fed back from the on-device argmax), measured with CUDA
+   events on the launching stream. */
+double plamo_cuda_time_decode(struct plamo_cuda *, struct model *, uint64_t repeats);
+/* Same for the standalone GEMV over `repeats` launches. */
+double plamo_cuda_time_gemv(struct plamo_cuda *, const uint16_t *w, const float *x, float *y,
+                            uint64_t rows, uint64_t cols, uint64_t repeats);
+/* Kernels launched by the library since open (counts every launch and every
+   kernel node of a launched graph). */
+uint64_t plamo_cuda_kernel_launches(const struct plamo_cuda *);
+
+/* Synthetic BF16 weights generated on the device: value(i) =
+   mean + std * z(seed, i), z = (sum of 12 hash bytes - 1530) / 256, rounded to
+   BF16 (plamo_synthetic.h restates it for the host). Registers the range
+   [host_key, host_key + count*2) like plamo_cuda_preload without reading it. */
+int plamo_cuda_preload_synthetic(struct plamo_cuda *, const void *host_key, uint64_t count,
+                                 uint64_t seed, float mean, float std);
+/* Copy the HBM bytes registered under host key range [key, key+bytes) to dst. */
+int plamo_cuda_read_weights(struct plamo_cuda *, const void *key, void *dst, uint64_t bytes);
+int plamo_cuda_fill_synthetic_bf16(struct plamo_cuda *, uint16_t *device_dst, uint64_t count,
+                                   uint64_t seed, float mean, float std);
+int plamo_cuda_fill_synthetic_f32(struct plamo_cuda *, float *device_dst, uint64_t count,
+                                  uint64_t seed, float mean, float std);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,1445 @@
+// Host side of the B200 backend: context, HBM weight registry, per-model
+// device state, the decode step as one CUDA graph, the layer-major prompt,
+// speculative verification/commit and the greedy request loop.
+//
+// Interface: include/plamo_cuda.h (drop-in for reference runtime/metal.h).
+#include "../../include/plamo_cuda.h"
+#include "../../include/plamo_synthetic.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "attention.cuh"
+#include "rows.cuh"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+using namespace plamo;
+
+namespace {
+
+constexpr float kPostMixerOffset = 0.2f;                 // reference src/layer.s:51
+constexpr float kPostMlpOffset = 0.08944271909999159f;   // reference src/model.s:112
+constexpr uint64_t kVerifyMax = PLAMO_CUDA_VERIFY_MAX;
+
+struct Range {
+    uintptr_t host;
+    uint64_t bytes;
+    char *dev;
+};
+
+// cos|sin table of one (frequency set, dim, concentration), positions rows.
+struct Rope {
+    std::vector<float> freq;
+    uint64_t dim;
+    uint32_t scale_bits;
+    uint64_t positions;
+    float *dev;
+};
+
+struct DLayer {
+    struct layer *host;
+    const uint16_t *qkv_w, *qn, *kn, *o_w, *pre, *post, *mpre, *mpost, *gu, *down;
+    float *ring_k, *ring_v;
+    uint64_t ring, capacity;
+    int sliding;
+    Rope *rope;
+    float scale;
+    uint64_t appended;  // committed rows of the request (host mirror of d_appended)
+    bool stale;         // host rows are canonical: upload before the next use
+    uint64_t host_hash; // FNV-1a of the newest host K row written by this backend
+};
+
+struct DModel {
+    struct model *host;
+    uint64_t H, QH, KH, D, I, V, L, QW, AW, KVW;
+    const uint16_t *emb, *norm, *head;
+    std::vector<DLayer> layers;
+    uint64_t *d_appended;
+    // decode step
+    float *state[2], *final_state, *normalized, *logits;
+    float *qkv, *q, *attn, *branch, *mid, *part;
+    uint32_t *tickets, *arg_idx, *arg_nan, *d_token, *d_next, *d_error;
+    float *arg_val;
+    uint32_t splits, gemv_grid;
+    // prompt / verification
+    uint64_t tmax;
+    float *p_states, *p_norm, *p_qkv, *p_q, *p_attn, *p_branch, *p_gu, *p_logits, *p_part;
+    uint32_t *p_ids, *p_next, *p_tickets;
+    float *v_kv;  // [L][kVerifyMax][2][KVW]
+    uint64_t verify_count = 0, verify_committed = 0;
+    bool verify_valid = false;
+    // graph
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    uint64_t graph_nodes = 0;
+    std::vector<void *> allocations;
+};
+
+}  // namespace
+
+struct plamo_cuda {
+    int device;
+    cudaStream_t stream;
+    cudaEvent_t ev0, ev1;
+    plamo_cuda_config config;
+    plamo_cuda_info info;
+    std::vector<Range> ranges;
+    std::vector<std::unique_ptr<Rope>> ropes;
+    std::map<struct model *, std::unique_ptr<DModel>> models;
+    uint32_t *pinned_u32;  // small pinned staging (tokens, ids)
+    uint64_t pinned_capacity;
+    int sm_count;
+    bool pdl;
+    int gemv_ctas;
+    uint32_t *sink;
+};
+
+namespace {
+
+bool note(plamo_cuda *c, const char *what, cudaError_t e) {
+    if (e == cudaSuccess) return true;
+    c->info.errors++;
+    snprintf(c->info.note, sizeof c->info.note, "%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+
+uint32_t float_to_bits(float f) {
+    uint32_t b;
+    memcpy(&b, &f, 4);
+    return b;
+}
+
+// ---- exact RoPE tables (host) ------------------------------------------
+// The reference builds its GPU tables on the CPU with its own sin/cos
+// (runtime/metal_model.m:145-175 -> src/rope_table.s, src/trig.s): angle =
+// fp32(position) * freq[j] in FP32, then sin/cos in double by reduction modulo
+// 2*pi and the Taylor series of sin(r)/r and cos(r) to r^16, each rounded to
+// FP32 and multiplied by the concentration in FP32. Restated here so the
+// device tables hold the same bits.
+const double kTwoPi = 6.283185307179586;
+const double kSinSeries[8] = {1.0 / 355687428096000.0, -1.0 / 1307674368000.0,
+                              1.0 / 6227020800.0,      -1.0 / 39916800.0,
+                              1.0 / 362880.0,          -1.0 / 5040.0,
+                              1.0 / 120.0,             -1.0 / 6.0};
+const double kCosSeries[8] = {1.0 / 20922789888000.0, -1.0 / 87178291200.0,
+                              1.0 / 479001600.0,      -1.0 / 3628800.0,
+                              1.0 / 40320.0,          -1.0 / 720.0,
+                              1.0 / 24.0,             -1.0 / 2.0};
+
+void sincos_exact(double angle, float *s, float *c) {
+    double n = std::rint(angle / kTwoPi);
+    double r = std::fma(-n, kTwoPi, angle);
+    double r2 = r * r;
+    double p = kSinSeries[0];
+    for (int k = 1; k < 8; ++k) p = std::fma(p, r2, kSinSeries[k]);
+    p = std::fma(p, r2, 1.0);
+    volatile double sp = p * r;
+    *s = static_cast<float>(sp);
+    p = kCosSeries[0];
+    for (int k = 1; k < 8; ++k) p = std::fma(p, r2, kCosSeries[k]);
+    p = std::fma(p, r2, 1.0);
+    *c = static_cast<float>(p);
+}
+
+void build_rope_rows(const float *freq, uint64_t dim, float scale, uint64_t from, uint64_t to,
+                     float *out) {
+    const uint64_t half = dim / 2;
+    for (uint64_t pos = from; pos < to; ++pos) {
+        float *row = out + (pos - from) * dim;
+        const float p = static_cast<float>(pos);
+        for (uint64_t j = 0; j < half; ++j) {
+            volatile float angle = freq[j] * p;
+            float s, c;
+            sincos_exact(static_cast<double>(angle), &s, &c);
+            volatile float cs = c * scale, ss = s * scale;
+            row[j] = cs;
+            row[half + j] = ss;
+        }
+    }
+}
+
+Rope *get_rope(plamo_cuda *c, const float *freq, uint64_t dim, float scale, uint64_t positions) {
+    const uint32_t bits = float_to_bits(scale);
+    for (auto &r : c->ropes)
+        if (r->dim == dim && r->scale_bits == bits && r->positions >= positions &&
+            !memcmp(r->freq.data(), freq, dim / 2 * sizeof(float)))
+            return r.get();
+    auto r = std::make_unique<Rope>();
+    r->freq.assign(freq, freq + dim / 2);
+    r->dim = dim;
+    r->scale_bits = bits;
+    r->positions = positions;
+    std::vector<float> host(positions * dim);
+    build_rope_rows(freq, dim, scale, 0, positions, host.data());
+    if (!note(c, "rope alloc", cudaMalloc(&r->dev, host.size() * 4))) return nullptr;
+    if (!note(c, "rope copy", cudaMemcpy(r->dev, host.data(), host.size() * 4, cudaMemcpyHostToDevice)))
+        return nullptr;
+    c->info.allocated_bytes += host.size() * 4;
+    c->ropes.push_back(std::move(r));
+    return c->ropes.back().get();
+}
+
+// ---- weight registry -----------------------------------------------------
+const Range *find_range(plamo_cuda *c, const void *p, uint64_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    for (const Range &r : c->ranges)
+        if (a >= r.host && a + bytes <= r.host + r.bytes) return &r;
+    return nullptr;
+}
+const uint16_t *resolve(plamo_cuda *c, const void *p, uint64_t bytes, bool upload) {
+    if (!p) return nullptr;
+    const Range *r = find_range(c, p, bytes);
+    if (!r && upload) {
+        if (!plamo_cuda_preload(c, p, bytes)) return nullptr;
+        r = find_range(c, p, bytes);
+    }
+    if (!r) return nullptr;
+    return reinterpret_cast<const uint16_t *>(r->dev + (reinterpret_cast<uintptr_t>(p) - r->host));
+}
+
+// ---- launches ------------------------------------------------------------
+template <typename... KArgs, typename... Args>
+bool launch(plamo_cuda *c, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+            Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    if (c->pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    c->info.launches++;
+    return note(c, "launch", cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
+template <int PRO, int EPI>
+bool launch_gemv_shape(plamo_cuda *c, const GemvParams &p, int U, uint32_t grid, size_t smem) {
+    switch (U) {
+    case 4: return launch(c, gemv_kernel<PRO, EPI, 4>, dim3(grid), dim3(kGemvThreads), smem, p);
+    case 2: return launch(c, gemv_kernel<PRO, EPI, 2>, dim3(grid), dim3(kGemvThreads), smem, p);
+    case 1: return launch(c, gemv_kernel<PRO, EPI, 1>, dim3(grid), dim3(kGemvThreads), smem, p);
+    default: return launch(c, gemv_kernel<PRO, EPI, 0>, dim3(grid), dim3(kGemvThreads), smem, p);
+    }
+}
+
+template <int PRO, int EPI>
+void set_gemv_smem_limits() {
+    const int max = 227 * 1024;
+    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
+    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
+    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
+    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
+}
+
+// Grid of a projection: one CTA per SM (times the configured factor), fewer
+// when there are fewer output units, more when the per-block partials would
+// not fit in shared memory.
+uint32_t gemv_grid(plamo_cuda *c, uint64_t units, uint64_t cols, int U, int pair, size_t *smem) {
+    uint64_t grid = std::min<uint64_t>(units, static_cast<uint64_t>(c->sm_count) * c->gemv_ctas);
+    if (!grid) grid = 1;
+    const uint64_t segs = U ? cols / (256ull * U) : 1;
+    const uint64_t cols_pad = (cols + 3) & ~3ull;
+    for (;;) {
+        const uint64_t per = (units + grid - 1) / grid;
+        const size_t bytes = (cols_pad + per * segs * pair) * sizeof(float);
+        if (bytes <= 200 * 1024 || grid >= units) {
+            *smem = bytes;
+            return static_cast<uint32_t>(grid);
+        }
+        grid *= 2;
+        if (grid > units) grid = units;
+    }
+}
+
+int gemv_chunks(const void *w, uint64_t cols) {
+    if (reinterpret_cast<uintptr_t>(w) % 16) return 0;
+    if (cols % 1024 == 0) return 4;
+    if (cols % 512 == 0) return 2;
+    if (cols % 256 == 0) return 1;
+    return 0;
+}
+
+template <int PRO, int EPI>
+bool gemv(plamo_cuda *c, GemvParams p, uint32_t *grid_out = nullptr) {
+    const int U = gemv_chunks(p.w, p.cols);
+    const int pair = EPI == EPI_SWIGLU ? 2 : 1;
+    size_t smem = 0;
+    const uint32_t grid = gemv_grid(c, p.rows / pair, p.cols, U, pair, &smem);
+    if (grid_out) *grid_out = grid;
+    return launch_gemv_shape<PRO, EPI>(c, p, U, grid, smem);
+}
+
+bool gemm(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys,
+          uint64_t T, uint64_t R, uint64_t K) {
+    if (!T || !R) return true;
+    dim3 grid((R + kGemmBN - 1) / kGemmBN, (T + kGemmBM - 1) / kGemmBM);
+    return launch(c, gemm_simt_kernel, grid, dim3(256), 0, X, xs, W, Y, ys, T, R, K);
+}
+
+AttnLayer attn_layer(const DModel *m, uint64_t l) {
+    const DLayer &L = m->layers[l];
+    AttnLayer a;
+    a.ring_k = L.ring_k;
+    a.ring_v = L.ring_v;
+    a.ring_k_w = L.ring_k;
+    a.ring_v_w = L.ring_v;
+    a.appended = m->d_appended + l;
+    a.ring = L.ring;
+    a.capacity = L.capacity;
+    a.sliding = L.sliding;
+    a.table = L.rope->dev;
+    a.positions = L.rope->positions;
+    a.qn = L.qn;
+    a.kn = L.kn;
+    return a;
+}
+
+uint64_t layer_count(const DLayer &L) {
+    return L.sliding ? std::min(L.appended, L.capacity) : L.appended;
+}
+
+void *dalloc(plamo_cuda *c, DModel *m, uint64_t bytes) {
+    void *p = nullptr;
+    if (!bytes) bytes = 16;
+    if (!note(c, "cudaMalloc", cudaMalloc(&p, bytes))) return nullptr;
+    cudaMemset(p, 0, bytes);
+    m->allocations.push_back(p);
+    c->info.allocated_bytes += bytes;
+    return p;
+}
+
+void free_model(plamo_cuda *c, DModel *m) {
+    if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    for (void *p : m->allocations) cudaFree(p);
+    m->allocations.clear();
+    (void)c;
+}
+
+DModel *find_model(plamo_cuda *c, struct model *model) {
+    auto it = c->models.find(model);
+    return it == c->models.end() ? nullptr : it->second.get();
+}
+
+// Bring the device KV in line with the host descriptors: a host count of
+// zero resets the layer (the engine's plamo_reset_request); any other count
+// the device does not hold means the host wrote the rows itself (for example
+// a prompt-cache restore), so they are uploaded as rows 0..count-1.
+uint64_t row_hash(const float *row, uint64_t n) {
+    const unsigned char *p = reinterpret_cast<const unsigned char *>(row);
+    uint64_t h = 14695981039346656037ull;
+    for (uint64_t i = 0; i < n * 4; ++i) {
+        h ^= p[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+uint64_t newest_row_hash(const DModel *m, const DLayer &L) {
+    const struct cache *hc = L.host->mixer->cache;
+    if (!hc->count) return 0;
+    return row_hash(hc->k + (hc->count - 1) * m->KVW, m->KVW);
+}
+
+bool reconcile(plamo_cuda *c, DModel *m) {
+    bool changed = false;
+    for (uint64_t l = 0; l < m->L; ++l) {
+        DLayer &L = m->layers[l];
+        const struct cache *hc = L.host->mixer->cache;
+        const uint64_t dc = layer_count(L);
+        // With host copies enabled, a host write that kept the count is seen
+        // through the newest row's hash.
+        if (!L.stale && c->config.copy_kv_to_host && hc->count && hc->count == dc &&
+            newest_row_hash(m, L) != L.host_hash)
+            L.stale = true;
+        if (hc->count == dc && !L.stale) continue;
+        changed = true;
+        L.stale = false;
+        if (hc->count > L.ring || hc->count > L.capacity) return false;
+        if (hc->count) {
+            const uint64_t bytes = hc->count * m->KVW * 4;
+            if (!note(c, "kv upload", cudaMemcpyAsync(L.ring_k, hc->k, bytes, cudaMemcpyHostToDevice, c->stream)) ||
+                !note(c, "kv upload", cudaMemcpyAsync(L.ring_v, hc->v, bytes, cudaMemcpyHostToDevice, c->stream)))
+                return false;
+        }
+        L.appended = hc->count;
+    }
+    if (changed) {
+        std::vector<uint64_t> counts(m->L);
+        for (uint64_t l = 0; l < m->L; ++l) counts[l] = m->layers[l].appended;
+        if (!note(c, "counter upload", cudaMemcpyAsync(m->d_appended, counts.data(), m->L * 8,
+                                                       cudaMemcpyHostToDevice, c->stream)))
+            return false;
+        if (!note(c, "sync", cudaStreamSynchronize(c->stream))) return false;
+    }
+    return true;
+}
+
+// Mirror the CPU path's descriptor updates after `rows` committed rows.
+void publish_counts(DModel *m, uint64_t rows) {
+    for (uint64_t l = 0; l < m->L; ++l) {
+        DLayer &L = m->layers[l];
+        L.appended += rows;
+        struct cache *hc = L.host->mixer->cache;
+        struct rotation *r = L.host->mixer->rotation;
+        hc->count = layer_count(L);
+        r->processed_count = hc->count;
+        r->scale_bits = float_to_bits(L.scale);
+    }
+}
+
+// Rows a decode/prefill of `tokens` would need; false when a full-attention
+// cache cannot take them (the reference declines: src/cache.s global full).
+bool fits(const DModel *m, uint64_t tokens) {
+    for (const DLayer &L : m->layers) {
+        if (!L.sliding && L.appended + tokens > L.capacity) return false;
+        if (!L.sliding && L.appended + tokens > L.ring) return false;
+        if (L.sliding && std::min(L.appended + tokens, L.capacity) > L.rope->positions) return false;
+        if (!L.sliding && L.appended + tokens > L.rope->positions) return false;
+    }
+    return true;
+}
+
+// ---- decode step -----------------------------------------------------------
+bool record_decode(plamo_cuda *c, DModel *m) {
+    int s = 0;
+    AttnShape shape{1, m->QH, m->KH, m->D, m->QW};
+    const uint64_t G = m->QH / m->KH;
+    const size_t attn_smem = attention_smem_bytes(G, m->D);
+    for (uint64_t l = 0; l < m->L; ++l) {
+        const DLayer &L = m->layers[l];
+        GemvParams p{};
+        p.w = L.qkv_w;
+        p.rows = m->QW;
+        p.cols = m->H;
+        p.norm2 = L.pre;
+        p.off2 = 1.0f;
+        p.y = m->qkv;
+        p.error = m->d_error;
+        bool ok;
+        if (l == 0) {
+            p.embedding = m->emb;
+            p.token = m->d_token;
+            p.vocab = m->V;
+            p.state_out = m->state[s];
+            ok = gemv<PRO_EMBED_NORM, EPI_STORE>(c, p);
+        } else {
+            p.state_in = m->state[s];
+            p.branch = m->branch;
+            p.norm1 = m->layers[l - 1].mpost;
+            p.off1 = kPostMlpOffset;
+            p.state_out = m->state[s ^ 1];
+            s ^= 1;
+            ok = gemv<PRO_RESID_NORM, EPI_STORE>(c, p);
+        }
+        if (!ok) return false;
+        AttnLayer al = attn_layer(m, l);
+        if (!launch(c, qk_prep_kernel, dim3(m->QH + m->KH, 1), dim3(128), 0, m->qkv, m->q, al, shape))
+            return false;
+        AttnParams ap{al, shape, m->q, m->qkv, m->attn, m->part, m->tickets, m->splits};
+        if (!launch(c, attention_kernel, dim3(m->KH, 1, m->splits), dim3(kAttnThreads), attn_smem, ap))
+            return false;
+        if (!launch(c, kv_store_kernel, dim3(1), dim3(256), 0, al, shape, static_cast<const float *>(m->qkv),
+                    uint64_t{0}))
+            return false;
+        GemvParams o{};
+        o.w = L.o_w;
+        o.rows = m->H;
+        o.cols = m->AW;
+        o.x = m->attn;
+        o.y = m->branch;
+        if (!gemv<PRO_X, EPI_STORE>(c, o)) return false;
+        GemvParams g{};
+        g.w = L.gu;
+        g.rows = 2 * m->I;
+        g.cols = m->H;
+        g.state_in = m->state[s];
+        g.branch = m->branch;
+        g.norm1 = L.post;
+        g.off1 = kPostMixerOffset;
+        g.norm2 = L.mpre;
+        g.off2 = 1.0f;
+        g.state_out = m->state[s ^ 1];
+        s ^= 1;
+        g.y = m->mid;
+        if (!gemv<PRO_RESID_NORM, EPI_SWIGLU>(c, g)) return false;
+        GemvParams d{};
+        d.w = L.down;
+        d.rows = m->H;
+        d.cols = m->I;
+        d.x = m->mid;
+        d.y = m->branch;
+        if (!gemv<PRO_X, EPI_STORE>(c, d)) return false;
+    }
+    GemvParams h{};
+    h.w = m->head;
+    h.rows = m->V;
+    h.cols = m->H;
+    h.state_in = m->state[s];
+    h.branch = m->branch;
+    h.norm1 = m->layers[m->L - 1].mpost;
+    h.off1 = kPostMlpOffset;
+    h.norm2 = m->norm;
+    h.off2 = 1.0f;
+    h.state_out = m->state[s ^ 1];
+    m->final_state = m->state[s ^ 1];
+    h.norm_out = m->normalized;
+    h.y = m->logits;
+    h.arg_val = m->arg_val;
+    h.arg_idx = m->arg_idx;
+    h.arg_nan = m->arg_nan;
+    uint32_t grid = 0;
+    if (!gemv<PRO_RESID_NORM, EPI_ARGMAX>(c, h, &grid)) return false;
+    if (!launch(c, argmax_merge_kernel, dim3(1), dim3(256), 0, static_cast<const float *>(m->arg_val),
+                static_cast<const uint32_t *>(m->arg_idx), static_cast<const uint32_t *>(m->arg_nan), grid,
+                m->d_next, m->d_token))
+        return false;
+    return launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended, m->L, uint64_t{1});
+}
+
+bool ensure_graph(plamo_cuda *c, DModel *m) {
+    if (m->graph_exec) return true;
+    if (!note(c, "capture", cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal)))
+        return false;
+    const uint64_t before = c->info.launches;
+    const bool ok = record_decode(c, m);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+    if (!ok || !note(c, "capture end", e)) {
+        if (graph) cudaGraphDestroy(graph);
+        return false;
+    }
+    m->graph_nodes = c->info.launches - before;
+    c->info.launches = before;
+    m->graph = graph;
+    return note(c, "instantiate", cudaGraphInstantiate(&m->graph_exec, graph, 0));
+}
+
+bool launch_decode(plamo_cuda *c, DModel *m) {
+    if (!note(c, "graph launch", cudaGraphLaunch(m->graph_exec, c->stream))) return false;
+    c->info.graph_launches++;
+    c->info.launches += m->graph_nodes;
+    return true;
+}
+
+bool check_device_error(plamo_cuda *c, DModel *m) {
+    uint32_t err = 0;
+    if (!note(c, "error flag", cudaMemcpy(&err, m->d_error, 4, cudaMemcpyDeviceToHost))) return false;
+    if (err) {
+        cudaMemset(m->d_error, 0, 4);
+        c->info.errors++;
+        snprintf(c->info.note, sizeof c->info.note, "device rejected a token id");
+        return false;
+    }
+    return true;
+}
+
+// ---- layer-major prompt / verification ------------------------------------
+// mode 0: prefill (rows stored into the rings); 1: verification (rows kept
+// per layer in v_kv, nothing committed).
+bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all_logits) {
+    const uint64_t H = m->H;
+    AttnShape shape{T, m->QH, m->KH, m->D, m->QW};
+    const uint64_t G = m->QH / m->KH;
+    const size_t attn_smem = attention_smem_bytes(G, m->D);
+    if (!launch(c, embed_rows_kernel, dim3(T), dim3(256), 0, m->emb, static_cast<const uint32_t *>(m->p_ids),
+                m->V, H, m->p_states, m->d_error))
+        return false;
+    for (uint64_t l = 0; l < m->L; ++l) {
+        const DLayer &L = m->layers[l];
+        bool ok;
+        if (l == 0)
+            ok = launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(256), 0, m->p_states,
+                        static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, L.pre,
+                        1.0f, m->p_norm, H);
+        else
+            ok = launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(256), 0, m->p_states,
+                        static_cast<const float *>(m->p_branch), m->layers[l - 1].mpost, kPostMlpOffset, L.pre,
+                        1.0f, m->p_norm, H);
+        if (!ok || !gemm(c, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H)) return false;
+        AttnLayer al = attn_layer(m, l);
+        if (!launch(c, qk_prep_kernel, dim3(m->QH + m->KH, T), dim3(128), 0, m->p_qkv, m->p_q, al, shape))
+            return false;
+        const uint32_t splits = T >= 16 ? 1u : m->splits;
+        AttnParams ap{al, shape, m->p_q, m->p_qkv, m->p_attn, m->p_part, m->p_tickets, splits};
+        if (!launch(c, attention_kernel, dim3(m->KH, T, splits), dim3(kAttnThreads), attn_smem, ap))
+            return false;
+        if (mode == 0) {
+            const uint64_t first = T > L.ring ? T - L.ring : 0;
+            if (!launch(c, kv_store_kernel, dim3(T - first), dim3(256), 0, al, shape,
+                        static_cast<const float *>(m->p_qkv), first))
+                return false;
+        } else {
+            // K and V of every candidate, per layer: [T][2][KVW]
+            float *dst = m->v_kv + l * kVerifyMax * 2 * m->KVW;
+            if (!note(c, "verify kv", cudaMemcpy2DAsync(dst, 2 * m->KVW * 4, m->p_qkv + m->QH * m->D,
+                                                        m->QW * 4, 2 * m->KVW * 4, T, cudaMemcpyDeviceToDevice,
+                                                        c->stream)))
+                return false;
+        }
+        if (!gemm(c, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
+        if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(256), 0, m->p_states,
+                    static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H))
+            return false;
+        if (!gemm(c, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H)) return false;
+        if (!launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((m->I * T + 255) / 256, 4096)), dim3(256), 0,
+                    m->p_gu, m->I, T))
+            return false;
+        if (!gemm(c, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
+    }
+    if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(256), 0, m->p_states,
+                static_cast<const float *>(m->p_branch), m->layers[m->L - 1].mpost, kPostMlpOffset,
+                static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H))
+        return false;
+    if (need_all_logits) {
+        if (!launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(256), 0, m->p_states,
+                    static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, m->norm,
+                    1.0f, m->p_norm, H))
+            return false;
+        return gemm(c, m->p_norm, H, m->head, m->p_logits, m->V, T, m->V, H);
+    }
+    // Final norm and head for the last prompt token only (reference
+    // src/prefill.s:136-158), with the greedy choice on the device.
+    GemvParams h{};
+    h.w = m->head;
+    h.rows = m->V;
+    h.cols = H;
+    h.state_in = m->p_states + (T - 1) * H;
+    h.norm2 = m->norm;
+    h.off2 = 1.0f;
+    h.state_out = m->final_state;
+    h.norm_out = m->normalized;
+    h.y = m->logits;
+    h.arg_val = m->arg_val;
+    h.arg_idx = m->arg_idx;
+    h.arg_nan = m->arg_nan;
+    uint32_t grid = 0;
+    if (!gemv<PRO_NORM, EPI_ARGMAX>(c, h, &grid)) return false;
+    if (!launch(c, argmax_merge_kernel, dim3(1), dim3(256), 0, static_cast<const float *>(m->arg_val),
+                static_cast<const uint32_t *>(m->arg_idx), static_cast<const uint32_t *>(m->arg_nan), grid,
+                m->d_next, m->d_token))
+        return false;
+    return launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended, m->L, T);
+}
+
+bool copy_outputs(plamo_cuda *c, DModel *m) {
+    struct model *h = m->host;
+    return note(c, "state", cudaMemcpyAsync(h->state, m->final_state, m->H * 4, cudaMemcpyDeviceToHost, c->stream)) &&
+           note(c, "normalized", cudaMemcpyAsync(h->normalized, m->normalized, m->H * 4, cudaMemcpyDeviceToHost,
+                                                 c->stream)) &&
+           note(c, "logits", cudaMemcpyAsync(h->logits, m->logits, m->V * 4, cudaMemcpyDeviceToHost, c->stream));
+}
+
+bool sync_kv(plamo_cuda *c, DModel *m);
+
+double elapsed(plamo_cuda *c) {
+    float ms = 0;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    return ms * 1e-3;
+}
+
+}  // namespace
+
+// ============================================================================
+extern "C" {
+
+struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char *error, size_t cap) {
+    plamo_cuda_config cfg{};
+    if (config) cfg = *config;
+    if (!cfg.max_context) cfg.max_context = 8192 + 16;
+    if (!cfg.max_prefill) cfg.max_prefill = 4096;
+    if (!cfg.reserve) cfg.reserve = 1ull << 30;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count <= cfg.device || cfg.device < 0) {
+        if (error && cap) snprintf(error, cap, "CUDA requires an available device (%s)",
+                                   e == cudaSuccess ? "ordinal out of range" : cudaGetErrorString(e));
+        return nullptr;
+    }
+    cudaDeviceProp prop{};
+    if ((e = cudaSetDevice(cfg.device)) != cudaSuccess ||
+        (e = cudaGetDeviceProperties(&prop, cfg.device)) != cudaSuccess) {
+        if (error && cap) snprintf(error, cap, "cannot open CUDA device: %s", cudaGetErrorString(e));
+        return nullptr;
+    }
+    if (prop.major < 10) {
+        if (error && cap) snprintf(error, cap, "device %s is sm_%d%d; this build targets sm_100a", prop.name,
+                                   prop.major, prop.minor);
+        return nullptr;
+    }
+    auto *c = new plamo_cuda();
+    c->device = cfg.device;
+    c->config = cfg;
+    memset(&c->info, 0, sizeof c->info);
+    snprintf(c->info.device, sizeof c->info.device, "%.127s", prop.name);
+    c->sm_count = prop.multiProcessorCount;
+    c->info.sm_count = prop.multiProcessorCount;
+    const char *pdl = getenv("PLAMO_CUDA_PDL");
+    c->pdl = !pdl || strcmp(pdl, "0");
+    const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
+    c->gemv_ctas = ctas ? std::max(1, atoi(ctas)) : 1;
+    if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaEventCreate(&c->ev0)) != cudaSuccess || (e = cudaEventCreate(&c->ev1)) != cudaSuccess ||
+        (e = cudaMallocHost(&c->pinned_u32, 64 * 1024 * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&c->sink, 4)) != cudaSuccess) {
+        if (error && cap) snprintf(error, cap, "cannot create CUDA stream: %s", cudaGetErrorString(e));
+        delete c;
+        return nullptr;
+    }
+    c->pinned_capacity = 64 * 1024;
+    set_gemv_smem_limits<PRO_X, EPI_STORE>();
+    set_gemv_smem_limits<PRO_NORM, EPI_STORE>();
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_STORE>();
+    set_gemv_smem_limits<PRO_EMBED_NORM, EPI_STORE>();
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_SWIGLU>();
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>();
+    set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>();
+    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    return c;
+}
+
+void plamo_cuda_close(struct plamo_cuda *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (auto &kv : c->models) free_model(c, kv.second.get());
+    for (auto &r : c->ropes) cudaFree(r->dev);
+    for (Range &r : c->ranges) cudaFree(r.dev);
+    cudaFreeHost(c->pinned_u32);
+    cudaFree(c->sink);
+    cudaEventDestroy(c->ev0);
+    cudaEventDestroy(c->ev1);
+    cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+void plamo_cuda_maintain(struct plamo_cuda *c) {
+    if (c) cudaStreamSynchronize(c->stream);
+}
+
+void plamo_cuda_get_info(const struct plamo_cuda *c, struct plamo_cuda_info *info) {
+    if (!c || !info) return;
+    *info = c->info;
+}
+
+int plamo_cuda_preload(struct plamo_cuda *c, const void *src, uint64_t bytes) {
+    if (!c || !src || !bytes) return 0;
+    if (find_range(c, src, bytes)) return 1;
+    cudaSetDevice(c->device);
+    char *dev = nullptr;
+    if (!note(c, "preload alloc", cudaMalloc(&dev, bytes))) return 0;
+    if (!note(c, "preload copy", cudaMemcpy(dev, src, bytes, cudaMemcpyHostToDevice))) {
+        cudaFree(dev);
+        return 0;
+    }
+    c->ranges.push_back({reinterpret_cast<uintptr_t>(src), bytes, dev});
+    c->info.weight_bytes += bytes;
+    c->info.allocated_bytes += bytes;
+    return 1;
+}
+
+int plamo_cuda_preload_synthetic(struct plamo_cuda *c, const void *host_key, uint64_t count, uint64_t seed,
+                                 float mean, float std) {
+    if (!c || !host_key || !count) return 0;
+    cudaSetDevice(c->device);
+    char *dev = nullptr;
+    if (!note(c, "synthetic alloc", cudaMalloc(&dev, count * 2))) return 0;
+    if (!plamo_cuda_fill_synthetic_bf16(c, reinterpret_cast<uint16_t *>(dev), count, seed, mean, std)) {
+        cudaFree(dev);
+        return 0;
+    }
+    c->ranges.push_back({reinterpret_cast<uintptr_t>(host_key), count * 2, dev});
+    c->info.weight_bytes += count * 2;
+    c->info.allocated_bytes += count * 2;
+    return 1;
+}
+
+int plamo_cuda_fill_synthetic_bf16(struct plamo_cuda *c, uint16_t *dst, uint64_t count, uint64_t seed, float mean,
+                                   float std) {
+    if (!c) return 0;
+    fill_synthetic_bf16_kernel<<<c->sm_count * 8, 256, 0, c->stream>>>(dst, count, seed, mean, std);
+    c->info.launches++;
+    return note(c, "synthetic", cudaGetLastError()) && note(c, "synthetic", cudaStreamSynchronize(c->stream));
+}
+
+int plamo_cuda_fill_synthetic_f32(struct plamo_cuda *c, float *dst, uint64_t count, uint64_t seed, float mean,
+                                  float std) {
+    if (!c) return 0;
+    fill_synthetic_f32_kernel<<<c->sm_count * 8, 256, 0, c->stream>>>(dst, count, seed, mean, std);
+    c->info.launches++;
+    return note(c, "synthetic", cudaGetLastError()) && note(c, "synthetic", cudaStreamSynchronize(c->stream));
+}
+
+int plamo_cuda_warm_cache(struct plamo_cuda *c) {
+    if (!c) return 0;
+    for (const Range &r : c->ranges) {
+        touch_kernel<<<c->sm_count * 4, 256, 0, c->stream>>>(reinterpret_cast<const uint4 *>(r.dev), r.bytes / 16,
+                                                              c->sink);
+        c->info.launches++;
+    }
+    return note(c, "warm", cudaStreamSynchronize(c->stream));
+}
+
+int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
+    if (!c || !model || !model->count || !model->hidden || !model->vocab || !model->layers) return 0;
+    cudaSetDevice(c->device);
+    if (find_model(c, model)) return 1;
+    auto m = std::make_unique<DModel>();
+    m->host = model;
+    const struct qkv *q0 = model->layers[0]->mixer->qkv;
+    m->H = model->hidden;
+    m->QH = q0->qh;
+    m->KH = q0->kh;
+    m->D = q0->dim;
+    m->I = model->layers[0]->mlp->intermediate;
+    m->V = model->vocab;
+    m->L = model->count;
+    m->QW = (m->QH + 2 * m->KH) * m->D;
+    m->AW = m->QH * m->D;
+    m->KVW = m->KH * m->D;
+    if (!m->KH || m->QH % m->KH || !m->D || m->D % 2 || m->D > 512 || !m->I) {
+        snprintf(c->info.note, sizeof c->info.note, "unsupported attention shape");
+        return 0;
+    }
+    const uint64_t H = m->H;
+    m->emb = resolve(c, model->embedding, m->V * H * 2, true);
+    m->head = resolve(c, model->head, m->V * H * 2, true);
+    m->norm = resolve(c, model->norm, H * 2, true);
+    if (!m->emb || !m->head || !m->norm) return 0;
+    m->d_appended = static_cast<uint64_t *>(dalloc(c, m.get(), m->L * 8));
+    for (uint64_t l = 0; l < m->L; ++l) {
+        struct layer *hl = model->layers[l];
+        const struct qkv *q = hl->mixer->qkv;
+        const struct mlp *p = hl->mlp;
+        const struct cache *kc = hl->mixer->cache;
+        if (q->qh != m->QH || q->kh != m->KH || q->dim != m->D || q->hidden != H || p->intermediate != m->I ||
+            kc->width != m->KVW || !kc->capacity) {
+            snprintf(c->info.note, sizeof c->info.note, "layers differ in shape");
+            return 0;
+        }
+        DLayer L{};
+        L.host = hl;
+        L.qkv_w = resolve(c, q->weight, m->QW * H * 2, true);
+        L.qn = resolve(c, q->qn, m->D * 2, true);
+        L.kn = resolve(c, q->kn, m->D * 2, true);
+        L.o_w = resolve(c, hl->mixer->weight, H * m->AW * 2, true);
+        L.pre = resolve(c, hl->pre, H * 2, true);
+        L.post = resolve(c, hl->post, H * 2, true);
+        L.mpre = resolve(c, p->pre, H * 2, true);
+        L.mpost = resolve(c, p->post, H * 2, true);
+        L.gu = resolve(c, p->gu, 2 * m->I * H * 2, true);
+        L.down = resolve(c, p->down, H * m->I * 2, true);
+        if (!L.qkv_w || !L.qn || !L.kn || !L.o_w || !L.pre || !L.post || !L.mpre || !L.mpost || !L.gu || !L.down)
+            return 0;
+        L.capacity = kc->capacity;
+        L.sliding = kc->sliding != 0;
+        // A sliding ring keeps spare slots so that one speculative row can be
+        // written without evicting a row still inside the window.
+        L.ring = L.sliding ? kc->capacity + kVerifyMax + 1
+                           : std::min<uint64_t>(kc->capacity, c->config.max_context);
+        L.scale = model->scales[l];
+        const uint64_t positions = L.sliding ? kc->capacity : std::min<uint64_t>(kc->capacity, c->config.max_context);
+        L.rope = get_rope(c, hl->mixer->rotation->freq, m->D, L.scale, positions);
+        if (!L.rope) return 0;
+        L.ring_k = static_cast<float *>(dalloc(c, m.get(), L.ring * m->KVW * 4));
+        L.ring_v = static_cast<float *>(dalloc(c, m.get(), L.ring * m->KVW * 4));
+        if (!L.ring_k || !L.ring_v) return 0;
+        c->info.kv_bytes += 2 * L.ring * m->KVW * 4;
+        L.appended = 0;
+        m->layers.push_back(L);
+    }
+    // Decode buffers.
+    const uint64_t G = m->QH / m->KH;
+    (void)G;
+    m->splits = 16;
+    const uint64_t before = c->info.allocated_bytes;
+    m->state[0] = static_cast<float *>(dalloc(c, m.get(), H * 4));
+    m->state[1] = static_cast<float *>(dalloc(c, m.get(), H * 4));
+    m->final_state = m->state[0];
+    m->normalized = static_cast<float *>(dalloc(c, m.get(), H * 4));
+    m->logits = static_cast<float *>(dalloc(c, m.get(), m->V * 4));
+    m->qkv = static_cast<float *>(dalloc(c, m.get(), m->QW * 4));
+    m->q = static_cast<float *>(dalloc(c, m.get(), m->AW * 4));
+    m->attn = static_cast<float *>(dalloc(c, m.get(), m->AW * 4));
+    m->branch = static_cast<float *>(dalloc(c, m.get(), H * 4));
+    m->mid = static_cast<float *>(dalloc(c, m.get(), m->I * 4));
+    m->part = static_cast<float *>(dalloc(c, m.get(), m->QH * m->splits * (m->D + 2) * 4));
+    m->tickets = static_cast<uint32_t *>(dalloc(c, m.get(), m->KH * 4));
+    const uint64_t grid_max = static_cast<uint64_t>(c->sm_count) * 64;
+    m->arg_val = static_cast<float *>(dalloc(c, m.get(), grid_max * 4));
+    m->arg_idx = static_cast<uint32_t *>(dalloc(c, m.get(), grid_max * 4));
+    m->arg_nan = static_cast<uint32_t *>(dalloc(c, m.get(), grid_max * 4));
+    m->d_token = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
+    m->d_next = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
+    m->d_error = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
+    // Prompt buffers.
+    m->tmax = std::max<uint64_t>(c->config.max_prefill, kVerifyMax);
+    const uint64_t T = m->tmax;
+    m->p_states = static_cast<float *>(dalloc(c, m.get(), T * H * 4));
+    m->p_norm = static_cast<float *>(dalloc(c, m.get(), T * H * 4));
+    m->p_qkv = static_cast<float *>(dalloc(c, m.get(), T * m->QW * 4));
+    m->p_q = static_cast<float *>(dalloc(c, m.get(), T * m->AW * 4));
+    m->p_attn = static_cast<float *>(dalloc(c, m.get(), T * m->AW * 4));
+    m->p_branch = static_cast<float *>(dalloc(c, m.get(), T * H * 4));
+    m->p_gu = static_cast<float *>(dalloc(c, m.get(), T * 2 * m->I * 4));
+    m->p_logits = static_cast<float *>(dalloc(c, m.get(), kVerifyMax * m->V * 4));
+    m->p_part = static_cast<float *>(dalloc(c, m.get(), kVerifyMax * m->QH * m->splits * (m->D + 2) * 4));
+    m->p_tickets = static_cast<uint32_t *>(dalloc(c, m.get(), T * m->KH * 4));
+    m->p_ids = static_cast<uint32_t *>(dalloc(c, m.get(), T * 4));
+    m->p_next = static_cast<uint32_t *>(dalloc(c, m.get(), kVerifyMax * 4));
+    m->v_kv = static_cast<float *>(dalloc(c, m.get(), m->L * kVerifyMax * 2 * m->KVW * 4));
+    for (void *p : m->allocations)
+        if (!p) return 0;
+    c->info.workspace_bytes += c->info.allocated_bytes - before;
+    // Start from the host's counts (zero for a fresh request).
+    if (!reconcile(c, m.get())) {
+        free_model(c, m.get());
+        return 0;
+    }
+    if (!note(c, "prepare", cudaStreamSynchronize(c->stream))) return 0;
+    c->models[model] = std::move(m);
+    return 1;
+}
+
+int plamo_cuda_forward(struct plamo_cuda *c, struct model *model, uint64_t token) {
+    uint32_t next;
+    if (!c) return 0;
+    DModel *m = find_model(c, model);
+    if (!m || token >= model->vocab) {
+        if (c) c->info.declines++;
+        return 0;
+    }
+    const int r = plamo_cuda_forward_greedy(c, model, token, &next);
+    if (r != 1) return r;
+    if (!copy_outputs(c, m) || !note(c, "forward", cudaStreamSynchronize(c->stream))) return -1;
+    if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
+    return 1;
+}
+
+int plamo_cuda_forward_greedy(struct plamo_cuda *c, struct model *model, uint64_t token, uint32_t *next) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || token >= model->vocab) {
+        c->info.declines++;
+        return 0;
+    }
+    if (!reconcile(c, m)) return -1;
+    if (!fits(m, 1)) {
+        c->info.declines++;
+        return 0;
+    }
+    if (!ensure_graph(c, m)) return -1;
+    m->verify_valid = false;
+    c->pinned_u32[0] = static_cast<uint32_t>(token);
+    if (!note(c, "token", cudaMemcpyAsync(m->d_token, c->pinned_u32, 4, cudaMemcpyHostToDevice, c->stream)))
+        return -1;
+    cudaEventRecord(c->ev0, c->stream);
+    if (!launch_decode(c, m)) return -1;
+    cudaEventRecord(c->ev1, c->stream);
+    if (!note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 1, m->d_next, 4, cudaMemcpyDeviceToHost, c->stream)) ||
+        !note(c, "forward", cudaStreamSynchronize(c->stream)))
+        return -1;
+    if (!check_device_error(c, m)) return -1;
+    c->info.gpu_seconds += elapsed(c);
+    c->info.forwards++;
+    publish_counts(m, 1);
+    if (next) *next = c->pinned_u32[1];
+    return 1;
+}
+
+static int prompt(struct plamo_cuda *c, struct model *model, const uint32_t *ids, uint64_t tokens, float *states,
+                  uint32_t *next) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || !tokens || !ids) {
+        c->info.declines++;
+        return 0;
+    }
+    for (uint64_t i = 0; i < tokens; ++i)
+        if (ids[i] >= model->vocab) {
+            snprintf(c->info.note, sizeof c->info.note, "prompt token %u outside the vocabulary", ids[i]);
+            c->info.errors++;
+            return -1;
+        }
+    if (tokens > m->tmax) {
+        c->info.declines++;
+        return 0;
+    }
+    if (!reconcile(c, m)) return -1;
+    if (!fits(m, tokens)) {
+        c->info.declines++;
+        return 0;
+    }
+    m->verify_valid = false;
+    if (!note(c, "ids", cudaMemcpyAsync(m->p_ids, ids, tokens * 4, cudaMemcpyHostToDevice, c->stream))) return -1;
+    cudaEventRecord(c->ev0, c->stream);
+    if (!record_prompt(c, m, tokens, 0, false)) return -1;
+    cudaEventRecord(c->ev1, c->stream);
+    if (states && !note(c, "states", cudaMemcpyAsync(states, m->p_states, tokens * m->H * 4, cudaMemcpyDeviceToHost,
+                                                     c->stream)))
+        return -1;
+    if (!copy_outputs(c, m) ||
+        !note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 2, m->d_next, 4, cudaMemcpyDeviceToHost, c->stream)) ||
+        !note(c, "prefill", cudaStreamSynchronize(c->stream)))
+        return -1;
+    if (!check_device_error(c, m)) return -1;
+    c->info.gpu_seconds += elapsed(c);
+    c->info.prefills++;
+    publish_counts(m, tokens);
+    if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
+    if (next) *next = c->pinned_u32[2];
+    return 1;
+}
+
+int plamo_cuda_prefill(struct plamo_cuda *c, struct model *model, const uint32_t *ids, uint64_t tokens,
+                       float *states) {
+    return prompt(c, model, ids, tokens, states, nullptr);
+}
+
+int plamo_cuda_prefill_greedy(struct plamo_cuda *c, struct model *model, const uint32_t *ids, uint64_t tokens,
+                              uint32_t *next) {
+    return prompt(c, model, ids, tokens, nullptr, next);
+}
+
+int plamo_cuda_verify(struct plamo_cuda *c, struct model *model, const uint32_t *ids, uint64_t tokens,
+                      uint32_t *next) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || !tokens || tokens > kVerifyMax || !ids || !next) {
+        c->info.declines++;
+        return 0;
+    }
+    for (uint64_t i = 0; i < tokens; ++i)
+        if (ids[i] >= model->vocab) {
+            c->info.declines++;
+            return 0;
+        }
+    if (!reconcile(c, m)) return -1;
+    if (!fits(m, tokens)) {
+        c->info.declines++;
+        return 0;
+    }
+    if (!note(c, "ids", cudaMemcpyAsync(m->p_ids, ids, tokens * 4, cudaMemcpyHostToDevice, c->stream))) return -1;
+    cudaEventRecord(c->ev0, c->stream);
+    if (!record_prompt(c, m, tokens, 1, true)) return -1;
+    if (!launch(c, rows_argmax_kernel, dim3(tokens), dim3(256), 0, static_cast<const float *>(m->p_logits), m->V,
+                m->p_next))
+        return -1;
+    cudaEventRecord(c->ev1, c->stream);
+    if (!note(c, "verify next", cudaMemcpyAsync(c->pinned_u32 + 16, m->p_next, tokens * 4, cudaMemcpyDeviceToHost,
+                                                c->stream)) ||
+        !note(c, "verify", cudaStreamSynchronize(c->stream)))
+        return -1;
+    if (!check_device_error(c, m)) return -1;
+    memcpy(next, c->pinned_u32 + 16, tokens * 4);
+    c->info.gpu_seconds += elapsed(c);
+    c->info.verification_batches++;
+    c->info.verified_tokens += tokens;
+    m->verify_count = tokens;
+    m->verify_committed = 0;
+    m->verify_valid = true;
+    return 1;
+}
+
+int plamo_cuda_commit(struct plamo_cuda *c, struct model *model, uint64_t index) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || !m->verify_valid || index != m->verify_committed || index >= m->verify_count) {
+        if (c) c->info.declines++;
+        return 0;
+    }
+    if (!fits(m, 1)) return 0;
+    for (uint64_t l = 0; l < m->L; ++l) {
+        AttnLayer al = attn_layer(m, l);
+        const float *row = m->v_kv + (l * kVerifyMax + index) * 2 * m->KVW;
+        kv_commit_kernel<<<1, 256, 0, c->stream>>>(al, m->KVW, row, row + m->KVW);
+        c->info.launches++;
+    }
+    advance_kernel<<<1, 32, 0, c->stream>>>(m->d_appended, m->L, 1);
+    c->info.launches++;
+    struct model *h = model;
+    // State of candidate `index`: final-layer state row; normalized and
+    // logits of the same row.
+    if (!note(c, "commit", cudaGetLastError()) ||
+        !note(c, "commit state", cudaMemcpyAsync(h->state, m->p_states + index * m->H, m->H * 4,
+                                                 cudaMemcpyDeviceToHost, c->stream)) ||
+        !note(c, "commit norm", cudaMemcpyAsync(h->normalized, m->p_norm + index * m->H, m->H * 4,
+                                                cudaMemcpyDeviceToHost, c->stream)) ||
+        !note(c, "commit logits", cudaMemcpyAsync(h->logits, m->p_logits + index * m->V, m->V * 4,
+                                                  cudaMemcpyDeviceToHost, c->stream)) ||
+        !note(c, "commit", cudaStreamSynchronize(c->stream)))
+        return -1;
+    publish_counts(m, 1);
+    m->verify_committed++;
+    c->info.committed_tokens++;
+    if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
+    return 1;
+}
+
+int plamo_cuda_sync_host(struct plamo_cuda *c, struct model *model) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m) return 0;
+    if (!sync_kv(c, m)) return -1;
+    return 1;
+}
+
+int plamo_cuda_read_weights(struct plamo_cuda *c, const void *key, void *dst, uint64_t bytes) {
+    if (!c || !key || !dst) return 0;
+    const Range *r = find_range(c, key, bytes);
+    if (!r) return 0;
+    const char *src = r->dev + (reinterpret_cast<uintptr_t>(key) - r->host);
+    return note(c, "read weights", cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost)) ? 1 : 0;
+}
+
+int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, float *state) {
+    if (!c || !state) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || index >= m->L) {
+        c->info.declines++;
+        return 0;
+    }
+    if (!reconcile(c, m)) return -1;
+    DLayer &L = m->layers[index];
+    if (!L.sliding && (L.appended + 1 > L.capacity || L.appended + 1 > L.ring)) {
+        c->info.declines++;
+        return 0;
+    }
+    m->verify_valid = false;
+    AttnShape shape{1, m->QH, m->KH, m->D, m->QW};
+    const size_t attn_smem = attention_smem_bytes(m->QH / m->KH, m->D);
+    AttnLayer al = attn_layer(m, index);
+    bool ok = note(c, "layer state", cudaMemcpyAsync(m->state[0], state, m->H * 4, cudaMemcpyHostToDevice,
+                                                     c->stream));
+    cudaEventRecord(c->ev0, c->stream);
+    GemvParams p{};
+    p.w = L.qkv_w;
+    p.rows = m->QW;
+    p.cols = m->H;
+    p.state_in = m->state[0];
+    p.norm2 = L.pre;
+    p.off2 = 1.0f;
+    p.y = m->qkv;
+    ok = ok && gemv<PRO_NORM, EPI_STORE>(c, p);
+    ok = ok && launch(c, qk_prep_kernel, dim3(m->QH + m->KH, 1), dim3(128), 0, m->qkv, m->q, al, shape);
+    AttnParams ap{al, shape, m->q, m->qkv, m->attn, m->part, m->tickets, m->splits};
+    ok = ok && launch(c, attention_kernel, dim3(m->KH, 1, m->splits), dim3(kAttnThreads), attn_smem, ap);
+    ok = ok && launch(c, kv_store_kernel, dim3(1), dim3(256), 0, al, shape, static_cast<const float *>(m->qkv),
+                      uint64_t{0});
+    GemvParams o{};
+    o.w = L.o_w;
+    o.rows = m->H;
+    o.cols = m->AW;
+    o.x = m->attn;
+    o.y = m->branch;
+    ok = ok && gemv<PRO_X, EPI_STORE>(c, o);
+    GemvParams g{};
+    g.w = L.gu;
+    g.rows = 2 * m->I;
+    g.cols = m->H;
+    g.state_in = m->state[0];
+    g.branch = m->branch;
+    g.norm1 = L.post;
+    g.off1 = kPostMixerOffset;
+    g.norm2 = L.mpre;
+    g.off2 = 1.0f;
+    g.state_out = m->state[1];
+    g.y = m->mid;
+    ok = ok && gemv<PRO_RESID_NORM, EPI_SWIGLU>(c, g);
+    GemvParams d{};
+    d.w = L.down;
+    d.rows = m->H;
+    d.cols = m->I;
+    d.x = m->mid;
+    d.y = m->branch;
+    ok = ok && gemv<PRO_X, EPI_STORE>(c, d);
+    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(1), dim3(256), 0, m->state[1],
+                      static_cast<const float *>(m->branch), L.mpost, kPostMlpOffset,
+                      static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), m->H);
+    ok = ok && launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended + index, uint64_t{1}, uint64_t{1});
+    cudaEventRecord(c->ev1, c->stream);
+    ok = ok && note(c, "layer out", cudaMemcpyAsync(state, m->state[1], m->H * 4, cudaMemcpyDeviceToHost,
+                                                    c->stream)) &&
+         note(c, "layer", cudaStreamSynchronize(c->stream));
+    if (!ok) return -1;
+    c->info.gpu_seconds += elapsed(c);
+    L.appended += 1;
+    struct cache *hc = L.host->mixer->cache;
+    hc->count = layer_count(L);
+    L.host->mixer->rotation->processed_count = hc->count;
+    L.host->mixer->rotation->scale_bits = float_to_bits(L.scale);
+    if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
+    return 1;
+}
+
+int plamo_cuda_invalidate(struct plamo_cuda *c, struct model *model) {
+    if (!c) return 0;
+    DModel *m = find_model(c, model);
+    if (!m) return 0;
+    for (DLayer &L : m->layers) L.stale = true;
+    return 1;
+}
+
+void plamo_cuda_reset_request(struct plamo_cuda *c, struct model *model) {
+    for (uint64_t i = 0; i < model->count; ++i) {
+        struct layer *l = model->layers[i];
+        l->state = model->state;
+        l->mixer->cache->count = 0;
+        l->mixer->rotation->processed_count = 0;
+        l->mixer->rotation->scale_bits = 0;
+        l->mixer->gqa->tokens = 0;
+    }
+    if (c) {
+        DModel *m = find_model(c, model);
+        if (m) reconcile(c, m);
+    }
+}
+
+int plamo_cuda_linear(struct plamo_cuda *c, const struct plamo_matmul *mm) {
+    if (!c || !mm) return 0;
+    if (!mm->rows || !mm->tokens) return 1;
+    cudaSetDevice(c->device);
+    const uint16_t *w = resolve(c, mm->weights, mm->rows * mm->columns * 2, false);
+    if (!w) {
+        c->info.declines++;
+        return 0;
+    }
+    float *x = nullptr, *y = nullptr;
+    const uint64_t T = mm->tokens, K = mm->columns, R = mm->rows;
+    if (!note(c, "linear alloc", cudaMalloc(&x, std::max<uint64_t>(T * K, 1) * 4)) ||
+        !note(c, "linear alloc", cudaMalloc(&y, T * R * 4))) {
+        cudaFree(x);
+        return -1;
+    }
+    bool ok = !K || note(c, "linear in", cudaMemcpy2DAsync(x, K * 4, mm->input, mm->input_stride * 4, K * 4, T,
+                                                          cudaMemcpyHostToDevice, c->stream));
+    if (ok && !K) ok = note(c, "linear zero", cudaMemsetAsync(y, 0, T * R * 4, c->stream));
+    else if (ok) ok = gemm(c, x, K, w, y, R, T, R, K);
+    ok = ok && note(c, "linear out", cudaMemcpy2DAsync(mm->output, mm->output_stride * 4, y, R * 4, R * 4, T,
+                                                       cudaMemcpyDeviceToHost, c->stream)) &&
+         note(c, "linear", cudaStreamSynchronize(c->stream));
+    cudaFree(x);
+    cudaFree(y);
+    return ok ? 1 : -1;
+}
+
+int plamo_cuda_mlp(struct plamo_cuda *c, const struct mlp *p, float *states, uint64_t tokens) {
+    if (!c || !p || !states) return 0;
+    if (!tokens) return 1;
+    cudaSetDevice(c->device);
+    const uint64_t H = p->hidden, I = p->intermediate;
+    const uint16_t *pre = resolve(c, p->pre, H * 2, false), *post = resolve(c, p->post, H * 2, false);
+    const uint16_t *gu = resolve(c, p->gu, 2 * I * H * 2, false), *down = resolve(c, p->down, H * I * 2, false);
+    if (!pre || !post || !gu || !down) {
+        c->info.declines++;
+        return 0;
+    }
+    float *s = nullptr, *n = nullptr, *g = nullptr, *b = nullptr;
+    bool ok = note(c, "mlp alloc", cudaMalloc(&s, tokens * H * 4)) && note(c, "mlp alloc", cudaMalloc(&n, tokens * H * 4)) &&
+              note(c, "mlp alloc", cudaMalloc(&g, tokens * 2 * I * 4)) &&
+              note(c, "mlp alloc", cudaMalloc(&b, tokens * H * 4));
+    ok = ok && note(c, "mlp in", cudaMemcpyAsync(s, states, tokens * H * 4, cudaMemcpyHostToDevice, c->stream));
+    ok = ok && launch(c, norm_rows_kernel<ROW_NORM>, dim3(tokens), dim3(256), 0, s, static_cast<const float *>(nullptr),
+                      static_cast<const uint16_t *>(nullptr), 0.0f, pre, 1.0f, n, H);
+    ok = ok && gemm(c, n, H, gu, g, 2 * I, tokens, 2 * I, H);
+    ok = ok && launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((I * tokens + 255) / 256, 4096)), dim3(256), 0,
+                      g, I, tokens);
+    ok = ok && gemm(c, g, 2 * I, down, b, H, tokens, H, I);
+    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(tokens), dim3(256), 0, s, static_cast<const float *>(b),
+                      post, kPostMlpOffset, static_cast<const uint16_t *>(nullptr), 0.0f,
+                      static_cast<float *>(nullptr), H);
+    ok = ok && note(c, "mlp out", cudaMemcpyAsync(states, s, tokens * H * 4, cudaMemcpyDeviceToHost, c->stream)) &&
+         note(c, "mlp", cudaStreamSynchronize(c->stream));
+    cudaFree(s);
+    cudaFree(n);
+    cudaFree(g);
+    cudaFree(b);
+    return ok ? 1 : -1;
+}
+
+int64_t plamo_cuda_generate(struct plamo_cuda *c, struct model *model, const uint32_t *ids, uint64_t tokens,
+                            uint64_t max_tokens, uint32_t *out, int (*on_token)(uint32_t, void *), void *context,
+                            struct plamo_cuda_timing *timing) {
+    plamo_cuda_timing local{};
+    plamo_cuda_timing *t = timing ? timing : &local;
+    memset(t, 0, sizeof *t);
+    if (!c || !model || !out || !max_tokens || max_tokens > 4096 || !tokens || tokens > 4096) return -1;
+    DModel *m = find_model(c, model);
+    if (!m) return -1;
+    t->prompt_tokens = tokens;
+    auto now = [] {
+        return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+    };
+    const double start = now();
+    uint32_t id = 0;
+    if (plamo_cuda_prefill_greedy(c, model, ids, tokens, &id) != 1) return -1;
+    t->prefill_seconds = now() - start;
+    t->finish_reason = "length";
+    const double decode_start = now();
+    int64_t emitted = 0;
+    for (;;) {
+        // Emit the selected token (reference runtime/engine.c:395-420).
+        if (id == 1 || id == 16) {
+            t->finish_reason = "stop";
+            break;
+        }
+        if (id >= model->vocab) {
+            t->finish_reason = "error";
+            return -1;
+        }
+        out[emitted++] = id;
+        if (emitted == 1) t->first_token_seconds = now() - start;
+        if (on_token && !on_token(id, context)) {
+            t->finish_reason = "cancelled";
+            break;
+        }
+        if (static_cast<uint64_t>(emitted) == max_tokens) break;
+        uint32_t next = 0;
+        if (plamo_cuda_forward_greedy(c, model, id, &next) != 1) return -1;
+        t->decode_steps++;
+        id = next;
+    }
+    t->decode_seconds = now() - decode_start;
+    t->completion_tokens = static_cast<uint64_t>(emitted);
+    return emitted;
+}
+
+int plamo_cuda_gemv_device(struct plamo_cuda *c, const uint16_t *w, const float *x, float *y, uint64_t rows,
+                           uint64_t cols) {
+    if (!c) return 0;
+    GemvParams p{};
+    p.w = w;
+    p.rows = rows;
+    p.cols = cols;
+    p.x = x;
+    p.y = y;
+    return gemv<PRO_X, EPI_STORE>(c, p) ? 1 : -1;
+}
+
+double plamo_cuda_time_gemv(struct plamo_cuda *c, const uint16_t *w, const float *x, float *y, uint64_t rows,
+                            uint64_t cols, uint64_t repeats) {
+    if (!c || !repeats) return -1;
+    cudaStreamSynchronize(c->stream);
+    cudaEventRecord(c->ev0, c->stream);
+    for (uint64_t i = 0; i < repeats; ++i)
+        if (plamo_cuda_gemv_device(c, w, x, y, rows, cols) != 1) return -1;
+    cudaEventRecord(c->ev1, c->stream);
+    if (!note(c, "time gemv", cudaStreamSynchronize(c->stream))) return -1;
+    float ms = 0;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    return ms;
+}
+
+double plamo_cuda_time_decode(struct plamo_cuda *c, struct model *model, uint64_t repeats) {
+    if (!c || !repeats) return -1;
+    DModel *m = find_model(c, model);
+    if (!m || !reconcile(c, m) || !fits(m, repeats) || !ensure_graph(c, m)) return -1;
+    m->verify_valid = false;
+    cudaStreamSynchronize(c->stream);
+    cudaEventRecord(c->ev0, c->stream);
+    for (uint64_t i = 0; i < repeats; ++i)
+        if (!launch_decode(c, m)) return -1;
+    cudaEventRecord(c->ev1, c->stream);
+    if (!note(c, "time decode", cudaStreamSynchronize(c->stream))) return -1;
+    if (!check_device_error(c, m)) return -1;
+    publish_counts(m, repeats);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    return ms;
+}
+
+uint64_t plamo_cuda_kernel_launches(const struct plamo_cuda *c) {
+    return c ? c->info.launches : 0;
+}
+
+void *plamo_cuda_device_alloc(struct plamo_cuda *c, uint64_t bytes) {
+    if (!c) return nullptr;
+    void *p = nullptr;
+    cudaSetDevice(c->device);
+    if (!note(c, "alloc", cudaMalloc(&p, bytes ? bytes : 16))) return nullptr;
+    return p;
+}
+
+void plamo_cuda_device_free(struct plamo_cuda *c, void *p) {
+    if (c && p) cudaFree(p);
+}
+
+int plamo_cuda_copy_to_device(struct plamo_cuda *c, void *dst, const void *src, uint64_t bytes) {
+    return c && note(c, "copy", cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice)) ? 1 : 0;
+}
+
+int plamo_cuda_copy_to_host(struct plamo_cuda *c, void *dst, const void *src, uint64_t bytes) {
+    return c && note(c, "copy", cudaStreamSynchronize(c->stream)) &&
+                   note(c, "copy", cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost))
+               ? 1
+               : 0;
+}
+
+int plamo_cuda_synchronize(struct plamo_cuda *c) {
+    return c && note(c, "synchronize", cudaStreamSynchronize(c->stream)) ? 1 : 0;
+}
+
+}  // extern "C"
+
+namespace {
+bool sync_kv(plamo_cuda *c, DModel *m) {
+    for (uint64_t l = 0; l < m->L; ++l) {
+        DLayer &L = m->layers[l];
+        const uint64_t count = layer_count(L);
+        struct cache *hc = L.host->mixer->cache;
+        struct rotation *r = L.host->mixer->rotation;
+        if (count) {
+            float *k = nullptr, *v = nullptr, *rot = nullptr;
+            const uint64_t bytes = count * m->KVW * 4;
+            if (!note(c, "sync alloc", cudaMalloc(&k, bytes)) || !note(c, "sync alloc", cudaMalloc(&v, bytes)) ||
+                !note(c, "sync alloc", cudaMalloc(&rot, bytes))) {
+                cudaFree(k);
+                cudaFree(v);
+                return false;
+            }
+            AttnLayer al = attn_layer(m, l);
+            kv_gather_kernel<<<count, 256, 0, c->stream>>>(al, m->KVW, m->KH, m->D, count, k, v, rot);
+            c->info.launches++;
+            bool ok = note(c, "gather", cudaGetLastError()) &&
+                      note(c, "sync k", cudaMemcpyAsync(hc->k, k, bytes, cudaMemcpyDeviceToHost, c->stream)) &&
+                      note(c, "sync v", cudaMemcpyAsync(hc->v, v, bytes, cudaMemcpyDeviceToHost, c->stream)) &&
+                      note(c, "sync rot", cudaMemcpyAsync(r->out, rot, bytes, cudaMemcpyDeviceToHost, c->stream)) &&
+                      note(c, "sync", cudaStreamSynchronize(c->stream));
+            cudaFree(k);
+            cudaFree(v);
+            cudaFree(rot);
+            if (!ok) return false;
+            // cos/sin scratch at the newest local position, as the CPU leaves it.
+            const uint64_t half = m->D / 2;
+            std::vector<float> row(m->D);
+            build_rope_rows(L.rope->freq.data(), m->D, L.scale, count - 1, count, row.data());
+            memcpy(r->cos, row.data(), half * 4);
+            memcpy(r->sin, row.data() + half, half * 4);
+        }
+        hc->count = count;
+        r->processed_count = count;
+        r->scale_bits = float_to_bits(L.scale);
+        L.host_hash = newest_row_hash(m, L);
+    }
+    return true;
+}
+}  // namespace

@@ -1,0 +1,112 @@
+// Shared device helpers of the PLaMo-3 sm_100a kernels.
+//
+// The library is compiled with --fmad=false: a multiply followed by an add is
+// two rounded operations unless the source writes fmaf(). That keeps every
+// elementwise formula in the same rounding order as the reference
+// (RMSNorm (x*inv)*(w+offset), split-half RoPE with separate products, SwiGLU
+// g/(exp(-g)+1)*u), while the long reductions (dot products, sums of squares,
+// softmax sums) use parallel trees whose results stay within the reference's
+// own GPU acceptance bound (relative L2 <= 1e-4).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace plamo {
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t bits) {
+    return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+}
+// Low/high BF16 of a packed 32-bit word -> FP32 (exact).
+__device__ __forceinline__ float bf16_lo(uint32_t word) { return __uint_as_float(word << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t word) { return __uint_as_float(word & 0xFFFF0000u); }
+
+// exp as the reference computes it (reference src/activation.s:6-46):
+// saturate below -87 to 0 and above 88 to +inf, n = rint(x*log2e),
+// r = fma(-n, ln2, x), degree-7 Taylor polynomial in FMA Horner form, times 2^n.
+// Bit-identical to the C oracle's plamo_exp.
+__device__ __forceinline__ float plamo_exp(float x) {
+    if (!(x >= -87.0f)) return 0.0f;
+    if (x > 88.0f) return __int_as_float(0x7f800000);
+    float n = rintf(__fmul_rn(x, 1.4426950408889634f));
+    int e = static_cast<int>(n);
+    float r = fmaf(-n, 0.6931471805599453f, x);
+    float p = 0.0001984126984126984f;
+    p = fmaf(p, r, 0.001388888888888889f);
+    p = fmaf(p, r, 0.008333333333333333f);
+    p = fmaf(p, r, 0.041666666666666664f);
+    p = fmaf(p, r, 0.16666666666666666f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    return __fmul_rn(p, __int_as_float((e + 127) << 23));
+}
+
+// SiLU(g) * u with the reference's operation order (src/activation.s:182-226).
+__device__ __forceinline__ float swiglu(float g, float u) {
+    float d = __fadd_rn(plamo_exp(-g), 1.0f);
+    return __fmul_rn(__fdiv_rn(g, d), u);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Deterministic block sum (same order for every block of the same shape).
+// `scratch` holds at least blockDim.x/32 floats. All threads get the result.
+__device__ __forceinline__ float block_sum(float v, float *scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = (blockDim.x + 31) >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float total = 0.0f;
+    for (int i = 0; i < warps; ++i) total += scratch[i];
+    return total;
+}
+
+// RMSNorm inverse 1/sqrt(sum/n + 1e-6) from a sum of squares (reference
+// src/math.s:349-366: divide, add eps, sqrt, reciprocal, each rounded).
+__device__ __forceinline__ float rms_inverse(float sum_squares, uint64_t n) {
+    float mean = __fdiv_rn(sum_squares, static_cast<float>(n));
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
+}
+// (x * inverse) * (w + offset)
+__device__ __forceinline__ float rms_apply(float x, float inverse, uint16_t w, float offset) {
+    return __fmul_rn(__fmul_rn(x, inverse), __fadd_rn(bf16_to_f32(w), offset));
+}
+
+// Streaming 128-bit load of weights that are read once per token: bypass L1
+// and mark the L2 line evict-first so activations and KV stay resident.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+__device__ __forceinline__ uint4 load_stream(const void *p, uint64_t policy) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p), "l"(policy));
+    return v;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// weight prefetch while this one finishes; wait for the previous kernel's
+// results before reading them.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+}  // namespace plamo

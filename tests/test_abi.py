@@ -1,0 +1,53 @@
+"""The C-ABI library loads and exports every entry point include/plamo_cuda.h declares."""
+import ctypes
+import os
+import re
+import subprocess
+
+from conftest import ROOT, load_package
+
+
+def declared_entry_points():
+    text = open(os.path.join(ROOT, "include", "plamo_cuda.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(plamo_cuda_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    pkg = load_package()
+    lib = pkg.load()
+    names = declared_entry_points()
+    assert len(names) >= 30
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(plamo_cuda_\w+)", out))
+    missing = [n for n in names if n not in exported]
+    assert not missing, missing
+    for n in names:
+        getattr(lib, n)
+    # ctypes bindings cover exactly the declared ABI
+    assert sorted(pkg._abi.SIGNATURES) == names
+
+
+def test_record_layouts_match_reference_abi():
+    pkg = load_package()
+    a = pkg._abi
+    sizes = {a.Qkv: 72, a.Cache: 48, a.Rotation: 72, a.Gqa: 72, a.Mixer: 56, a.Mlp: 80,
+             a.Layer: 64, a.Model: 88, a.Matmul: 64}
+    for s, n in sizes.items():
+        assert ctypes.sizeof(s) == n
+    assert a.Layer.mixer.offset == 40
+    assert a.Cache.count.offset == 24
+    assert a.Rotation.processed_count.offset == 56
+
+
+def test_open_reports_missing_device_without_gpu():
+    pkg = load_package()
+    lib = pkg.load()
+    cfg = pkg._abi.CudaConfig(device=0)
+    err = ctypes.create_string_buffer(256)
+    ctx = lib.plamo_cuda_open(ctypes.byref(cfg), err, 256)
+    if ctx:  # a GPU is present: nothing to check here
+        lib.plamo_cuda_close(ctx)
+        return
+    assert err.value, "open must explain a failure"
