@@ -91,6 +91,12 @@ int plamo_cuda_mlp(struct plamo_cuda *, const struct mlp *, float *states, uint6
    reference's rotation cache holds them), state, normalized and logits of
    `model` into its host arrays, and set the host counters. */
 int plamo_cuda_sync_host(struct plamo_cuda *, struct model *);
+/* Free the device state prepared for `model` (KV, workspace, graph). */
+int plamo_cuda_release_model(struct plamo_cuda *, struct model *);
+/* Unregister and free every preloaded range inside [src, src+bytes) (weights
+   whose host memory is about to be reused); prepared models are released too.
+   Returns the number of ranges freed. */
+int plamo_cuda_release_weights(struct plamo_cuda *, const void *src, uint64_t bytes);
 /* Declare the host K/V arrays of `model` canonical: the next call uploads
    rows [0, count) of every layer (use after writing host KV directly, e.g. by
    a CPU path or a prompt-cache restore that kept the same counts). A host

@@ -18,6 +18,8 @@
 // query of the same batch still needs; they are stored into the ring after
 // attention.
 #pragma once
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace plamo {
@@ -96,9 +98,10 @@ struct AttnParams {
 // (token, kv head) merges the split partials in split order.
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     extern __shared__ __align__(16) float sm[];
-    const uint64_t D = p.S.dim, half = D / 2, QH = p.S.qh, KH = p.S.kh, G = QH / KH;
+    const uint32_t D = static_cast<uint32_t>(p.S.dim), half = D / 2;
+    const uint32_t QH = static_cast<uint32_t>(p.S.qh), KH = static_cast<uint32_t>(p.S.kh), G = QH / KH;
     const uint64_t kh = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
-    const uint64_t KS = D + 1;          // padded key row: conflict-free column reads
+    const uint32_t KS = D + 1;          // padded key row: conflict-free column reads
     float *qs = sm;                     // [G][D]
     float *kt = qs + G * D;             // [tile][D + 1]
     float *vt = kt + kAttnTile * KS;    // [tile][D]
@@ -131,8 +134,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     for (uint64_t base = k0; base < k1; base += kAttnTile) {
         const uint64_t rows = k1 - base < kAttnTile ? k1 - base : kAttnTile;
         // Stage rotated keys and values of the tile.
-        for (uint64_t i = threadIdx.x; i < rows * half; i += blockDim.x) {
-            const uint64_t r = i / half, d = i % half, key = base + r;
+        for (uint32_t i = threadIdx.x; i < rows * half; i += blockDim.x) {
+            const uint32_t r = i / static_cast<uint32_t>(half), d = i - r * static_cast<uint32_t>(half);
+            const uint64_t key = base + r;
             const float *ksrc, *vsrc;
             if (key < P) {
                 const uint64_t slot = key % p.L.ring;
@@ -152,11 +156,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
         }
         __syncthreads();
         // Scores: sequential FMA over dim per (head, key), times 1/sqrt(dim).
-        for (uint64_t i = threadIdx.x; i < G * rows; i += blockDim.x) {
-            const uint64_t g = i / rows, r = i % rows;
+        for (uint32_t i = threadIdx.x; i < G * rows; i += blockDim.x) {
+            const uint32_t g = i / static_cast<uint32_t>(rows), r = i - g * static_cast<uint32_t>(rows);
             const float *qv = qs + g * D, *kv = kt + r * KS;
             float a = 0.0f;
-            for (uint64_t d = 0; d < D; ++d) a = fmaf(qv[d], kv[d], a);
+            for (uint32_t d = 0; d < D; ++d) a = fmaf(qv[d], kv[d], a);
             sc[g * kAttnTile + r] = __fmul_rn(a, scale);
         }
         __syncthreads();
@@ -177,10 +181,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
         }
         __syncthreads();
         // Weighted values: sequential FMA over the tile's keys.
-        for (uint64_t i = threadIdx.x; i < G * D; i += blockDim.x) {
-            const uint64_t g = i / D, d = i % D;
+        for (uint32_t i = threadIdx.x; i < G * D; i += blockDim.x) {
+            const uint32_t g = i / static_cast<uint32_t>(D), d = i - g * static_cast<uint32_t>(D);
             float a = __fmul_rn(acc[i], corr[g]);
-            for (uint64_t r = 0; r < rows; ++r) a = fmaf(sc[g * kAttnTile + r], vt[r * D + d], a);
+            for (uint32_t r = 0; r < rows; ++r) a = fmaf(sc[g * kAttnTile + r], vt[r * D + d], a);
             acc[i] = a;
         }
         __syncthreads();
@@ -236,6 +240,308 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
 inline size_t attention_smem_bytes(uint64_t G, uint64_t D) {
     return (G * D + kAttnTile * (D + 1) + kAttnTile * D + G * kAttnTile + G * D + 3 * G) *
            sizeof(float);
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention, fused: one launch per layer does the Q/K head RMSNorm and
+// RoPE of the new token, attention over the window with keys rotated on the
+// fly, and the store of the new K/V row into the ring.
+//
+// Grid (kv head, 8 key splits); the 8 splits of a kv head form one thread
+// block cluster. Every CTA normalises and rotates the G query heads of its
+// group itself (a few KB from L2); the CTA whose split ends at the new row
+// also normalises its key and writes K and V to ring slot P % ring (no CTA of
+// this launch reads that slot: it holds a row outside every window). Scores
+// are sequential FMA dots over dim, as the reference computes them; softmax
+// is online per tile with the reference's exp. The split partials stay in
+// shared memory and cluster rank 0 merges them through distributed shared
+// memory (no global round trip, no atomics).
+constexpr int kDecThreads = 256;
+constexpr int kDecTile = 64;
+constexpr int kDecSplits = 8;
+
+struct DecodeAttnParams {
+    AttnLayer L;
+    uint32_t qh, kh, dim;
+    float *qkv;  // [qh + 2 kh][dim] projection of the token (read only)
+    float *out;  // [qh][dim]
+};
+
+// Key tile row stride: D + 4 keeps 16-byte alignment and spreads the rows of
+// eight lanes over all 32 banks for 128-bit reads (D = 128), D + 1 for any D.
+__host__ __device__ inline uint32_t decode_key_stride(uint32_t D) { return D % 8 == 0 ? D + 4 : D + 1; }
+
+inline size_t decode_attention_smem(uint32_t G, uint32_t D) {
+    return sizeof(float) * (static_cast<size_t>(G) * D                     // qs
+                            + kDecTile * decode_key_stride(D)              // kt
+                            + kDecTile * D                                 // vt
+                            + G * kDecTile                                 // sc
+                            + G * D                                        // acc
+                            + 2 * D                                        // knew, vnew
+                            + 3 * G);                                      // m, l, corr
+}
+
+// DT: compile-time head dim (128) for the vectorised path, 0 for any even dim.
+template <int DT>
+__global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)
+    decode_attention_kernel(DecodeAttnParams p) {
+    extern __shared__ __align__(16) float sm[];
+    const uint32_t D = DT ? DT : p.dim, half = D / 2, G = p.qh / p.kh, KS = decode_key_stride(D);
+    const uint32_t kh = blockIdx.x, split = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = kDecThreads / 32;
+    float *qs = sm;
+    float *kt = qs + G * D;
+    float *vt = kt + kDecTile * KS;
+    float *sc = vt + kDecTile * D;
+    float *acc = sc + G * kDecTile;
+    float *knew = acc + G * D;
+    float *vnew = knew + D;
+    float *mrow = vnew + D;
+    float *lrow = mrow + G;
+    float *corr = lrow + G;
+    cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+
+    pdl_wait();
+    const uint64_t P = *p.L.appended;
+    const uint64_t lo = window_start(p.L, P, 0);
+    const uint32_t n = static_cast<uint32_t>(P + 1 - lo);
+    const uint64_t k0 = lo + static_cast<uint64_t>(n) * split / kDecSplits;
+    const uint64_t k1 = lo + static_cast<uint64_t>(n) * (split + 1) / kDecSplits;
+    const float *table_q = p.L.table + static_cast<uint64_t>(n - 1) * D;
+
+    // Q heads of the group: RMSNorm(+1), rotate at the query position.
+    for (uint32_t g = warp; g < G; g += warps) {
+        const float *x = p.qkv + static_cast<uint64_t>(kh * G + g) * D;
+        float ss = 0.0f;
+        if constexpr (DT != 0) {
+#pragma unroll
+            for (uint32_t i = lane; i < DT; i += 32) ss += x[i] * x[i];
+        } else {
+            for (uint32_t i = lane; i < D; i += 32) ss += x[i] * x[i];
+        }
+        const float inv = rms_inverse(warp_sum(ss), D);
+        for (uint32_t i = lane; i < half; i += 32) {
+            const float a = rms_apply(x[i], inv, p.L.qn[i], 1.0f);
+            const float b = rms_apply(x[i + half], inv, p.L.qn[i + half], 1.0f);
+            const float c = table_q[i], s = table_q[half + i];
+            qs[g * D + i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+            qs[g * D + i + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+        }
+    }
+    // The new row: normalised K (unrotated) and V, stored to the ring by the
+    // CTA whose split contains it.
+    const bool has_new = k1 == P + 1;
+    if (has_new && warp == warps - 1) {
+        const float *x = p.qkv + static_cast<uint64_t>(p.qh + kh) * D;
+        const float *v = p.qkv + static_cast<uint64_t>(p.qh + p.kh + kh) * D;
+        float ss = 0.0f;
+        for (uint32_t i = lane; i < D; i += 32) ss += x[i] * x[i];
+        const float inv = rms_inverse(warp_sum(ss), D);
+        const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
+        const uint64_t slot = P % p.L.ring;
+        for (uint32_t i = lane; i < D; i += 32) {
+            const float k = rms_apply(x[i], inv, p.L.kn[i], 1.0f);
+            knew[i] = k;
+            vnew[i] = v[i];
+            p.L.ring_k_w[slot * kvw + kh * D + i] = k;
+            p.L.ring_v_w[slot * kvw + kh * D + i] = v[i];
+        }
+    }
+    for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) acc[i] = 0.0f;
+    for (uint32_t g = threadIdx.x; g < G; g += kDecThreads) {
+        mrow[g] = -__int_as_float(0x7f800000);
+        lrow[g] = 0.0f;
+    }
+    __syncthreads();
+
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(D)));
+    const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
+    for (uint64_t base = k0; base < k1; base += kDecTile) {
+        const uint32_t rows = static_cast<uint32_t>(k1 - base < kDecTile ? k1 - base : kDecTile);
+        if constexpr (DT != 0) {
+            // 4 coordinate pairs per item, float4 loads and stores.
+            constexpr uint32_t Q = DT / 8;  // float4 groups per half
+            const uint32_t items = rows * Q;
+            for (uint32_t i0 = threadIdx.x; i0 < items; i0 += 2 * kDecThreads) {
+                float4 a[2], b[2], c[2], sn[2], va[2], vb[2];
+                uint32_t rr[2], dd[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const uint32_t i = i0 + u * kDecThreads;
+                    rr[u] = dd[u] = 0;
+                    if (i < items) {
+                        const uint32_t r = i / Q, d = (i - r * Q) * 4;
+                        const uint64_t key = base + r;
+                        const float *ksrc, *vsrc;
+                        if (key < P) {
+                            const uint64_t slot = key % p.L.ring;
+                            ksrc = p.L.ring_k + slot * kvw + kh * DT;
+                            vsrc = p.L.ring_v + slot * kvw + kh * DT;
+                        } else {
+                            ksrc = knew;
+                            vsrc = vnew;
+                        }
+                        const float *cs = p.L.table + (key - lo) * DT;
+                        a[u] = ld4(ksrc + d);
+                        b[u] = ld4(ksrc + d + DT / 2);
+                        c[u] = ld4(cs + d);
+                        sn[u] = ld4(cs + DT / 2 + d);
+                        va[u] = ld4(vsrc + d);
+                        vb[u] = ld4(vsrc + d + DT / 2);
+                        rr[u] = r;
+                        dd[u] = d;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    if (i0 + u * kDecThreads < items) {
+                        const uint32_t r = rr[u], d = dd[u];
+                        float4 lo4, hi4;
+                        lo4.x = __fsub_rn(__fmul_rn(a[u].x, c[u].x), __fmul_rn(b[u].x, sn[u].x));
+                        lo4.y = __fsub_rn(__fmul_rn(a[u].y, c[u].y), __fmul_rn(b[u].y, sn[u].y));
+                        lo4.z = __fsub_rn(__fmul_rn(a[u].z, c[u].z), __fmul_rn(b[u].z, sn[u].z));
+                        lo4.w = __fsub_rn(__fmul_rn(a[u].w, c[u].w), __fmul_rn(b[u].w, sn[u].w));
+                        hi4.x = __fadd_rn(__fmul_rn(b[u].x, c[u].x), __fmul_rn(a[u].x, sn[u].x));
+                        hi4.y = __fadd_rn(__fmul_rn(b[u].y, c[u].y), __fmul_rn(a[u].y, sn[u].y));
+                        hi4.z = __fadd_rn(__fmul_rn(b[u].z, c[u].z), __fmul_rn(a[u].z, sn[u].z));
+                        hi4.w = __fadd_rn(__fmul_rn(b[u].w, c[u].w), __fmul_rn(a[u].w, sn[u].w));
+                        *reinterpret_cast<float4 *>(kt + r * KS + d) = lo4;
+                        *reinterpret_cast<float4 *>(kt + r * KS + d + DT / 2) = hi4;
+                        *reinterpret_cast<float4 *>(vt + r * DT + d) = va[u];
+                        *reinterpret_cast<float4 *>(vt + r * DT + d + DT / 2) = vb[u];
+                    }
+                }
+            }
+        } else {
+            const uint32_t items = rows * half;
+            for (uint32_t i = threadIdx.x; i < items; i += kDecThreads) {
+                const uint32_t r = i / half, d = i - r * half;
+                const uint64_t key = base + r;
+                const float *ksrc, *vsrc;
+                if (key < P) {
+                    const uint64_t slot = key % p.L.ring;
+                    ksrc = p.L.ring_k + slot * kvw + kh * D;
+                    vsrc = p.L.ring_v + slot * kvw + kh * D;
+                } else {
+                    ksrc = knew;
+                    vsrc = vnew;
+                }
+                const float *cs = p.L.table + (key - lo) * D;
+                const float a = ksrc[d], b = ksrc[d + half], c = cs[d], sn = cs[half + d];
+                kt[r * KS + d] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+                kt[r * KS + d + half] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sn));
+                vt[r * D + d] = vsrc[d];
+                vt[r * D + d + half] = vsrc[d + half];
+            }
+        }
+        __syncthreads();
+        // Scores: one (head, key) per thread, sequential FMA over dim.
+        for (uint32_t i = threadIdx.x; i < G * rows; i += kDecThreads) {
+            const uint32_t g = i / rows, r = i - g * rows;
+            const float *qv = qs + g * D, *kv = kt + r * KS;
+            float a = 0.0f;
+            if constexpr (DT != 0) {
+#pragma unroll
+                for (uint32_t d = 0; d < DT; d += 4) {
+                    const float4 q4 = ld4(qv + d), k4 = ld4(kv + d);
+                    a = fmaf(q4.x, k4.x, a);
+                    a = fmaf(q4.y, k4.y, a);
+                    a = fmaf(q4.z, k4.z, a);
+                    a = fmaf(q4.w, k4.w, a);
+                }
+            } else {
+                for (uint32_t d = 0; d < D; ++d) a = fmaf(qv[d], kv[d], a);
+            }
+            sc[g * kDecTile + r] = __fmul_rn(a, scale);
+        }
+        __syncthreads();
+        // Online softmax: one warp per head, two keys per lane.
+        for (uint32_t g = warp; g < G; g += warps) {
+            const float ninf = -__int_as_float(0x7f800000);
+            const float v0 = lane < static_cast<int>(rows) ? sc[g * kDecTile + lane] : ninf;
+            const float v1 = lane + 32 < static_cast<int>(rows) ? sc[g * kDecTile + lane + 32] : ninf;
+            const float m = fmaxf(mrow[g], warp_max(fmaxf(v0, v1)));
+            const float e0 = lane < static_cast<int>(rows) ? plamo_exp(__fsub_rn(v0, m)) : 0.0f;
+            const float e1 = lane + 32 < static_cast<int>(rows) ? plamo_exp(__fsub_rn(v1, m)) : 0.0f;
+            if (lane < static_cast<int>(rows)) sc[g * kDecTile + lane] = e0;
+            if (lane + 32 < static_cast<int>(rows)) sc[g * kDecTile + lane + 32] = e1;
+            const float tile_sum = warp_sum(__fadd_rn(e0, e1));
+            if (lane == 0) {
+                const float cr = plamo_exp(__fsub_rn(mrow[g], m));
+                lrow[g] = __fadd_rn(__fmul_rn(lrow[g], cr), tile_sum);
+                mrow[g] = m;
+                corr[g] = cr;
+            }
+        }
+        __syncthreads();
+        // Weighted values: sequential FMA over the tile's keys.
+        if constexpr (DT != 0) {
+            for (uint32_t i = threadIdx.x; i < G * (DT / 4); i += kDecThreads) {
+                const uint32_t g = i / (DT / 4), d = (i - g * (DT / 4)) * 4;
+                float4 a = ld4(acc + g * DT + d);
+                const float cr = corr[g];
+                a = make_float4(__fmul_rn(a.x, cr), __fmul_rn(a.y, cr), __fmul_rn(a.z, cr), __fmul_rn(a.w, cr));
+                const float *sg = sc + g * kDecTile;
+#pragma unroll 8
+                for (uint32_t r = 0; r < rows; ++r) {
+                    const float pr = sg[r];
+                    const float4 v4 = ld4(vt + r * DT + d);
+                    a.x = fmaf(pr, v4.x, a.x);
+                    a.y = fmaf(pr, v4.y, a.y);
+                    a.z = fmaf(pr, v4.z, a.z);
+                    a.w = fmaf(pr, v4.w, a.w);
+                }
+                *reinterpret_cast<float4 *>(acc + g * DT + d) = a;
+            }
+        } else {
+            for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) {
+                const uint32_t g = i / D, d = i - g * D;
+                float a = __fmul_rn(acc[i], corr[g]);
+                for (uint32_t r = 0; r < rows; ++r) a = fmaf(sc[g * kDecTile + r], vt[r * D + d], a);
+                acc[i] = a;
+            }
+        }
+        __syncthreads();
+    }
+
+    // Merge the cluster's partials on rank 0 through distributed shared
+    // memory, in split order: M = max m_s, L = sum l_s e^(m_s - M),
+    // out = sum acc_s e^(m_s - M) / L.
+    cluster.sync();
+    if (cluster.block_rank() == 0) {
+        float *w = kt;  // [G][splits] weights, then [G] denominators
+        if (threadIdx.x < G) {
+            const uint32_t g = threadIdx.x;
+            float ms[kDecSplits];
+            float M = -__int_as_float(0x7f800000);
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) {
+                ms[r] = cluster.map_shared_rank(mrow, r)[g];
+                M = fmaxf(M, ms[r]);
+            }
+            float Ls = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) {
+                const float e = plamo_exp(__fsub_rn(ms[r], M));
+                w[g * kDecSplits + r] = e;
+                Ls = fmaf(cluster.map_shared_rank(lrow, r)[g], e, Ls);
+            }
+            w[G * kDecSplits + g] = Ls;
+        }
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) {
+            const uint32_t g = i / D;
+            float parts[kDecSplits];
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) parts[r] = cluster.map_shared_rank(acc, r)[i];
+            float A = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) A = fmaf(parts[r], w[g * kDecSplits + r], A);
+            p.out[static_cast<uint64_t>(kh * G) * D + i] = __fdiv_rn(A, w[G * kDecSplits + g]);
+        }
+    }
+    pdl_launch_dependents();
+    cluster.sync();  // keep every CTA's shared memory alive until rank 0 is done
 }
 
 // Store the K/V rows of tokens [first, tokens) (normalised K, V from the QKV

@@ -81,6 +81,7 @@ struct DModel {
     cudaGraphExec_t graph_exec = nullptr;
     uint64_t graph_nodes = 0;
     std::vector<void *> allocations;
+    std::vector<uintptr_t> signature;  // host descriptor identity at prepare time
 };
 
 }  // namespace
@@ -97,7 +98,10 @@ struct plamo_cuda {
     uint32_t *pinned_u32;  // small pinned staging (tokens, ids)
     uint64_t pinned_capacity;
     int sm_count;
+    int smem_optin;
     bool pdl;
+    bool bulk_gemv;
+    int gemv_ring_kb;
     int gemv_ctas;
     uint32_t *sink;
 };
@@ -235,13 +239,24 @@ bool launch_gemv_shape(plamo_cuda *c, const GemvParams &p, int U, uint32_t grid,
     }
 }
 
+// Allow each kernel the device's opt-in shared memory minus its static part.
+template <typename K>
+void allow_smem(K kernel, int optin) {
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, kernel) == cudaSuccess)
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - static_cast<int>(a.sharedSizeBytes));
+}
+
 template <int PRO, int EPI>
-void set_gemv_smem_limits() {
-    const int max = 227 * 1024;
-    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
-    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
-    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
-    cudaFuncSetAttribute(gemv_kernel<PRO, EPI, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, max);
+void set_gemv_smem_limits(int optin) {
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 1>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 2>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 4>, optin);
+    allow_smem(gemv_kernel<PRO, EPI, 4>, optin);
+    allow_smem(gemv_kernel<PRO, EPI, 2>, optin);
+    allow_smem(gemv_kernel<PRO, EPI, 1>, optin);
+    allow_smem(gemv_kernel<PRO, EPI, 0>, optin);
 }
 
 // Grid of a projection: one CTA per SM (times the configured factor), fewer
@@ -255,7 +270,7 @@ uint32_t gemv_grid(plamo_cuda *c, uint64_t units, uint64_t cols, int U, int pair
     for (;;) {
         const uint64_t per = (units + grid - 1) / grid;
         const size_t bytes = (cols_pad + per * segs * pair) * sizeof(float);
-        if (bytes <= 200 * 1024 || grid >= units) {
+        if (bytes + 1024 <= static_cast<size_t>(c->smem_optin) || grid >= units) {
             *smem = bytes;
             return static_cast<uint32_t>(grid);
         }
@@ -274,10 +289,32 @@ int gemv_chunks(const void *w, uint64_t cols) {
 
 template <int PRO, int EPI>
 bool gemv(plamo_cuda *c, GemvParams p, uint32_t *grid_out = nullptr) {
-    const int U = gemv_chunks(p.w, p.cols);
     const int pair = EPI == EPI_SWIGLU ? 2 : 1;
+    const uint64_t units = p.rows / pair;
+    if (c->bulk_gemv && gemv_bulk_shape(p.cols) && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 && units) {
+        uint64_t grid = std::min<uint64_t>(units, static_cast<uint64_t>(c->sm_count) * c->gemv_ctas);
+        // Ring depth: about gemv_ring_kb of chunks, at least two.
+        const uint32_t chunk = gemv_bulk_chunk_bytes(p.cols);
+        int stages = std::max(2, std::min<int>(kMaxStages, c->gemv_ring_kb * 1024 / static_cast<int>(chunk)));
+        size_t smem = 0;
+        for (;;) {
+            smem = gemv_bulk_smem(p.cols, (units + grid - 1) / grid, pair, stages);
+            if (smem + 2048 <= static_cast<size_t>(c->smem_optin)) break;
+            if (stages > 2) --stages;
+            else if (grid < units) grid = std::min<uint64_t>(units, grid * 2);
+            else return false;
+        }
+        if (grid_out) *grid_out = static_cast<uint32_t>(grid);
+        const dim3 g(static_cast<uint32_t>(grid)), b(kBulkThreads);
+        switch (gemv_bulk_sets(p.cols)) {
+        case 1: return launch(c, gemv_bulk_kernel<PRO, EPI, 1>, g, b, smem, p, stages);
+        case 2: return launch(c, gemv_bulk_kernel<PRO, EPI, 2>, g, b, smem, p, stages);
+        default: return launch(c, gemv_bulk_kernel<PRO, EPI, 4>, g, b, smem, p, stages);
+        }
+    }
+    const int U = gemv_chunks(p.w, p.cols);
     size_t smem = 0;
-    const uint32_t grid = gemv_grid(c, p.rows / pair, p.cols, U, pair, &smem);
+    const uint32_t grid = gemv_grid(c, units, p.cols, U, pair, &smem);
     if (grid_out) *grid_out = grid;
     return launch_gemv_shape<PRO, EPI>(c, p, U, grid, smem);
 }
@@ -327,6 +364,35 @@ void free_model(plamo_cuda *c, DModel *m) {
     for (void *p : m->allocations) cudaFree(p);
     m->allocations.clear();
     (void)c;
+}
+
+// Identity of a host descriptor tree: dimensions, every weight and KV pointer.
+std::vector<uintptr_t> model_signature(const struct model *model) {
+    std::vector<uintptr_t> sig;
+    auto add = [&](const void *p) { sig.push_back(reinterpret_cast<uintptr_t>(p)); };
+    sig.push_back(model->vocab);
+    sig.push_back(model->hidden);
+    sig.push_back(model->count);
+    add(model->embedding);
+    add(model->norm);
+    add(model->head);
+    add(model->state);
+    add(model->logits);
+    for (uint64_t i = 0; i < model->count; ++i) {
+        const struct layer *l = model->layers[i];
+        const struct qkv *q = l->mixer->qkv;
+        const struct cache *k = l->mixer->cache;
+        add(l);
+        add(q->weight);
+        add(l->mixer->weight);
+        add(l->mlp->gu);
+        add(l->mlp->down);
+        add(k->k);
+        sig.push_back(k->capacity);
+        sig.push_back(q->dim);
+        sig.push_back(l->mlp->intermediate);
+    }
+    return sig;
 }
 
 DModel *find_model(plamo_cuda *c, struct model *model) {
@@ -414,11 +480,17 @@ bool fits(const DModel *m, uint64_t tokens) {
 }
 
 // ---- decode step -----------------------------------------------------------
+bool launch_decode_attention(plamo_cuda *c, DModel *m, uint64_t l) {
+    DecodeAttnParams dp{attn_layer(m, l), static_cast<uint32_t>(m->QH), static_cast<uint32_t>(m->KH),
+                        static_cast<uint32_t>(m->D), m->qkv, m->attn};
+    const size_t smem = decode_attention_smem(static_cast<uint32_t>(m->QH / m->KH), static_cast<uint32_t>(m->D));
+    const dim3 grid(static_cast<uint32_t>(m->KH), kDecSplits), block(kDecThreads);
+    if (m->D == 128) return launch(c, decode_attention_kernel<128>, grid, block, smem, dp);
+    return launch(c, decode_attention_kernel<0>, grid, block, smem, dp);
+}
+
 bool record_decode(plamo_cuda *c, DModel *m) {
     int s = 0;
-    AttnShape shape{1, m->QH, m->KH, m->D, m->QW};
-    const uint64_t G = m->QH / m->KH;
-    const size_t attn_smem = attention_smem_bytes(G, m->D);
     for (uint64_t l = 0; l < m->L; ++l) {
         const DLayer &L = m->layers[l];
         GemvParams p{};
@@ -446,15 +518,7 @@ bool record_decode(plamo_cuda *c, DModel *m) {
             ok = gemv<PRO_RESID_NORM, EPI_STORE>(c, p);
         }
         if (!ok) return false;
-        AttnLayer al = attn_layer(m, l);
-        if (!launch(c, qk_prep_kernel, dim3(m->QH + m->KH, 1), dim3(128), 0, m->qkv, m->q, al, shape))
-            return false;
-        AttnParams ap{al, shape, m->q, m->qkv, m->attn, m->part, m->tickets, m->splits};
-        if (!launch(c, attention_kernel, dim3(m->KH, 1, m->splits), dim3(kAttnThreads), attn_smem, ap))
-            return false;
-        if (!launch(c, kv_store_kernel, dim3(1), dim3(256), 0, al, shape, static_cast<const float *>(m->qkv),
-                    uint64_t{0}))
-            return false;
+        if (!launch_decode_attention(c, m, l)) return false;
         GemvParams o{};
         o.w = L.o_w;
         o.rows = m->H;
@@ -689,6 +753,10 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->info.sm_count = prop.multiProcessorCount;
     const char *pdl = getenv("PLAMO_CUDA_PDL");
     c->pdl = !pdl || strcmp(pdl, "0");
+    const char *bulk = getenv("PLAMO_CUDA_BULK_GEMV");
+    c->bulk_gemv = !bulk || strcmp(bulk, "0");
+    const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
+    c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
     c->gemv_ctas = ctas ? std::max(1, atoi(ctas)) : 1;
     if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
@@ -700,14 +768,24 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
         return nullptr;
     }
     c->pinned_capacity = 64 * 1024;
-    set_gemv_smem_limits<PRO_X, EPI_STORE>();
-    set_gemv_smem_limits<PRO_NORM, EPI_STORE>();
-    set_gemv_smem_limits<PRO_RESID_NORM, EPI_STORE>();
-    set_gemv_smem_limits<PRO_EMBED_NORM, EPI_STORE>();
-    set_gemv_smem_limits<PRO_RESID_NORM, EPI_SWIGLU>();
-    set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>();
-    set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>();
-    cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg.device);
+    c->smem_optin = optin;
+    set_gemv_smem_limits<PRO_X, EPI_STORE>(optin);
+    set_gemv_smem_limits<PRO_NORM, EPI_STORE>(optin);
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_STORE>(optin);
+    set_gemv_smem_limits<PRO_EMBED_NORM, EPI_STORE>(optin);
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_SWIGLU>(optin);
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>(optin);
+    set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin);
+    allow_smem(attention_kernel, optin);
+    allow_smem(decode_attention_kernel<128>, optin);
+    allow_smem(decode_attention_kernel<0>, optin);
+    if ((e = cudaGetLastError()) != cudaSuccess) {
+        if (error && cap) snprintf(error, cap, "cannot configure kernels: %s", cudaGetErrorString(e));
+        plamo_cuda_close(c);
+        return nullptr;
+    }
     return c;
 }
 
@@ -796,9 +874,16 @@ int plamo_cuda_warm_cache(struct plamo_cuda *c) {
 int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     if (!c || !model || !model->count || !model->hidden || !model->vocab || !model->layers) return 0;
     cudaSetDevice(c->device);
-    if (find_model(c, model)) return 1;
+    if (DModel *old = find_model(c, model)) {
+        if (old->signature == model_signature(model)) return 1;
+        // Another descriptor now lives at this address: drop the stale state.
+        cudaStreamSynchronize(c->stream);
+        free_model(c, old);
+        c->models.erase(model);
+    }
     auto m = std::make_unique<DModel>();
     m->host = model;
+    m->signature = model_signature(model);
     const struct qkv *q0 = model->layers[0]->mixer->qkv;
     m->H = model->hidden;
     m->QH = q0->qh;
@@ -883,8 +968,9 @@ int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     m->arg_idx = static_cast<uint32_t *>(dalloc(c, m.get(), grid_max * 4));
     m->arg_nan = static_cast<uint32_t *>(dalloc(c, m.get(), grid_max * 4));
     m->d_token = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
+    // [next token, error flag]: one 8-byte read returns both.
     m->d_next = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
-    m->d_error = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
+    m->d_error = m->d_next + 1;
     // Prompt buffers.
     m->tmax = std::max<uint64_t>(c->config.max_prefill, kVerifyMax);
     const uint64_t T = m->tmax;
@@ -950,10 +1036,10 @@ int plamo_cuda_forward_greedy(struct plamo_cuda *c, struct model *model, uint64_
     cudaEventRecord(c->ev0, c->stream);
     if (!launch_decode(c, m)) return -1;
     cudaEventRecord(c->ev1, c->stream);
-    if (!note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 1, m->d_next, 4, cudaMemcpyDeviceToHost, c->stream)) ||
+    if (!note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 1, m->d_next, 8, cudaMemcpyDeviceToHost, c->stream)) ||
         !note(c, "forward", cudaStreamSynchronize(c->stream)))
         return -1;
-    if (!check_device_error(c, m)) return -1;
+    if (c->pinned_u32[2] && !check_device_error(c, m)) return -1;
     c->info.gpu_seconds += elapsed(c);
     c->info.forwards++;
     publish_counts(m, 1);
@@ -994,15 +1080,15 @@ static int prompt(struct plamo_cuda *c, struct model *model, const uint32_t *ids
                                                      c->stream)))
         return -1;
     if (!copy_outputs(c, m) ||
-        !note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 2, m->d_next, 4, cudaMemcpyDeviceToHost, c->stream)) ||
+        !note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 4, m->d_next, 8, cudaMemcpyDeviceToHost, c->stream)) ||
         !note(c, "prefill", cudaStreamSynchronize(c->stream)))
         return -1;
-    if (!check_device_error(c, m)) return -1;
+    if (c->pinned_u32[5] && !check_device_error(c, m)) return -1;
     c->info.gpu_seconds += elapsed(c);
     c->info.prefills++;
     publish_counts(m, tokens);
     if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
-    if (next) *next = c->pinned_u32[2];
+    if (next) *next = c->pinned_u32[4];
     return 1;
 }
 
@@ -1125,9 +1211,6 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
         return 0;
     }
     m->verify_valid = false;
-    AttnShape shape{1, m->QH, m->KH, m->D, m->QW};
-    const size_t attn_smem = attention_smem_bytes(m->QH / m->KH, m->D);
-    AttnLayer al = attn_layer(m, index);
     bool ok = note(c, "layer state", cudaMemcpyAsync(m->state[0], state, m->H * 4, cudaMemcpyHostToDevice,
                                                      c->stream));
     cudaEventRecord(c->ev0, c->stream);
@@ -1140,11 +1223,7 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
     p.off2 = 1.0f;
     p.y = m->qkv;
     ok = ok && gemv<PRO_NORM, EPI_STORE>(c, p);
-    ok = ok && launch(c, qk_prep_kernel, dim3(m->QH + m->KH, 1), dim3(128), 0, m->qkv, m->q, al, shape);
-    AttnParams ap{al, shape, m->q, m->qkv, m->attn, m->part, m->tickets, m->splits};
-    ok = ok && launch(c, attention_kernel, dim3(m->KH, 1, m->splits), dim3(kAttnThreads), attn_smem, ap);
-    ok = ok && launch(c, kv_store_kernel, dim3(1), dim3(256), 0, al, shape, static_cast<const float *>(m->qkv),
-                      uint64_t{0});
+    ok = ok && launch_decode_attention(c, m, index);
     GemvParams o{};
     o.w = L.o_w;
     o.rows = m->H;
@@ -1189,6 +1268,39 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
     L.host->mixer->rotation->scale_bits = float_to_bits(L.scale);
     if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
     return 1;
+}
+
+int plamo_cuda_release_model(struct plamo_cuda *c, struct model *model) {
+    if (!c) return 0;
+    DModel *m = find_model(c, model);
+    if (!m) return 0;
+    cudaStreamSynchronize(c->stream);
+    free_model(c, m);
+    c->models.erase(model);
+    return 1;
+}
+
+int plamo_cuda_release_weights(struct plamo_cuda *c, const void *src, uint64_t bytes) {
+    if (!c) return 0;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(src), hi = lo + bytes;
+    cudaStreamSynchronize(c->stream);
+    int released = 0;
+    for (size_t i = 0; i < c->ranges.size();) {
+        const Range &r = c->ranges[i];
+        if (r.host >= lo && r.host + r.bytes <= hi) {
+            cudaFree(r.dev);
+            c->info.weight_bytes -= r.bytes;
+            c->ranges.erase(c->ranges.begin() + static_cast<long>(i));
+            ++released;
+        } else {
+            ++i;
+        }
+    }
+    if (released) {  // prepared models may point into the freed ranges
+        for (auto &kv : c->models) free_model(c, kv.second.get());
+        c->models.clear();
+    }
+    return released;
 }
 
 int plamo_cuda_invalidate(struct plamo_cuda *c, struct model *model) {

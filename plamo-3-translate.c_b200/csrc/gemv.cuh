@@ -67,16 +67,60 @@ __device__ __forceinline__ float dot8(uint4 w, const float *x, float acc) {
     return acc;
 }
 
+// Same with the 8 inputs in registers.
+__device__ __forceinline__ float dot8r(uint4 w, const float *x, float acc) {
+    acc = fmaf(bf16_lo(w.x), x[0], acc);
+    acc = fmaf(bf16_hi(w.x), x[1], acc);
+    acc = fmaf(bf16_lo(w.y), x[2], acc);
+    acc = fmaf(bf16_hi(w.y), x[3], acc);
+    acc = fmaf(bf16_lo(w.z), x[4], acc);
+    acc = fmaf(bf16_hi(w.z), x[5], acc);
+    acc = fmaf(bf16_lo(w.w), x[6], acc);
+    acc = fmaf(bf16_hi(w.w), x[7], acc);
+    return acc;
+}
+
 // Build the FP32 input vector in shared memory. All blocks compute the same
 // bits (same reduction shape), block 0 publishes state/normalised copies.
+//
+// Latency matters more than work here (a few KB per block while the weight
+// stream waits), so every global load of a phase is issued before any of
+// them is used: the vector path keeps up to kPV float4 per thread in
+// registers, one L2 round trip per input instead of one per loop trip.
+constexpr int kPV = 4;
+
+__device__ __forceinline__ float4 norm4(uint2 w, float offset) {
+    return make_float4(__fadd_rn(bf16_lo(w.x), offset), __fadd_rn(bf16_hi(w.x), offset),
+                       __fadd_rn(bf16_lo(w.y), offset), __fadd_rn(bf16_hi(w.y), offset));
+}
+__device__ __forceinline__ float sq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+__device__ __forceinline__ float4 apply4(float4 x, float inv, float4 w) {
+    return make_float4(__fmul_rn(__fmul_rn(x.x, inv), w.x), __fmul_rn(__fmul_rn(x.y, inv), w.y),
+                       __fmul_rn(__fmul_rn(x.z, inv), w.z), __fmul_rn(__fmul_rn(x.w, inv), w.w));
+}
+
 template <int PRO>
 __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, float *red) {
     const uint64_t n = p.cols;
     const bool publish = blockIdx.x == 0;
+    const uint32_t nt = blockDim.x;
     if (PRO == PRO_X) {
-        for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) xs[i] = p.x[i];
+        const uint32_t n4 = static_cast<uint32_t>(n / 4);
+        const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+        float4 *xs4 = reinterpret_cast<float4 *>(xs);
+        uint32_t i = threadIdx.x;
+        for (; i + 3 * nt < n4; i += 4 * nt) {
+            const float4 a = x4[i], b = x4[i + nt], c = x4[i + 2 * nt], d = x4[i + 3 * nt];
+            xs4[i] = a;
+            xs4[i + nt] = b;
+            xs4[i + 2 * nt] = c;
+            xs4[i + 3 * nt] = d;
+        }
+        for (; i < n4; i += nt) xs4[i] = x4[i];
+        for (uint64_t j = 4ull * n4 + threadIdx.x; j < n; j += nt) xs[j] = p.x[j];
         return true;
     }
+    const bool vec = n % 4 == 0 && n <= 4ull * kPV * nt;
     if (PRO == PRO_EMBED_NORM) {
         const uint32_t token = *p.token;
         if (token >= p.vocab) {
@@ -84,28 +128,81 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
             return false;
         }
         const uint16_t *row = p.embedding + static_cast<uint64_t>(token) * n;
-        for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) xs[i] = bf16_to_f32(row[i]);
-    } else if (PRO == PRO_NORM) {
-        for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) xs[i] = p.state_in[i];
-    } else {  // PRO_RESID_NORM: state + rmsnorm(branch, norm1, off1)
+        for (uint64_t i = threadIdx.x; i < n; i += nt) xs[i] = bf16_to_f32(row[i]);
+    } else if (vec) {
+        const uint32_t n4 = static_cast<uint32_t>(n / 4);
+        float4 st[kPV], br[kPV];
+        uint2 w1[kPV];
+#pragma unroll
+        for (int k = 0; k < kPV; ++k) {
+            const uint32_t i = threadIdx.x + k * nt;
+            if (i < n4) {
+                st[k] = ld4(p.state_in + 4 * i);
+                if (PRO == PRO_RESID_NORM) {
+                    br[k] = ld4(p.branch + 4 * i);
+                    w1[k] = *reinterpret_cast<const uint2 *>(p.norm1 + 4 * i);
+                }
+            }
+        }
+        if (PRO == PRO_RESID_NORM) {
+            float s = 0.0f;
+#pragma unroll
+            for (int k = 0; k < kPV; ++k)
+                if (threadIdx.x + k * nt < n4) s += sq4(br[k]);
+            const float inv = rms_inverse(block_sum(s, red), n);
+#pragma unroll
+            for (int k = 0; k < kPV; ++k) {
+                const uint32_t i = threadIdx.x + k * nt;
+                if (i < n4) {
+                    const float4 b = apply4(br[k], inv, norm4(w1[k], p.off1));
+                    st[k] = make_float4(__fadd_rn(st[k].x, b.x), __fadd_rn(st[k].y, b.y),
+                                        __fadd_rn(st[k].z, b.z), __fadd_rn(st[k].w, b.w));
+                }
+            }
+        }
+        uint2 w2[kPV];
         float s = 0.0f;
-        for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
+#pragma unroll
+        for (int k = 0; k < kPV; ++k) {
+            const uint32_t i = threadIdx.x + k * nt;
+            if (i < n4) {
+                w2[k] = *reinterpret_cast<const uint2 *>(p.norm2 + 4 * i);
+                s += sq4(st[k]);
+                if (publish && p.state_out) *reinterpret_cast<float4 *>(p.state_out + 4 * i) = st[k];
+            }
+        }
+        const float inv = rms_inverse(block_sum(s, red), n);
+#pragma unroll
+        for (int k = 0; k < kPV; ++k) {
+            const uint32_t i = threadIdx.x + k * nt;
+            if (i < n4) {
+                const float4 v = apply4(st[k], inv, norm4(w2[k], p.off2));
+                *reinterpret_cast<float4 *>(xs + 4 * i) = v;
+                if (publish && p.norm_out) *reinterpret_cast<float4 *>(p.norm_out + 4 * i) = v;
+            }
+        }
+        return true;
+    } else if (PRO == PRO_NORM) {
+        for (uint64_t i = threadIdx.x; i < n; i += nt) xs[i] = p.state_in[i];
+    } else {  // PRO_RESID_NORM, any length: state + rmsnorm(branch, norm1, off1)
+        float s = 0.0f;
+        for (uint64_t i = threadIdx.x; i < n; i += nt) {
             const float b = p.branch[i];
             s += b * b;
         }
         const float inv = rms_inverse(block_sum(s, red), n);
-        for (uint64_t i = threadIdx.x; i < n; i += blockDim.x)
+        for (uint64_t i = threadIdx.x; i < n; i += nt)
             xs[i] = __fadd_rn(p.state_in[i], rms_apply(p.branch[i], inv, p.norm1[i], p.off1));
     }
     __syncthreads();
     float s = 0.0f;
-    for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    for (uint64_t i = threadIdx.x; i < n; i += nt) {
         const float v = xs[i];
         s += v * v;
         if (publish && p.state_out) p.state_out[i] = v;
     }
     const float inv = rms_inverse(block_sum(s, red), n);
-    for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    for (uint64_t i = threadIdx.x; i < n; i += nt) {
         const float v = rms_apply(xs[i], inv, p.norm2[i], p.off2);
         xs[i] = v;
         if (publish && p.norm_out) p.norm_out[i] = v;
@@ -118,108 +215,25 @@ __device__ __forceinline__ bool arg_better(float v, uint32_t i, float bv, uint32
     return v > bv || (v == bv && i < bi);
 }
 
-// U: 256-column chunks per work item (U = 0: any shape, scalar loads).
-template <int PRO, int EPI, int U>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
-    extern __shared__ __align__(16) float smem[];
-    __shared__ float red[kGemvWarps];
-    __shared__ float best_val[kGemvWarps];
-    __shared__ uint32_t best_idx[kGemvWarps];
+// Fixed-order reduction of per-slot partials ([unit][slot][pair]), then the
+// epilogue: store, SwiGLU of gate/up pairs, or per-block argmax candidates.
+template <int EPI>
+__device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *partial, uint64_t u0,
+                                              uint64_t u1, uint64_t slots, float *) {
+    __shared__ float best_val[32];
+    __shared__ uint32_t best_idx[32];
     __shared__ uint32_t any_nan;
-
     constexpr int kPair = EPI == EPI_SWIGLU ? 2 : 1;
-    const uint64_t cols = p.cols;
-    const uint64_t units = p.rows / kPair;
-    const uint64_t u0 = units * blockIdx.x / gridDim.x;
-    const uint64_t u1 = units * (blockIdx.x + 1) / gridDim.x;
-    const uint64_t seg_cols = U ? 256 * U : cols;
-    const uint64_t segs = U ? cols / seg_cols : 1;
-    const uint64_t items = (u1 - u0) * segs;
-    const uint64_t cols_pad = (cols + 3) & ~3ull;
-    float *xs = smem;
-    float *partial = smem + cols_pad;  // [(u1-u0) * segs * kPair]
-
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint64_t policy = evict_first_policy();
-    const uint64_t half_rows = p.rows / 2;
-
-    // Row pointer of work item j, pair member m.
-    auto row_ptr = [&](uint64_t j, int m) -> const uint16_t * {
-        const uint64_t unit = u0 + j / segs;
-        const uint64_t row = m ? unit + half_rows : unit;
-        return p.w + row * cols + (j % segs) * seg_cols;
-    };
-
-    constexpr int kLoads = (U ? U : 1) * kPair;
-    uint4 cur[kLoads];
-    uint64_t j = warp;
-    if (U) {
-        if (j < items) {
-#pragma unroll
-            for (int m = 0; m < kPair; ++m)
-#pragma unroll
-                for (int k = 0; k < U; ++k)
-                    cur[m * U + k] = load_stream(row_ptr(j, m) + k * 256 + lane * 8, policy);
-        }
-    }
-
-    pdl_wait();
-    const bool ok = gemv_prologue<PRO>(p, xs, red);
-    __syncthreads();
-    if (!ok) return;
-
-    if (U) {
-        for (; j < items; j += kGemvWarps) {
-            const uint64_t jn = j + kGemvWarps;
-            uint4 nxt[kLoads];
-            if (jn < items) {
-#pragma unroll
-                for (int m = 0; m < kPair; ++m)
-#pragma unroll
-                    for (int k = 0; k < U; ++k)
-                        nxt[m * U + k] = load_stream(row_ptr(jn, m) + k * 256 + lane * 8, policy);
-            }
-            const float *xseg = xs + (j % segs) * seg_cols + lane * 8;
-#pragma unroll
-            for (int m = 0; m < kPair; ++m) {
-                float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-                for (int k = 0; k < U; ++k) {
-                    if (k & 1) a1 = dot8(cur[m * U + k], xseg + k * 256, a1);
-                    else a0 = dot8(cur[m * U + k], xseg + k * 256, a0);
-                }
-                const float s = warp_sum(a0 + a1);
-                if (lane == 0) partial[(j * kPair) + m] = s;
-            }
-            if (jn < items) {
-#pragma unroll
-                for (int k = 0; k < kLoads; ++k) cur[k] = nxt[k];
-            }
-        }
-    } else {
-        for (; j < items; j += kGemvWarps) {
-#pragma unroll
-            for (int m = 0; m < kPair; ++m) {
-                const uint16_t *wr = row_ptr(j, m);
-                float a = 0.0f;
-                for (uint64_t c = lane; c < cols; c += 32) a = fmaf(bf16_to_f32(wr[c]), xs[c], a);
-                a = warp_sum(a);
-                if (lane == 0) partial[(j * kPair) + m] = a;
-            }
-        }
-    }
-    pdl_launch_dependents();
-    __syncthreads();
-
-    // Fixed-order reduction of the segment partials, then the epilogue.
+    const int warps = (blockDim.x + 31) >> 5;
     float bv = -__int_as_float(0x7f800000);
     uint32_t bi = 0xffffffffu;
     bool saw_nan = false;
     for (uint64_t u = threadIdx.x; u < u1 - u0; u += blockDim.x) {
         float t0 = 0.0f, t1 = 0.0f;
-        for (uint64_t s = 0; s < segs; ++s) {
-            t0 += partial[(u * segs + s) * kPair];
-            if (kPair == 2) t1 += partial[(u * segs + s) * kPair + 1];
+        for (uint64_t s = 0; s < slots; ++s) {
+            t0 += partial[(u * slots + s) * kPair];
+            if (kPair == 2) t1 += partial[(u * slots + s) * kPair + 1];
         }
         const uint64_t unit = u0 + u;
         if (EPI == EPI_SWIGLU) {
@@ -254,7 +268,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
         }
         __syncthreads();
         if (threadIdx.x == 0) {
-            for (int w = 1; w < kGemvWarps; ++w)
+            for (int w = 1; w < warps; ++w)
                 if (arg_better(best_val[w], best_idx[w], bv, bi)) {
                     bv = best_val[w];
                     bi = best_idx[w];
@@ -264,6 +278,288 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
             p.arg_nan[blockIdx.x] = any_nan;
         }
     }
+}
+
+// Register-streamed variant for shapes the bulk kernel does not take.
+// U: 256-column chunks per work item (U = 0: any shape, scalar loads).
+template <int PRO, int EPI, int U>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
+    extern __shared__ __align__(16) float smem[];
+    __shared__ float red[kGemvWarps];
+
+    constexpr int kPair = EPI == EPI_SWIGLU ? 2 : 1;
+    const uint64_t cols = p.cols;
+    const uint64_t units = p.rows / kPair;
+    const uint64_t u0 = units * blockIdx.x / gridDim.x;
+    const uint64_t u1 = units * (blockIdx.x + 1) / gridDim.x;
+    const uint64_t seg_cols = U ? 256 * U : cols;
+    const uint64_t segs = U ? cols / seg_cols : 1;
+    const uint64_t items = (u1 - u0) * segs;
+    const uint64_t cols_pad = (cols + 3) & ~3ull;
+    float *xs = smem;
+    float *partial = smem + cols_pad;  // [(u1-u0) * segs * kPair]
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t policy = evict_first_policy();
+    const uint64_t half_rows = p.rows / 2;
+
+    // Row pointer of work item j, pair member m (32-bit split of j).
+    const uint32_t segs32 = static_cast<uint32_t>(segs);
+    auto row_ptr = [&](uint64_t j, int m) -> const uint16_t * {
+        const uint32_t jj = static_cast<uint32_t>(j), q = jj / segs32;
+        const uint64_t unit = u0 + q;
+        const uint64_t row = m ? unit + half_rows : unit;
+        return p.w + row * cols + static_cast<uint64_t>(jj - q * segs32) * seg_cols;
+    };
+
+    constexpr int kLoads = (U ? U : 1) * kPair;
+    uint4 cur[kLoads];
+    uint64_t j = warp;
+    if (U) {
+        if (j < items) {
+#pragma unroll
+            for (int m = 0; m < kPair; ++m)
+#pragma unroll
+                for (int k = 0; k < U; ++k)
+                    cur[m * U + k] = load_stream(row_ptr(j, m) + k * 256 + lane * 8, policy);
+        }
+    }
+
+    pdl_wait();
+    const bool ok = gemv_prologue<PRO>(p, xs, red);
+    __syncthreads();
+    if (!ok) return;
+
+    if (U) {
+        for (; j < items; j += kGemvWarps) {
+            const uint64_t jn = j + kGemvWarps;
+            uint4 nxt[kLoads];
+            if (jn < items) {
+#pragma unroll
+                for (int m = 0; m < kPair; ++m)
+#pragma unroll
+                    for (int k = 0; k < U; ++k)
+                        nxt[m * U + k] = load_stream(row_ptr(jn, m) + k * 256 + lane * 8, policy);
+            }
+            const float *xseg = xs + static_cast<uint64_t>(static_cast<uint32_t>(j) % segs32) * seg_cols + lane * 8;
+#pragma unroll
+            for (int m = 0; m < kPair; ++m) {
+                float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    if (k & 1) a1 = dot8(cur[m * U + k], xseg + k * 256, a1);
+                    else a0 = dot8(cur[m * U + k], xseg + k * 256, a0);
+                }
+                const float s = warp_sum(a0 + a1);
+                if (lane == 0) partial[(j * kPair) + m] = s;
+            }
+            if (jn < items) {
+#pragma unroll
+                for (int k = 0; k < kLoads; ++k) cur[k] = nxt[k];
+            }
+        }
+    } else {
+        for (; j < items; j += kGemvWarps) {
+#pragma unroll
+            for (int m = 0; m < kPair; ++m) {
+                const uint16_t *wr = row_ptr(j, m);
+                float a = 0.0f;
+                for (uint64_t c = lane; c < cols; c += 32) a = fmaf(bf16_to_f32(wr[c]), xs[c], a);
+                a = warp_sum(a);
+                if (lane == 0) partial[(j * kPair) + m] = a;
+            }
+        }
+    }
+    pdl_launch_dependents();
+    __syncthreads();
+    gemv_epilogue<EPI>(p, partial, u0, u1, segs, red);
+}
+
+// ---------------------------------------------------------------------------
+// Bulk-streamed variant (cols % 512 == 0, 16-byte aligned rows).
+//
+// A CTA's rows are one contiguous byte range of W (two for gate/up pairs). A
+// producer warp streams it through a ring of shared-memory stages with
+// cp.async.bulk (the TMA engine, plain 1-D copies), each stage guarded by a
+// full/empty mbarrier pair; the first stages are requested before
+// griddepcontrol.wait, so under programmatic dependent launch the stream
+// starts while the previous kernel drains. A chunk is a whole number of
+// rows (several short rows, or one long row), split into 512-element
+// sub-ranges; consumer warp w takes sub-ranges w, w+16, w+32, w+48 of every
+// chunk, which are always the same column slots, so each warp keeps its
+// slice of the input vector in registers for the whole kernel and reduces
+// each sub-range to one partial sum per (row, 512-column slot).
+constexpr int kBulkConsumers = 16;
+constexpr int kBulkThreads = (kBulkConsumers + 1) * 32;
+constexpr int kSubElems = 512;
+constexpr int kMaxStages = 12;
+constexpr int kMaxSets = 4;  // sub-ranges per warp per chunk
+
+// Sub-ranges per chunk for `slots` 512-column slots per row: whole rows, at
+// most 16 sub-ranges when rows are short, one row (<= 64 slots) otherwise.
+__host__ __device__ inline uint32_t bulk_chunk_subs(uint32_t slots) {
+    if (slots <= 16) return (16 / slots) * slots;
+    return slots;
+}
+
+template <int PRO, int EPI, int SETS>
+__global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, int stages) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    __shared__ float red[32];
+    __shared__ int abort_flag;
+
+    constexpr int kPair = EPI == EPI_SWIGLU ? 2 : 1;
+    const uint64_t cols = p.cols;
+    const uint64_t units = p.rows / kPair;
+    const uint64_t u0 = units * blockIdx.x / gridDim.x;
+    const uint64_t u1 = units * (blockIdx.x + 1) / gridDim.x;
+    const uint64_t rows_local = u1 - u0;
+    const uint32_t slots = static_cast<uint32_t>(cols / kSubElems);
+    const uint32_t csubs = bulk_chunk_subs(slots);
+    const uint32_t chunk_bytes = csubs * kSubElems * 2;
+    const uint32_t subs_per_range = static_cast<uint32_t>(rows_local) * slots;
+    const uint32_t cpr = (subs_per_range + csubs - 1) / csubs;  // chunks per range
+    const uint32_t total = kPair * cpr;
+    const uint64_t cols_pad = (cols + 3) & ~3ull;
+    unsigned char *ring = smem_raw;
+    float *xs = reinterpret_cast<float *>(smem_raw + static_cast<size_t>(stages) * chunk_bytes);
+    float *partial = xs + cols_pad;  // [rows_local][slots][kPair]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool producer = warp == kBulkConsumers;
+    const uint64_t policy = evict_first_policy();
+    const uint64_t half_rows = p.rows / 2;
+    const uint16_t *range_base[2] = {p.w + u0 * cols, p.w + (u0 + half_rows) * cols};
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], kBulkConsumers);
+        }
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](uint32_t k, uint32_t s) {
+        const uint32_t m = (kPair == 2 && k >= cpr) ? 1u : 0u;
+        const uint32_t kc = k - m * cpr;
+        const uint32_t left = subs_per_range - kc * csubs;
+        const uint32_t bytes = (left < csubs ? left : csubs) * kSubElems * 2;
+        mbar_expect_tx(&full_bar[s], bytes);
+        bulk_load(ring + static_cast<size_t>(s) * chunk_bytes,
+                  range_base[m] + static_cast<uint64_t>(kc) * csubs * kSubElems, bytes, &full_bar[s], policy);
+    };
+    const uint32_t primed = total < static_cast<uint32_t>(stages) ? total : static_cast<uint32_t>(stages);
+    uint32_t issued = 0;  // meaningful in the producer lane only
+    if (producer && lane == 0)
+        for (; issued < primed; ++issued) issue(issued, issued);
+
+    pdl_wait();
+    const bool ok = gemv_prologue<PRO>(p, xs, red);
+    __syncthreads();
+
+    // Register copy of this warp's input slots: set i serves sub-range w+16i.
+    float xr[SETS][16];
+    if (!producer) {
+#pragma unroll
+        for (int i = 0; i < SETS; ++i) {
+            const uint32_t j = static_cast<uint32_t>(warp) + 16u * i;
+            if (j < csubs) {
+                const float *xc = xs + (j % slots) * kSubElems + lane * 8;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    xr[i][e] = xc[e];
+                    xr[i][8 + e] = xc[256 + e];
+                }
+            }
+        }
+    }
+
+    if (producer) {
+        if (lane == 0 && ok) {
+            uint32_t s = primed % static_cast<uint32_t>(stages);
+            uint32_t phase = primed == static_cast<uint32_t>(stages) ? 0u : 1u;  // parity to wait for
+            for (uint32_t k = primed; k < total; ++k) {
+                if (!mbar_wait(&empty_bar[s], phase)) {
+                    *reinterpret_cast<volatile int *>(&abort_flag) = 1;
+                    if (p.error) atomicExch(p.error, 2u);
+                    break;
+                }
+                issue(k, s);
+                issued = k + 1;
+                if (++s == static_cast<uint32_t>(stages)) {
+                    s = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+    } else if (ok) {
+        uint32_t s = 0, phase = 0;
+        for (uint32_t k = 0; k < total; ++k) {
+            if (!mbar_wait(&full_bar[s], phase)) {
+                *reinterpret_cast<volatile int *>(&abort_flag) = 1;
+                if (p.error && lane == 0) atomicExch(p.error, 2u);
+                break;
+            }
+            const uint32_t m = (kPair == 2 && k >= cpr) ? 1u : 0u;
+            const uint32_t sub0 = (k - m * cpr) * csubs;
+            const uint32_t left = subs_per_range - sub0;
+            const uint32_t nsub = left < csubs ? left : csubs;
+            const uint4 *stage = reinterpret_cast<const uint4 *>(ring + static_cast<size_t>(s) * chunk_bytes);
+#pragma unroll
+            for (int i = 0; i < SETS; ++i) {
+                const uint32_t j = static_cast<uint32_t>(warp) + 16u * i;
+                if (j < nsub) {
+                    const uint32_t g = sub0 + j;
+                    const uint32_t row = g / slots, slot = g - row * slots;
+                    const uint4 w0 = stage[j * 64 + lane];
+                    const uint4 w1 = stage[j * 64 + 32 + lane];
+                    const float a = dot8r(w0, xr[i], 0.0f);
+                    const float b = dot8r(w1, xr[i] + 8, 0.0f);
+                    const float sum = warp_sum(a + b);
+                    if (lane == 0) partial[(row * slots + slot) * kPair + m] = sum;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[s]);
+            if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
+            if (++s == static_cast<uint32_t>(stages)) {
+                s = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+    pdl_launch_dependents();
+    __syncthreads();
+    if (!ok || abort_flag) {
+        // Drain: every copy that was issued lands before the CTA exits
+        // (bounded waits; phases already complete return at once).
+        if (producer && lane == 0)
+            for (uint32_t k = issued > static_cast<uint32_t>(stages) ? issued - stages : 0; k < issued; ++k)
+                mbar_wait(&full_bar[k % stages], (k / stages) & 1u);
+        return;
+    }
+    gemv_epilogue<EPI>(p, partial, u0, u1, slots, red);
+}
+
+// Bulk path applies when rows split into 512-column slots and a chunk (one
+// row at most 64 slots) fits the ring.
+inline bool gemv_bulk_shape(uint64_t cols) {
+    return cols % kSubElems == 0 && cols / kSubElems <= 16ull * kMaxSets;
+}
+// Register sets a warp needs: one per 16 sub-ranges of a chunk.
+inline int gemv_bulk_sets(uint64_t cols) {
+    const uint32_t subs = bulk_chunk_subs(static_cast<uint32_t>(cols / kSubElems));
+    return subs <= 16 ? 1 : (subs <= 32 ? 2 : 4);
+}
+inline uint32_t gemv_bulk_chunk_bytes(uint64_t cols) {
+    return bulk_chunk_subs(static_cast<uint32_t>(cols / kSubElems)) * kSubElems * 2;
+}
+inline size_t gemv_bulk_smem(uint64_t cols, uint64_t rows_per_block, int pair, int stages) {
+    return static_cast<size_t>(stages) * gemv_bulk_chunk_bytes(cols) +
+           (((cols + 3) & ~3ull) + rows_per_block * (cols / kSubElems) * pair) * sizeof(float);
 }
 
 // Merge per-block argmax candidates: first maximal index, NaN -> UINT32_MAX

@@ -357,6 +357,11 @@ class Backend:
                                                          seed * 1000003 + k, mean, s):
                 raise RuntimeError(self.info().note.decode())
 
+    def release(self, hm):
+        """Drop the device copies of `hm` (its host memory may be reused)."""
+        self.lib.plamo_cuda_release_model(self.ctx, hm.ptr)
+        self.lib.plamo_cuda_release_weights(self.ctx, hm.base, hm.blob_bytes)
+
     def prepare(self, hm):
         if self.lib.plamo_cuda_prepare_model(self.ctx, hm.ptr) != 1:
             raise RuntimeError("prepare_model failed: " + self.info().note.decode())

@@ -96,8 +96,13 @@ def oracle():
     return load_oracle()
 
 
-@pytest.fixture(scope="session")
+@pytest.fixture
 def backend(pkg):
     b = pkg.Backend(device=0, max_context=4200, max_prefill=4096)
     yield b
     b.close()
+
+
+def expect(backend, rc, want=1):
+    """Assert a tri-state return code, reporting the backend's last note."""
+    assert rc == want, f"returned {rc}, expected {want}: {backend.info().note.decode()}"

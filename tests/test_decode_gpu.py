@@ -9,7 +9,7 @@ rotation bookkeeping with the reference's acceptance rule.
 import numpy as np
 import pytest
 
-from conftest import assert_close, load_oracle, load_package
+from conftest import assert_close, expect, load_oracle, load_package
 from fixtures import compare_models, decode_fixture_pair, oracle_forward, oracle_prefill
 
 pytestmark = pytest.mark.gpu
@@ -35,19 +35,26 @@ def reset(*models):
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "h%d-n%d-d%d-c%d" % s)
 def test_fixture_decode_prefill_verify(kv_backend, shape):
     h, n, dim, capacity = shape
-    lib, ctx = kv_backend.lib, kv_backend.ctx
     a, b = decode_fixture_pair(h, n, dim, capacity)
+    try:
+        run_fixture(kv_backend, a, b, h, capacity)
+    finally:
+        kv_backend.release(a)
+
+
+def run_fixture(kv_backend, a, b, h, capacity):
+    lib, ctx = kv_backend.lib, kv_backend.ctx
     # Not prepared yet: declined without touching anything.
-    assert lib.plamo_cuda_forward(ctx, a.ptr, 2) == 0
+    expect(kv_backend, lib.plamo_cuda_forward(ctx, a.ptr, 2), 0)
     ids = np.array([2, 5, 9], dtype=np.uint32)
     untouched = np.zeros((3, h), dtype=np.float32)
-    assert lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, 3, untouched.ctypes.data) == 0
+    expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, 3, untouched.ctypes.data), 0)
     compare_models(a, b)
     kv_backend.preload_model(a)
     kv_backend.prepare(a)
     # An id outside the vocabulary fails (-1) before any state changes.
     bad = np.array([2, 5, 17], dtype=np.uint32)
-    assert lib.plamo_cuda_prefill(ctx, a.ptr, bad.ctypes.data, 3, untouched.ctypes.data) == -1
+    expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, bad.ctypes.data, 3, untouched.ctypes.data), -1)
     compare_models(a, b)
     assert np.all(untouched == 0)
 
@@ -68,13 +75,13 @@ def test_fixture_decode_prefill_verify(kv_backend, shape):
                 ids = np.array([(j * 7 + 3) % 17 for j in range(count)], dtype=np.uint32)
                 actual = np.zeros((count, h), dtype=np.float32)
                 ptr = 0 if final_only else actual.ctypes.data
-                assert lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, count, ptr) == 1
+                expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, count, ptr), 1)
                 ok, expected = oracle_prefill(b, ids)
                 assert ok == 1
                 if not final_only:
                     assert_close(actual, expected[:count], "all prompt states")
                 compare_models(a, b)
-                assert lib.plamo_cuda_forward(ctx, a.ptr, 7) == 1
+                expect(kv_backend, lib.plamo_cuda_forward(ctx, a.ptr, 7), 1)
                 assert oracle_forward(b, 7) == 1
                 compare_models(a, b)
 
@@ -90,32 +97,32 @@ def test_fixture_decode_prefill_verify(kv_backend, shape):
             gold_states.append(b.state_array())
             gold_logits.append(b.logits_array())
             gold_next.append(int(load_oracle().plamo_argmax(b.model.logits, b.profile.vocab)))
-        assert lib.plamo_cuda_prefill(ctx, a.ptr, prefix.ctypes.data, 2, 0) == 1
+        expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, prefix.ctypes.data, 2, 0), 1)
         before = (a.state_array(), a.logits_array(), [c.count for c in a.caches])
         nxt = np.zeros(16, dtype=np.uint32)
-        assert lib.plamo_cuda_verify(ctx, a.ptr, cand.ctypes.data, count, nxt.ctypes.data) == 1
+        expect(kv_backend, lib.plamo_cuda_verify(ctx, a.ptr, cand.ctypes.data, count, nxt.ctypes.data), 1)
         assert np.array_equal(a.state_array(), before[0])
         assert [c.count for c in a.caches] == before[2]
         assert lib.plamo_cuda_commit(ctx, a.ptr, 1) == 0  # out of order
         for i in range(count):
             assert nxt[i] == gold_next[i]
-            assert lib.plamo_cuda_commit(ctx, a.ptr, i) == 1
+            expect(kv_backend, lib.plamo_cuda_commit(ctx, a.ptr, i), 1)
             assert_close(a.state_array(), gold_states[i], "verified state")
             assert_close(a.logits_array(), gold_logits[i], "verified logits")
         compare_models(a, b)
-        assert lib.plamo_cuda_commit(ctx, a.ptr, count) == 0
+        expect(kv_backend, lib.plamo_cuda_commit(ctx, a.ptr, count), 0)
         if count >= 4:  # rejected suffix, then ordinary decode recovers
             reset(a, b)
             assert oracle_prefill(b, prefix)[0] == 1
             for i in range(3):
                 assert oracle_forward(b, int(cand[i])) == 1
             assert oracle_forward(b, 12) == 1
-            assert lib.plamo_cuda_prefill(ctx, a.ptr, prefix.ctypes.data, 2, 0) == 1
-            assert lib.plamo_cuda_verify(ctx, a.ptr, cand.ctypes.data, count, nxt.ctypes.data) == 1
+            expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, prefix.ctypes.data, 2, 0), 1)
+            expect(kv_backend, lib.plamo_cuda_verify(ctx, a.ptr, cand.ctypes.data, count, nxt.ctypes.data), 1)
             for i in range(3):
-                assert lib.plamo_cuda_commit(ctx, a.ptr, i) == 1
-            assert lib.plamo_cuda_forward(ctx, a.ptr, 12) == 1
-            assert lib.plamo_cuda_commit(ctx, a.ptr, 3) == 0
+                expect(kv_backend, lib.plamo_cuda_commit(ctx, a.ptr, i), 1)
+            expect(kv_backend, lib.plamo_cuda_forward(ctx, a.ptr, 12), 1)
+            expect(kv_backend, lib.plamo_cuda_commit(ctx, a.ptr, 3), 0)
             compare_models(a, b)
 
     # --- decode steps (reference tests/metal_decode.c:450-495) -------------
@@ -125,7 +132,7 @@ def test_fixture_decode_prefill_verify(kv_backend, shape):
             # A prompt in the middle of decoding, then a fresh request.
             ids = np.array([2, 5, 9], dtype=np.uint32)
             got = np.zeros((3, h), dtype=np.float32)
-            assert lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, 3, got.ctypes.data) == 1
+            expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, 3, got.ctypes.data), 1)
             ok, want = oracle_prefill(b, ids)
             assert ok == 1
             assert_close(got, want[:3], "prefill")
@@ -140,7 +147,7 @@ def test_fixture_decode_prefill_verify(kv_backend, shape):
                     m.rotation(i).processed_count = 0
         token = (step * 7 + 2) % 17
         assert oracle_forward(b, token) == 1
-        assert lib.plamo_cuda_forward(ctx, a.ptr, token) == 1
+        expect(kv_backend, lib.plamo_cuda_forward(ctx, a.ptr, token), 1)
         compare_models(a, b)
     count = a.caches[1].count
     assert lib.plamo_cuda_forward(ctx, a.ptr, 17) == 0 and a.caches[1].count == count
