@@ -281,6 +281,245 @@ inline size_t decode_attention_smem(uint32_t G, uint32_t D) {
                             + 3 * G);                                      // m, l, corr
 }
 
+// Head dim 128: every load of a tile is an asynchronous 16-byte copy issued
+// before any compute (raw keys into the padded key tile, values, and the
+// tile's cos/sin rows, which are consecutive table rows), the Q/K head norms
+// run while they are in flight, and keys are then rotated in place.
+constexpr uint32_t kD128Stride = 132;
+inline size_t decode_attention128_smem(uint32_t G) {
+    return sizeof(float) * (static_cast<size_t>(G) * 128  // qs
+                            + kDecTile * kD128Stride      // kt (raw, then rotated in place)
+                            + kDecTile * 128              // tab (cos | sin rows)
+                            + kDecTile * 128              // vt
+                            + G * kDecTile                // sc
+                            + G * 128                     // acc
+                            + 2 * 128                     // knew, vnew
+                            + 3 * G);
+}
+
+__global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)
+    decode_attention128_kernel(DecodeAttnParams p) {
+    constexpr uint32_t D = 128, H = 64, KS = kD128Stride;
+    extern __shared__ __align__(16) float sm[];
+    const uint32_t G = p.qh / p.kh;
+    const uint32_t kh = blockIdx.x, split = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = kDecThreads / 32;
+    float *qs = sm;
+    float *kt = qs + G * D;
+    float *tab = kt + kDecTile * KS;
+    float *vt = tab + kDecTile * D;
+    float *sc = vt + kDecTile * D;
+    float *acc = sc + G * kDecTile;
+    float *knew = acc + G * D;
+    float *vnew = knew + D;
+    float *mrow = vnew + D;
+    float *lrow = mrow + G;
+    float *corr = lrow + G;
+    cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+
+    pdl_launch_dependents();  // the next projection may start streaming its weights
+    pdl_wait();
+    const uint64_t P = *p.L.appended;
+    const uint64_t lo = window_start(p.L, P, 0);
+    const uint32_t n = static_cast<uint32_t>(P + 1 - lo);
+    const uint64_t k0 = lo + static_cast<uint64_t>(n) * split / kDecSplits;
+    const uint64_t k1 = lo + static_cast<uint64_t>(n) * (split + 1) / kDecSplits;
+    const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
+
+    // Asynchronous staging of one tile: 32 16-byte pieces per 512-byte row.
+    auto stage = [&](uint64_t base, uint32_t rows) {
+        for (uint32_t i = threadIdx.x; i < rows * 32; i += kDecThreads) {
+            const uint32_t r = i >> 5, c = (i & 31) * 4;
+            const uint64_t key = base + r;
+            cp_async16(tab + r * D + c, p.L.table + (key - lo) * D + c);
+            if (key < P) {
+                const uint64_t slot = key % p.L.ring;
+                cp_async16(kt + r * KS + c, p.L.ring_k + slot * kvw + kh * D + c);
+                cp_async16(vt + r * D + c, p.L.ring_v + slot * kvw + kh * D + c);
+            }
+        }
+        cp_async_commit();
+    };
+    if (k0 < k1) stage(k0, static_cast<uint32_t>(k1 - k0 < kDecTile ? k1 - k0 : kDecTile));
+
+    // Q heads of the group (one warp each): lane l < 16 owns coordinate pairs
+    // 4l..4l+3 / 64+4l..64+4l+3; RMSNorm(+1), rotate at the query position.
+    const float *table_q = p.L.table + static_cast<uint64_t>(n - 1) * D;
+    for (uint32_t g = warp; g < G; g += warps) {
+        const float *x = p.qkv + static_cast<uint64_t>(kh * G + g) * D;
+        float4 a = make_float4(0, 0, 0, 0), b = a, c = a, sn = a;
+        uint2 wa = make_uint2(0, 0), wb = wa;
+        if (lane < 16) {
+            a = ld4(x + 4 * lane);
+            b = ld4(x + H + 4 * lane);
+            wa = *reinterpret_cast<const uint2 *>(p.L.qn + 4 * lane);
+            wb = *reinterpret_cast<const uint2 *>(p.L.qn + H + 4 * lane);
+            c = ld4(table_q + 4 * lane);
+            sn = ld4(table_q + H + 4 * lane);
+        }
+        const float inv = rms_inverse(warp_sum(sq4(a) + sq4(b)), D);
+        if (lane < 16) {
+            const float4 qa = apply4(a, inv, norm4(wa, 1.0f)), qb = apply4(b, inv, norm4(wb, 1.0f));
+            float4 lo4, hi4;
+            lo4.x = __fsub_rn(__fmul_rn(qa.x, c.x), __fmul_rn(qb.x, sn.x));
+            lo4.y = __fsub_rn(__fmul_rn(qa.y, c.y), __fmul_rn(qb.y, sn.y));
+            lo4.z = __fsub_rn(__fmul_rn(qa.z, c.z), __fmul_rn(qb.z, sn.z));
+            lo4.w = __fsub_rn(__fmul_rn(qa.w, c.w), __fmul_rn(qb.w, sn.w));
+            hi4.x = __fadd_rn(__fmul_rn(qb.x, c.x), __fmul_rn(qa.x, sn.x));
+            hi4.y = __fadd_rn(__fmul_rn(qb.y, c.y), __fmul_rn(qa.y, sn.y));
+            hi4.z = __fadd_rn(__fmul_rn(qb.z, c.z), __fmul_rn(qa.z, sn.z));
+            hi4.w = __fadd_rn(__fmul_rn(qb.w, c.w), __fmul_rn(qa.w, sn.w));
+            *reinterpret_cast<float4 *>(qs + g * D + 4 * lane) = lo4;
+            *reinterpret_cast<float4 *>(qs + g * D + H + 4 * lane) = hi4;
+        }
+    }
+    // The new row: normalised K (unrotated) and V, stored to the ring by the
+    // CTA whose split contains it.
+    const bool has_new = k1 == P + 1;
+    if (has_new && warp == warps - 1) {
+        const float *x = p.qkv + static_cast<uint64_t>(p.qh + kh) * D;
+        const float *v = p.qkv + static_cast<uint64_t>(p.qh + p.kh + kh) * D;
+        const float4 xk = ld4(x + 4 * lane), xv = ld4(v + 4 * lane);
+        const uint2 wk = *reinterpret_cast<const uint2 *>(p.L.kn + 4 * lane);
+        const float inv = rms_inverse(warp_sum(sq4(xk)), D);
+        const float4 k4 = apply4(xk, inv, norm4(wk, 1.0f));
+        const uint64_t slot = P % p.L.ring;
+        *reinterpret_cast<float4 *>(knew + 4 * lane) = k4;
+        *reinterpret_cast<float4 *>(vnew + 4 * lane) = xv;
+        *reinterpret_cast<float4 *>(p.L.ring_k_w + slot * kvw + kh * D + 4 * lane) = k4;
+        *reinterpret_cast<float4 *>(p.L.ring_v_w + slot * kvw + kh * D + 4 * lane) = xv;
+    }
+    for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) acc[i] = 0.0f;
+    for (uint32_t g = threadIdx.x; g < G; g += kDecThreads) {
+        mrow[g] = -__int_as_float(0x7f800000);
+        lrow[g] = 0.0f;
+    }
+
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(D)));
+    for (uint64_t base = k0; base < k1; base += kDecTile) {
+        const uint32_t rows = static_cast<uint32_t>(k1 - base < kDecTile ? k1 - base : kDecTile);
+        cp_async_wait_all();
+        __syncthreads();
+        // The new row is not in the ring yet: take it from shared memory.
+        if (base + rows == P + 1) {
+            const uint32_t r = rows - 1;
+            for (uint32_t i = threadIdx.x; i < D; i += kDecThreads) {
+                kt[r * KS + i] = knew[i];
+                vt[r * D + i] = vnew[i];
+            }
+            __syncthreads();
+        }
+        // Rotate keys in place at their local positions (tab rows).
+        for (uint32_t i = threadIdx.x; i < rows * 16; i += kDecThreads) {
+            const uint32_t r = i >> 4, d = (i & 15) * 4;
+            const float4 a = ld4(kt + r * KS + d), b = ld4(kt + r * KS + H + d);
+            const float4 c = ld4(tab + r * D + d), sn = ld4(tab + r * D + H + d);
+            float4 lo4, hi4;
+            lo4.x = __fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(b.x, sn.x));
+            lo4.y = __fsub_rn(__fmul_rn(a.y, c.y), __fmul_rn(b.y, sn.y));
+            lo4.z = __fsub_rn(__fmul_rn(a.z, c.z), __fmul_rn(b.z, sn.z));
+            lo4.w = __fsub_rn(__fmul_rn(a.w, c.w), __fmul_rn(b.w, sn.w));
+            hi4.x = __fadd_rn(__fmul_rn(b.x, c.x), __fmul_rn(a.x, sn.x));
+            hi4.y = __fadd_rn(__fmul_rn(b.y, c.y), __fmul_rn(a.y, sn.y));
+            hi4.z = __fadd_rn(__fmul_rn(b.z, c.z), __fmul_rn(a.z, sn.z));
+            hi4.w = __fadd_rn(__fmul_rn(b.w, c.w), __fmul_rn(a.w, sn.w));
+            *reinterpret_cast<float4 *>(kt + r * KS + d) = lo4;
+            *reinterpret_cast<float4 *>(kt + r * KS + H + d) = hi4;
+        }
+        __syncthreads();
+        // Scores: one (head, key) per thread, sequential FMA over dim.
+        for (uint32_t i = threadIdx.x; i < G * rows; i += kDecThreads) {
+            const uint32_t g = i / rows, r = i - g * rows;
+            const float *qv = qs + g * D, *kv = kt + r * KS;
+            float a = 0.0f;
+#pragma unroll
+            for (uint32_t d = 0; d < D; d += 4) {
+                const float4 q4 = ld4(qv + d), k4 = ld4(kv + d);
+                a = fmaf(q4.x, k4.x, a);
+                a = fmaf(q4.y, k4.y, a);
+                a = fmaf(q4.z, k4.z, a);
+                a = fmaf(q4.w, k4.w, a);
+            }
+            sc[g * kDecTile + r] = __fmul_rn(a, scale);
+        }
+        __syncthreads();
+        for (uint32_t g = warp; g < G; g += warps) {
+            const float ninf = -__int_as_float(0x7f800000);
+            const float v0 = lane < static_cast<int>(rows) ? sc[g * kDecTile + lane] : ninf;
+            const float v1 = lane + 32 < static_cast<int>(rows) ? sc[g * kDecTile + lane + 32] : ninf;
+            const float m = fmaxf(mrow[g], warp_max(fmaxf(v0, v1)));
+            const float e0 = lane < static_cast<int>(rows) ? plamo_exp(__fsub_rn(v0, m)) : 0.0f;
+            const float e1 = lane + 32 < static_cast<int>(rows) ? plamo_exp(__fsub_rn(v1, m)) : 0.0f;
+            if (lane < static_cast<int>(rows)) sc[g * kDecTile + lane] = e0;
+            if (lane + 32 < static_cast<int>(rows)) sc[g * kDecTile + lane + 32] = e1;
+            const float tile_sum = warp_sum(__fadd_rn(e0, e1));
+            if (lane == 0) {
+                const float cr = plamo_exp(__fsub_rn(mrow[g], m));
+                lrow[g] = __fadd_rn(__fmul_rn(lrow[g], cr), tile_sum);
+                mrow[g] = m;
+                corr[g] = cr;
+            }
+        }
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < G * 32; i += kDecThreads) {
+            const uint32_t g = i >> 5, d = (i & 31) * 4;
+            float4 a = ld4(acc + g * D + d);
+            const float cr = corr[g];
+            a = make_float4(__fmul_rn(a.x, cr), __fmul_rn(a.y, cr), __fmul_rn(a.z, cr), __fmul_rn(a.w, cr));
+            const float *sg = sc + g * kDecTile;
+#pragma unroll 8
+            for (uint32_t r = 0; r < rows; ++r) {
+                const float pr = sg[r];
+                const float4 v4 = ld4(vt + r * D + d);
+                a.x = fmaf(pr, v4.x, a.x);
+                a.y = fmaf(pr, v4.y, a.y);
+                a.z = fmaf(pr, v4.z, a.z);
+                a.w = fmaf(pr, v4.w, a.w);
+            }
+            *reinterpret_cast<float4 *>(acc + g * D + d) = a;
+        }
+        __syncthreads();
+        const uint64_t next = base + kDecTile;
+        if (next < k1) stage(next, static_cast<uint32_t>(k1 - next < kDecTile ? k1 - next : kDecTile));
+    }
+    __syncthreads();
+
+    cluster.sync();
+    if (cluster.block_rank() == 0) {
+        float *w = kt;  // [G][splits] weights, then [G] denominators
+        if (threadIdx.x < G) {
+            const uint32_t g = threadIdx.x;
+            float ms[kDecSplits];
+            float M = -__int_as_float(0x7f800000);
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) {
+                ms[r] = cluster.map_shared_rank(mrow, r)[g];
+                M = fmaxf(M, ms[r]);
+            }
+            float Ls = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) {
+                const float e = plamo_exp(__fsub_rn(ms[r], M));
+                w[g * kDecSplits + r] = e;
+                Ls = fmaf(cluster.map_shared_rank(lrow, r)[g], e, Ls);
+            }
+            w[G * kDecSplits + g] = Ls;
+        }
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) {
+            const uint32_t g = i / D;
+            float parts[kDecSplits];
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) parts[r] = cluster.map_shared_rank(acc, r)[i];
+            float A = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kDecSplits; ++r) A = fmaf(parts[r], w[g * kDecSplits + r], A);
+            p.out[static_cast<uint64_t>(kh * G) * D + i] = __fdiv_rn(A, w[G * kDecSplits + g]);
+        }
+    }
+    cluster.sync();
+}
+
 // DT: compile-time head dim (128) for the vectorised path, 0 for any even dim.
 template <int DT>
 __global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)

@@ -485,7 +485,9 @@ bool launch_decode_attention(plamo_cuda *c, DModel *m, uint64_t l) {
                         static_cast<uint32_t>(m->D), m->qkv, m->attn};
     const size_t smem = decode_attention_smem(static_cast<uint32_t>(m->QH / m->KH), static_cast<uint32_t>(m->D));
     const dim3 grid(static_cast<uint32_t>(m->KH), kDecSplits), block(kDecThreads);
-    if (m->D == 128) return launch(c, decode_attention_kernel<128>, grid, block, smem, dp);
+    if (m->D == 128 && m->QH / m->KH <= 32)
+        return launch(c, decode_attention128_kernel, grid, block,
+                      decode_attention128_smem(static_cast<uint32_t>(m->QH / m->KH)), dp);
     return launch(c, decode_attention_kernel<0>, grid, block, smem, dp);
 }
 
@@ -779,6 +781,7 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>(optin);
     set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin);
     allow_smem(attention_kernel, optin);
+    allow_smem(decode_attention128_kernel, optin);
     allow_smem(decode_attention_kernel<128>, optin);
     allow_smem(decode_attention_kernel<0>, optin);
     if ((e = cudaGetLastError()) != cudaSuccess) {

@@ -86,6 +86,16 @@ __device__ __forceinline__ float rms_apply(float x, float inverse, uint16_t w, f
     return __fmul_rn(__fmul_rn(x, inverse), __fadd_rn(bf16_to_f32(w), offset));
 }
 
+__device__ __forceinline__ float4 norm4(uint2 w, float offset) {
+    return make_float4(__fadd_rn(bf16_lo(w.x), offset), __fadd_rn(bf16_hi(w.x), offset),
+                       __fadd_rn(bf16_lo(w.y), offset), __fadd_rn(bf16_hi(w.y), offset));
+}
+__device__ __forceinline__ float sq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+__device__ __forceinline__ float4 apply4(float4 x, float inv, float4 w) {
+    return make_float4(__fmul_rn(__fmul_rn(x.x, inv), w.x), __fmul_rn(__fmul_rn(x.y, inv), w.y),
+                       __fmul_rn(__fmul_rn(x.z, inv), w.z), __fmul_rn(__fmul_rn(x.w, inv), w.w));
+}
+
 // Streaming 128-bit load of weights that are read once per token: bypass L1
 // and mark the L2 line evict-first so activations and KV stay resident.
 __device__ __forceinline__ uint64_t evict_first_policy() {
@@ -163,5 +173,12 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+
+// 16-byte asynchronous global -> shared copy (LDGSTS), no registers involved.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 }  // namespace plamo

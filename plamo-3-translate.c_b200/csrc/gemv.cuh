@@ -89,16 +89,6 @@ __device__ __forceinline__ float dot8r(uint4 w, const float *x, float acc) {
 // registers, one L2 round trip per input instead of one per loop trip.
 constexpr int kPV = 4;
 
-__device__ __forceinline__ float4 norm4(uint2 w, float offset) {
-    return make_float4(__fadd_rn(bf16_lo(w.x), offset), __fadd_rn(bf16_hi(w.x), offset),
-                       __fadd_rn(bf16_lo(w.y), offset), __fadd_rn(bf16_hi(w.y), offset));
-}
-__device__ __forceinline__ float sq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
-__device__ __forceinline__ float4 apply4(float4 x, float inv, float4 w) {
-    return make_float4(__fmul_rn(__fmul_rn(x.x, inv), w.x), __fmul_rn(__fmul_rn(x.y, inv), w.y),
-                       __fmul_rn(__fmul_rn(x.z, inv), w.z), __fmul_rn(__fmul_rn(x.w, inv), w.w));
-}
-
 template <int PRO>
 __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, float *red) {
     const uint64_t n = p.cols;
@@ -312,6 +302,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
         return p.w + row * cols + static_cast<uint64_t>(jj - q * segs32) * seg_cols;
     };
 
+    pdl_launch_dependents();
     constexpr int kLoads = (U ? U : 1) * kPair;
     uint4 cur[kLoads];
     uint64_t j = warp;
@@ -370,7 +361,6 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
             }
         }
     }
-    pdl_launch_dependents();
     __syncthreads();
     gemv_epilogue<EPI>(p, partial, u0, u1, segs, red);
 }
@@ -441,6 +431,10 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
         fence_barrier_init();
     }
     __syncthreads();
+    // Let the next kernel's CTAs take SMs as soon as this grid's CTAs retire:
+    // they stream their first weight stages while this grid finishes, and
+    // their griddepcontrol.wait still orders every read of our results.
+    pdl_launch_dependents();
 
     auto issue = [&](uint32_t k, uint32_t s) {
         const uint32_t m = (kPair == 2 && k >= cpr) ? 1u : 0u;
@@ -531,7 +525,6 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
             }
         }
     }
-    pdl_launch_dependents();
     __syncthreads();
     if (!ok || abort_flag) {
         // Drain: every copy that was issued lands before the CTA exits
