@@ -81,6 +81,21 @@ int plamo_cuda_verify(struct plamo_cuda *, struct model *, const uint32_t *ids,
 int plamo_cuda_commit(struct plamo_cuda *, struct model *, uint64_t index);
 /* reference runtime/metal.h:85: synchronous dense projection of host buffers. */
 int plamo_cuda_linear(struct plamo_cuda *, const struct plamo_matmul *);
+/* Size of the static device staging used by plamo_cuda_linear_static, in
+   FP32 elements (16 MiB): tokens * (columns + rows) must not exceed it. */
+#define PLAMO_CUDA_LINEAR_STATIC_FLOATS (4ull << 20)
+/* No counterpart in the reference. Same projection as plamo_cuda_linear, for
+   callers that cannot allocate device memory: it stages the host input and
+   output rows in one fixed array compiled into this library (every GPU that
+   loads it holds 16 MiB until the process exits) and calls no cudaMalloc,
+   cudaFree or allocating library routine. Weights must already be preloaded
+   (0 otherwise). A request needing more than PLAMO_CUDA_LINEAR_STATIC_FLOATS
+   staging floats is declined (0) with the reason in plamo_cuda_info.note.
+   The first call on a device looks up the array's device address; make that
+   first call before any stream capture. All calls share the array, so calls
+   that overlap on the GPU (several host threads, several contexts on one
+   device) race; serialise them. */
+int plamo_cuda_linear_static(struct plamo_cuda *, const struct plamo_matmul *);
 /* reference runtime/metal.h:88: complete MLP branch (norm, gate_up, SwiGLU, down,
    norm, residual) applied in place to states[tokens x hidden]. */
 int plamo_cuda_mlp(struct plamo_cuda *, const struct mlp *, float *states, uint64_t tokens);

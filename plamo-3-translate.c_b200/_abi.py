@@ -13,6 +13,7 @@ from ctypes import POINTER, c_char, c_char_p, c_double, c_int, c_int64, c_uint, 
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libplamo_cuda.so")
+LINEAR_STATIC_FLOATS = 4 << 20  # PLAMO_CUDA_LINEAR_STATIC_FLOATS
 
 
 class Qkv(ctypes.Structure):
@@ -110,6 +111,7 @@ SIGNATURES = {
     "plamo_cuda_verify": (c_int, [P, M, P, c_uint64, P]),
     "plamo_cuda_commit": (c_int, [P, M, c_uint64]),
     "plamo_cuda_linear": (c_int, [P, POINTER(Matmul)]),
+    "plamo_cuda_linear_static": (c_int, [P, POINTER(Matmul)]),
     "plamo_cuda_mlp": (c_int, [P, POINTER(Mlp), P, c_uint64]),
     "plamo_cuda_sync_host": (c_int, [P, M]),
     "plamo_cuda_invalidate": (c_int, [P, M]),

@@ -29,6 +29,12 @@ constexpr float kPostMixerOffset = 0.2f;                 // reference src/layer.
 constexpr float kPostMlpOffset = 0.08944271909999159f;   // reference src/model.s:112
 constexpr uint64_t kVerifyMax = PLAMO_CUDA_VERIFY_MAX;
 
+// Device staging of plamo_cuda_linear_static: a fixed array in the module
+// instead of cudaMalloc'd buffers. Every GPU that loads this library holds it
+// (16 MiB) until the process exits; the input rows are staged at its start,
+// the output rows right after them.
+constexpr uint64_t kStaticLinearFloats = PLAMO_CUDA_LINEAR_STATIC_FLOATS;
+
 struct Range {
     uintptr_t host;
     uint64_t bytes;
@@ -86,6 +92,10 @@ struct DModel {
 
 }  // namespace
 
+// File scope: the device array itself. Host code only ever uses the address
+// returned by cudaGetSymbolAddress (the name is a host-side stand-in).
+static __device__ __align__(256) float g_linear_static_scratch[kStaticLinearFloats];
+
 struct plamo_cuda {
     int device;
     cudaStream_t stream;
@@ -104,6 +114,7 @@ struct plamo_cuda {
     int gemv_ring_kb;
     int gemv_ctas;
     uint32_t *sink;
+    float *static_scratch;  // device address of g_linear_static_scratch (set on first use)
 };
 
 namespace {
@@ -1354,6 +1365,42 @@ int plamo_cuda_linear(struct plamo_cuda *c, const struct plamo_matmul *mm) {
          note(c, "linear", cudaStreamSynchronize(c->stream));
     cudaFree(x);
     cudaFree(y);
+    return ok ? 1 : -1;
+}
+
+int plamo_cuda_linear_static(struct plamo_cuda *c, const struct plamo_matmul *mm) {
+    if (!c || !mm) return 0;
+    if (!mm->rows || !mm->tokens) return 1;
+    cudaSetDevice(c->device);
+    const uint64_t T = mm->tokens, K = mm->columns, R = mm->rows;
+    if (T * K + T * R > kStaticLinearFloats || T * K / T != K || T * R / T != R) {
+        c->info.declines++;
+        snprintf(c->info.note, sizeof c->info.note,
+                 "linear_static: %llu input + %llu output floats exceed the static staging of %llu floats",
+                 static_cast<unsigned long long>(T * K), static_cast<unsigned long long>(T * R),
+                 static_cast<unsigned long long>(kStaticLinearFloats));
+        return 0;
+    }
+    const uint16_t *w = resolve(c, mm->weights, R * K * 2, false);
+    if (!w) {
+        c->info.declines++;
+        snprintf(c->info.note, sizeof c->info.note, "linear_static: weights are not preloaded");
+        return 0;
+    }
+    // One-time set-up on this context's device (the first call, with the
+    // device current): the device address of the static array.
+    if (!c->static_scratch &&
+        !note(c, "linear_static symbol",
+              cudaGetSymbolAddress(reinterpret_cast<void **>(&c->static_scratch), g_linear_static_scratch)))
+        return -1;
+    float *x = c->static_scratch, *y = c->static_scratch + T * K;
+    bool ok = !K || note(c, "linear_static in", cudaMemcpy2DAsync(x, K * 4, mm->input, mm->input_stride * 4, K * 4,
+                                                                 T, cudaMemcpyHostToDevice, c->stream));
+    if (ok && !K) ok = note(c, "linear_static zero", cudaMemsetAsync(y, 0, T * R * 4, c->stream));
+    else if (ok) ok = gemm(c, x, K, w, y, R, T, R, K);
+    ok = ok && note(c, "linear_static out", cudaMemcpy2DAsync(mm->output, mm->output_stride * 4, y, R * 4, R * 4, T,
+                                                              cudaMemcpyDeviceToHost, c->stream)) &&
+         note(c, "linear_static", cudaStreamSynchronize(c->stream));
     return ok ? 1 : -1;
 }
 
