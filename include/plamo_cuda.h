@@ -153,6 +153,13 @@ void plamo_cuda_reset_request(struct plamo_cuda *, struct model *);
 int plamo_cuda_gemv_device(struct plamo_cuda *, const uint16_t *w, const float *x, float *y,
                            uint64_t rows, uint64_t cols);
 
+/* Prompt projection on device buffers: y[t][r] (row stride ys) =
+   sum_k W[r][k] x[t][k] (x row stride xs, FP32). Tensor cores (tcgen05, x split
+   into three BF16 terms, FP32 accumulation) when rows are 16-byte aligned and
+   cols % 8 == 0, the FP32 CUDA-core kernel otherwise. Synchronous. */
+int plamo_cuda_gemm_device(struct plamo_cuda *, const float *x, uint64_t xs, const uint16_t *w, float *y,
+                           uint64_t ys, uint64_t tokens, uint64_t rows, uint64_t cols);
+
 /* ---- device memory and timing helpers for tests and benchmarks ---- */
 void *plamo_cuda_device_alloc(struct plamo_cuda *, uint64_t bytes);
 void plamo_cuda_device_free(struct plamo_cuda *, void *);
@@ -165,6 +172,9 @@ int plamo_cuda_synchronize(struct plamo_cuda *);
 double plamo_cuda_time_decode(struct plamo_cuda *, struct model *, uint64_t repeats);
 /* Same for the standalone GEMV over `repeats` launches. */
 double plamo_cuda_time_gemv(struct plamo_cuda *, const uint16_t *w, const float *x, float *y,
+                            uint64_t rows, uint64_t cols, uint64_t repeats);
+/* Same for `repeats` back-to-back prompt projections (split + GEMM). */
+double plamo_cuda_time_gemm(struct plamo_cuda *, const float *x, const uint16_t *w, float *y, uint64_t tokens,
                             uint64_t rows, uint64_t cols, uint64_t repeats);
 /* Kernels launched by the library since open (counts every launch and every
    kernel node of a launched graph). */

@@ -125,6 +125,8 @@ SIGNATURES = {
     "plamo_cuda_reset_request": (None, [P, M]),
     "plamo_cuda_read_weights": (c_int, [P, P, P, c_uint64]),
     "plamo_cuda_gemv_device": (c_int, [P, P, P, P, c_uint64, c_uint64]),
+    "plamo_cuda_gemm_device": (c_int, [P, P, c_uint64, P, P, c_uint64, c_uint64, c_uint64, c_uint64]),
+    "plamo_cuda_time_gemm": (c_double, [P, P, P, P, c_uint64, c_uint64, c_uint64, c_uint64]),
     "plamo_cuda_device_alloc": (c_void_p, [P, c_uint64]),
     "plamo_cuda_device_free": (None, [P, P]),
     "plamo_cuda_copy_to_device": (c_int, [P, P, P, c_uint64]),

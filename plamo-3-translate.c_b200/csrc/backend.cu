@@ -9,6 +9,9 @@
 #include "gemv.cuh"
 #include "attention.cuh"
 #include "rows.cuh"
+#include "gemm_tc.cuh"
+
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <chrono>
@@ -79,6 +82,7 @@ struct DModel {
     uint64_t tmax;
     float *p_states, *p_norm, *p_qkv, *p_q, *p_attn, *p_branch, *p_gu, *p_logits, *p_part;
     uint32_t *p_ids, *p_next, *p_tickets;
+    uint16_t *p_split;  // BF16 hi/mid/lo terms of a projection input, 3 x [T][K]
     float *v_kv;  // [L][kVerifyMax][2][KVW]
     uint64_t verify_count = 0, verify_committed = 0;
     bool verify_valid = false;
@@ -112,6 +116,7 @@ struct plamo_cuda {
     bool pdl;
     bool bulk_gemv;
     int gemv_ring_kb;
+    bool tc_gemm;
     int gemv_ctas;
     uint32_t *sink;
     float *static_scratch;  // device address of g_linear_static_scratch (set on first use)
@@ -335,6 +340,77 @@ bool gemm(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t *W, float *
     if (!T || !R) return true;
     dim3 grid((R + kGemmBN - 1) / kGemmBN, (T + kGemmBM - 1) / kGemmBM);
     return launch(c, gemm_simt_kernel, grid, dim3(256), 0, X, xs, W, Y, ys, T, R, K);
+}
+
+// ---- tcgen05 projections ---------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+
+bool tensor_maps_available() {
+    if (g_encode_tiled) return true;
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+        return false;
+    g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return true;
+}
+
+// 2-D BF16 row-major [rows][cols] map with a {64 x box_rows} box, 128-byte swizzle.
+bool bf16_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), box_rows};
+    cuuint32_t elem[2] = {1, 1};
+    return g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, elem,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int N>
+bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &mm,
+               const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T) {
+    int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, (c->smem_optin - 2048) / tc_stage_bytes(N)));
+    const dim3 grid((R + kTcM - 1) / kTcM, (T + N - 1) / N);
+    return launch(c, gemm_tc_kernel<N>, grid, dim3(kTcThreads), tc_smem_bytes(N, stages), mw, mh, mm, ml, p,
+                  stages);
+}
+
+// Y[T][R] (row stride ys) = X[T][K] (row stride xs, FP32) . W[R][K]^T on the
+// tensor cores when the shapes allow TMA (16-byte aligned rows), else on the
+// FP32 CUDA-core kernel otherwise. split: BF16 scratch of 3*T*K elements
+// (the hi, mid and lo terms).
+bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys, uint64_t T,
+                     uint64_t R, uint64_t K, uint16_t *split, uint32_t *error) {
+    if (!T || !R) return true;
+    const bool tc = c->tc_gemm && split && K % 8 == 0 && K >= kTcK && reinterpret_cast<uintptr_t>(W) % 16 == 0 &&
+                    T < (1ull << 31) && R < (1ull << 31) && tensor_maps_available();
+    if (!tc) return gemm(c, X, xs, W, Y, ys, T, R, K);
+    uint16_t *hi = split, *mid = split + T * K, *lo = split + 2 * T * K;
+    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((T * K + 255) / 256, 8192));
+    if (!launch(c, split_hilo_kernel, dim3(blocks), dim3(256), 0, X, xs, static_cast<uint32_t>(T),
+                static_cast<uint32_t>(K), hi, mid, lo))
+        return false;
+    const uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    CUtensorMap mw, mh, mm, ml;
+    if (!bf16_map(&mw, W, R, K, kTcM) || !bf16_map(&mh, hi, T, K, N) || !bf16_map(&mm, mid, T, K, N) ||
+        !bf16_map(&ml, lo, T, K, N)) {
+        snprintf(c->info.note, sizeof c->info.note, "tensor map encode failed");
+        return gemm(c, X, xs, W, Y, ys, T, R, K);
+    }
+    TcGemmParams p{Y, ys, static_cast<uint32_t>(T), static_cast<uint32_t>(R), static_cast<uint32_t>(K), error};
+    const uint32_t r32 = static_cast<uint32_t>(R), t32 = static_cast<uint32_t>(T);
+    switch (N) {
+    case 16: return launch_tc<16>(c, mw, mh, mm, ml, p, r32, t32);
+    case 32: return launch_tc<32>(c, mw, mh, mm, ml, p, r32, t32);
+    case 64: return launch_tc<64>(c, mw, mh, mm, ml, p, r32, t32);
+    default: return launch_tc<128>(c, mw, mh, mm, ml, p, r32, t32);
+    }
+}
+
+bool projection(plamo_cuda *c, DModel *m, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys,
+                uint64_t T, uint64_t R, uint64_t K) {
+    return projection_with(c, X, xs, W, Y, ys, T, R, K, T <= m->tmax ? m->p_split : nullptr, m->d_error);
 }
 
 AttnLayer attn_layer(const DModel *m, uint64_t l) {
@@ -646,7 +722,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
             ok = launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(256), 0, m->p_states,
                         static_cast<const float *>(m->p_branch), m->layers[l - 1].mpost, kPostMlpOffset, L.pre,
                         1.0f, m->p_norm, H);
-        if (!ok || !gemm(c, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H)) return false;
+        if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H)) return false;
         AttnLayer al = attn_layer(m, l);
         if (!launch(c, qk_prep_kernel, dim3(m->QH + m->KH, T), dim3(128), 0, m->p_qkv, m->p_q, al, shape))
             return false;
@@ -667,15 +743,15 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
                                                         c->stream)))
                 return false;
         }
-        if (!gemm(c, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
+        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
         if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(256), 0, m->p_states,
                     static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H))
             return false;
-        if (!gemm(c, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H)) return false;
+        if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H)) return false;
         if (!launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((m->I * T + 255) / 256, 4096)), dim3(256), 0,
                     m->p_gu, m->I, T))
             return false;
-        if (!gemm(c, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
+        if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
     }
     if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(256), 0, m->p_states,
                 static_cast<const float *>(m->p_branch), m->layers[m->L - 1].mpost, kPostMlpOffset,
@@ -686,7 +762,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
                     static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, m->norm,
                     1.0f, m->p_norm, H))
             return false;
-        return gemm(c, m->p_norm, H, m->head, m->p_logits, m->V, T, m->V, H);
+        return projection(c, m, m->p_norm, H, m->head, m->p_logits, m->V, T, m->V, H);
     }
     // Final norm and head for the last prompt token only (reference
     // src/prefill.s:136-158), with the greedy choice on the device.
@@ -768,6 +844,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->pdl = !pdl || strcmp(pdl, "0");
     const char *bulk = getenv("PLAMO_CUDA_BULK_GEMV");
     c->bulk_gemv = !bulk || strcmp(bulk, "0");
+    const char *tc = getenv("PLAMO_CUDA_TC_GEMM");
+    c->tc_gemm = !tc || strcmp(tc, "0");
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
     c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
@@ -793,6 +871,10 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin);
     allow_smem(attention_kernel, optin);
     allow_smem(decode_attention128_kernel, optin);
+    allow_smem(gemm_tc_kernel<16>, optin);
+    allow_smem(gemm_tc_kernel<32>, optin);
+    allow_smem(gemm_tc_kernel<64>, optin);
+    allow_smem(gemm_tc_kernel<128>, optin);
     allow_smem(decode_attention_kernel<128>, optin);
     allow_smem(decode_attention_kernel<0>, optin);
     if ((e = cudaGetLastError()) != cudaSuccess) {
@@ -1001,6 +1083,8 @@ int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     m->p_ids = static_cast<uint32_t *>(dalloc(c, m.get(), T * 4));
     m->p_next = static_cast<uint32_t *>(dalloc(c, m.get(), kVerifyMax * 4));
     m->v_kv = static_cast<float *>(dalloc(c, m.get(), m->L * kVerifyMax * 2 * m->KVW * 4));
+    const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(H, m->AW), m->I);
+    m->p_split = static_cast<uint16_t *>(dalloc(c, m.get(), 3 * T * kmax * 2));
     for (void *p : m->allocations)
         if (!p) return 0;
     c->info.workspace_bytes += c->info.allocated_bytes - before;
@@ -1483,6 +1567,39 @@ int64_t plamo_cuda_generate(struct plamo_cuda *c, struct model *model, const uin
     t->decode_seconds = now() - decode_start;
     t->completion_tokens = static_cast<uint64_t>(emitted);
     return emitted;
+}
+
+int plamo_cuda_gemm_device(struct plamo_cuda *c, const float *x, uint64_t xs, const uint16_t *w, float *y,
+                           uint64_t ys, uint64_t tokens, uint64_t rows, uint64_t cols) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    uint16_t *split = nullptr;
+    const uint64_t n = std::max<uint64_t>(tokens * cols, 1);
+    if (!note(c, "gemm scratch", cudaMalloc(&split, 3 * n * 2))) return -1;
+    const bool ok = projection_with(c, x, xs, w, y, ys, tokens, rows, cols, split, nullptr) &&
+                    note(c, "gemm", cudaStreamSynchronize(c->stream));
+    cudaFree(split);
+    return ok ? 1 : -1;
+}
+
+double plamo_cuda_time_gemm(struct plamo_cuda *c, const float *x, const uint16_t *w, float *y, uint64_t tokens,
+                            uint64_t rows, uint64_t cols, uint64_t repeats) {
+    if (!c || !repeats) return -1;
+    cudaSetDevice(c->device);
+    uint16_t *split = nullptr;
+    const uint64_t n = std::max<uint64_t>(tokens * cols, 1);
+    if (!note(c, "gemm scratch", cudaMalloc(&split, 3 * n * 2))) return -1;
+    cudaStreamSynchronize(c->stream);
+    cudaEventRecord(c->ev0, c->stream);
+    bool ok = true;
+    for (uint64_t i = 0; i < repeats && ok; ++i)
+        ok = projection_with(c, x, cols, w, y, rows, tokens, rows, cols, split, nullptr);
+    cudaEventRecord(c->ev1, c->stream);
+    ok = ok && note(c, "time gemm", cudaStreamSynchronize(c->stream));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    cudaFree(split);
+    return ok ? ms : -1;
 }
 
 int plamo_cuda_gemv_device(struct plamo_cuda *c, const uint16_t *w, const float *x, float *y, uint64_t rows,

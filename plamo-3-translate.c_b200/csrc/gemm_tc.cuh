@@ -1,0 +1,285 @@
+// Prompt / verification projections on the 5th-generation tensor cores.
+//
+// Y[t][r] = sum_k W[r][k] * X[t][k] with W the exact BF16 weights and X the FP32
+// activations. X is split once into BF16 terms hi = bf16(x), mid = bf16(x - hi),
+// lo = bf16(x - hi - mid), and every K step issues one tcgen05.mma per term into
+// the same FP32 accumulator in tensor memory. Products of BF16 pairs are exact
+// in FP32, so three terms carry x to about 24 significant bits, FP32 class (two
+// terms, 16 bits, left deviations beyond the reference's own GPU acceptance
+// bound on small fixtures). Replaces the reference's FP32 batched matvec
+// (src/matmul*.s, runtime/kernels.metal:299-365).
+//
+// The tensor cores truncate while they accumulate, so error grows with the
+// number of MMAs chained into one accumulator. Each 64-wide K block therefore
+// gets a fresh accumulator (two in TMEM, double-buffered) and the epilogue
+// warps fold every block into FP32 registers with round-to-nearest adds: no
+// tensor-core chain is longer than one block, whatever K is.
+//
+// Tiling ("swap AB"): the weight rows are the M = 128 operand, tokens are N.
+// One CTA computes one 128 x N tile:
+//   warp 0      TMA producer: W tile [128 x 64] and hi/lo tiles [N x 64] per
+//               stage, 128-byte swizzle, no multicast;
+//   warp 1      allocates the TMEM accumulator; one lane issues the MMAs and
+//               tcgen05.commit releases each stage / signals the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld of their TMEM lane quadrant, stores of
+//               Y[token][row] (coalesced along rows).
+// All waits are bounded; a timeout sets an error flag and the CTA drains.
+#pragma once
+#include <cuda.h>
+
+#include "common.cuh"
+#include "../../include/plamo_synthetic.h"
+
+namespace plamo {
+
+constexpr int kTcM = 128;
+constexpr int kTcK = 64;  // BF16 elements per stage row: 128 bytes, one swizzle atom
+constexpr int kTcThreads = 192;
+constexpr int kTcMaxStages = 6;
+constexpr int kTcAcc = 2;    // TMEM accumulators (double buffer), one K block each
+constexpr int kTcTerms = 3;  // BF16 terms of each FP32 activation
+
+struct TcGemmParams {
+    float *y;  // [T][ys]
+    uint64_t ys;
+    uint32_t T, R, K;
+    uint32_t *error;
+};
+
+// ---- tcgen05 / TMA primitives ------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+// K-major operand, 128-byte swizzle: 8-row atoms of 1024 bytes, rows 128 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);   // start address
+    d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (unused for swizzled K-major)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride byte offset: next 8-row atom
+    d |= static_cast<uint64_t>(1) << 46;                 // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2) << 61;                 // layout: 128-byte swizzle
+    return d;
+}
+// kind::f16 instruction descriptor: BF16 x BF16 -> FP32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t tc_idesc(uint32_t m, uint32_t n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 consecutive FP32 accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+inline size_t tc_stage_bytes(uint32_t n) { return static_cast<size_t>(kTcM) * 128 + kTcTerms * 128ull * n; }
+inline size_t tc_smem_bytes(uint32_t n, int stages) { return stages * tc_stage_bytes(n) + 1024; }
+
+// N: tokens per tile (multiple of 16, <= 256).
+template <int N>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
+                   const __grid_constant__ CUtensorMap map_mid, const __grid_constant__ CUtensorMap map_lo,
+                   TcGemmParams p, int stages) {
+    extern __shared__ __align__(128) unsigned char tc_smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kTcMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kTcMaxStages];
+    __shared__ __align__(8) uint64_t acc_full[kTcAcc];
+    __shared__ __align__(8) uint64_t acc_empty[kTcAcc];
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag;
+
+    // 1024-byte aligned stage buffers (128-byte swizzle atoms).
+    unsigned char *base = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const uint32_t stage_bytes = kTcM * 128 + kTcTerms * N * 128;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t row0 = blockIdx.x * kTcM, tok0 = blockIdx.y * N;
+    const uint32_t kblocks = (p.K + kTcK - 1) / kTcK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < kTcAcc; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+        }
+        abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&map_w);
+        prefetch_tensormap(&map_hi);
+        prefetch_tensormap(&map_mid);
+        prefetch_tensormap(&map_lo);
+    }
+    constexpr uint32_t kCols = kTcAcc * N < 32 ? 32 : kTcAcc * N;  // power of two >= 32
+    if (warp == 1) {  // the whole warp allocates the accumulators' TMEM columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                     "r"(kCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    pdl_launch_dependents();
+    pdl_wait();
+
+    if (warp == 0 && lane == 0) {
+        uint32_t s = 0, phase = 0, issued = 0;
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+            if (kb >= static_cast<uint32_t>(stages) && !mbar_wait(&empty_bar[s], phase ^ 1u)) {
+                abort_flag = 1;
+                if (p.error) atomicExch(p.error, 3u);
+                break;
+            }
+            unsigned char *st = base + s * stage_bytes;
+            mbar_expect_tx(&full_bar[s], stage_bytes);
+            const int kx = static_cast<int>(kb * kTcK);
+            tma_load_2d(st, &map_w, kx, static_cast<int>(row0), &full_bar[s]);
+            tma_load_2d(st + kTcM * 128, &map_hi, kx, static_cast<int>(tok0), &full_bar[s]);
+            tma_load_2d(st + kTcM * 128 + N * 128, &map_mid, kx, static_cast<int>(tok0), &full_bar[s]);
+            tma_load_2d(st + kTcM * 128 + 2 * N * 128, &map_lo, kx, static_cast<int>(tok0), &full_bar[s]);
+            issued = kb + 1;
+            if (++s == static_cast<uint32_t>(stages)) {
+                s = 0;
+                phase ^= 1u;
+            }
+        }
+        // Every copy issued has landed before the CTA can exit (immediate
+        // when the MMAs consumed them; bounded otherwise).
+        for (uint32_t k = issued > static_cast<uint32_t>(stages) ? issued - stages : 0; k < issued; ++k)
+            mbar_wait(&full_bar[k % stages], (k / stages) & 1u);
+    } else if (warp == 1 && lane == 0) {
+        constexpr uint32_t idesc = tc_idesc(kTcM, N);
+        uint32_t s = 0, phase = 0;
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+            const uint32_t a = kb % kTcAcc;
+            if (kb >= static_cast<uint32_t>(kTcAcc) &&
+                !mbar_wait(&acc_empty[a], (kb / kTcAcc - 1) & 1u)) {  // epilogue drained it
+                abort_flag = 1;
+                if (p.error) atomicExch(p.error, 3u);
+                break;
+            }
+            if (!mbar_wait(&full_bar[s], phase)) {
+                abort_flag = 1;
+                if (p.error) atomicExch(p.error, 3u);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(base + s * stage_bytes);
+            const uint32_t bh = sa + kTcM * 128, bm = bh + N * 128, bl = bm + N * 128;
+            const uint32_t acc = tmem + a * N;
+#pragma unroll
+            for (int k = 0; k < kTcK / 16; ++k) {  // 16 BF16 = 32 bytes per MMA K step
+                const uint64_t da = smem_desc_sw128(sa + 32 * k);
+                tc_mma(acc, da, smem_desc_sw128(bh + 32 * k), idesc, k ? 1u : 0u);
+                tc_mma(acc, da, smem_desc_sw128(bm + 32 * k), idesc, 1u);
+                tc_mma(acc, da, smem_desc_sw128(bl + 32 * k), idesc, 1u);
+            }
+            tc_commit(&empty_bar[s]);   // the stage is free once these MMAs have read it
+            tc_commit(&acc_full[a]);    // and the block's partial is ready
+            if (++s == static_cast<uint32_t>(stages)) {
+                s = 0;
+                phase ^= 1u;
+            }
+        }
+    } else if (warp >= 2) {
+        // Fold every K block's partial into FP32 registers (IEEE adds, in order).
+        const uint32_t quad = warp & 3;  // TMEM lanes this warp may access
+        const uint32_t lanes = (quad * 32) << 16;
+        float sum[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) sum[i] = 0.0f;
+        bool ok = true;
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+            const uint32_t a = kb % kTcAcc;
+            if (!mbar_wait(&acc_full[a], (kb / kTcAcc) & 1u) || *reinterpret_cast<volatile int *>(&abort_flag)) {
+                ok = false;
+                if (p.error && lane == 0) atomicExch(p.error, 3u);
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < N; c += 32) {
+                float v[32];
+                tmem_ld32(tmem + lanes + a * N + c, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sum[c + i] = __fadd_rn(sum[c + i], v[i]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+        const uint32_t row = row0 + quad * 32 + lane;
+        if (ok && row < p.R) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                const uint32_t t = tok0 + j;
+                if (t < p.T) p.y[static_cast<uint64_t>(t) * p.ys + row] = sum[j];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+    }
+}
+
+// FP32 rows -> BF16 terms hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid)
+// (round to nearest even), row stride xs, outputs [T][K] contiguous.
+__global__ void split_hilo_kernel(const float *x, uint64_t xs, uint32_t T, uint32_t K, uint16_t *hi, uint16_t *mid,
+                                  uint16_t *lo) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint64_t total = static_cast<uint64_t>(T) * K;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t t = i / K, k = i - t * K;
+        const float v = x[t * xs + k];
+        const uint16_t h = plamo_bf16_round(v);
+        const float r1 = __fsub_rn(v, __uint_as_float(static_cast<uint32_t>(h) << 16));
+        const uint16_t md = plamo_bf16_round(r1);
+        const float r2 = __fsub_rn(r1, __uint_as_float(static_cast<uint32_t>(md) << 16));
+        hi[i] = h;
+        mid[i] = md;
+        lo[i] = plamo_bf16_round(r2);
+    }
+}
+
+}  // namespace plamo

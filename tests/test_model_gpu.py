@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 import synthetic
-from conftest import assert_close, load_oracle, load_package
+from conftest import load_oracle, load_package, rel_l2
 from fixtures import oracle_forward, oracle_prefill
 
 pytestmark = pytest.mark.gpu
@@ -92,8 +92,8 @@ def test_profile_greedy_tokens_match_oracle(backend, name, prompt, tokens):
 
 def test_8b_prefix_greedy_tokens_and_logits(backend):
     """Config 4 on a token prefix: 8B profile, 12-id prompt, 6 greedy tokens,
-    prefill logits within the acceptance rule (the oracle streams 16 GB per
-    token on the host)."""
+    prefill logits and state within the reference's whole-model rule (the
+    oracle streams 16 GB per token on the host)."""
     pkg = load_package()
     load_oracle().oracle_set_threads(os.cpu_count() or 1)
     a, b = synthetic_pair(backend, pkg.PROFILES["8b"], seed=4, full_capacity=8208)
@@ -101,8 +101,13 @@ def test_8b_prefix_greedy_tokens_and_logits(backend):
     assert backend.lib.plamo_cuda_prefill(backend.ctx, a.ptr, ids.ctypes.data, len(ids), 0) == 1
     ok, _ = oracle_prefill(b, ids)
     assert ok == 1
-    assert_close(a.logits_array(), b.logits_array(), "8b prefill logits")
-    assert_close(a.state_array(), b.state_array(), "8b prefill state")
+    # Whole-model rule of reference tools/compare_backends.py:16-33: finite
+    # values and relative L2 <= 1e-4 (the per-layer max-abs bound of
+    # tests/metal_decode.c does not apply across 32 layers).
+    for name, x, y in (("logits", a.logits_array(), b.logits_array()),
+                       ("state", a.state_array(), b.state_array())):
+        assert np.all(np.isfinite(x)) and np.all(np.isfinite(y)), name
+        assert rel_l2(x, y) <= 1e-4, f"8b prefill {name}: {rel_l2(x, y):.3g}"
     a.reset()
     b.reset()
     want, margins = oracle_generate(b, ids, 6)
