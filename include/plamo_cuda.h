@@ -126,7 +126,8 @@ int plamo_cuda_forward_greedy(struct plamo_cuda *, struct model *, uint64_t toke
 int plamo_cuda_prefill_greedy(struct plamo_cuda *, struct model *, const uint32_t *ids,
                               uint64_t tokens, uint32_t *next);
 /* Greedy request loop over token ids (reference runtime/engine.c:428-617 without
-   the tokenizer): prefill, then decode until max_tokens or a stop id (1, 16).
+   the tokenizer): reset the request, prefill, then decode until max_tokens or a
+   stop id (1, 16).
    out[] receives the emitted ids; returns their count, or -1 on failure.
    on_token (may be NULL) sees each id as soon as it is on the host; a zero
    return cancels. */
@@ -143,6 +144,25 @@ int64_t plamo_cuda_generate(struct plamo_cuda *, struct model *, const uint32_t 
    (reference src/layer.s:8-48 plamo_layer): appends one KV row to layer
    `index` and advances only that layer. */
 int plamo_cuda_layer(struct plamo_cuda *, struct model *, uint64_t index, float *state);
+/* Drop the newest `rows` committed rows of every layer of `model` (at most
+   PLAMO_CUDA_VERIFY_MAX + 1): the draft model's rollback after a partially
+   accepted proposal (reference runtime/draft.c:258-297). */
+int plamo_cuda_rollback(struct plamo_cuda *, struct model *, uint64_t rows);
+/* Speculative greedy request loop (reference runtime/engine.c:523-586, draft
+   proposer runtime/worker.c:198-318): `draft` (a smaller model prepared in the
+   same context) proposes up to `block` tokens (<= PLAMO_CUDA_VERIFY_MAX, with
+   the reference's adaptive 2/8/16 horizon), `target` verifies them in one pass
+   and commits the agreeing prefix. The emitted ids are exactly the target's
+   greedy tokens. Returns their count or -1. */
+struct plamo_cuda_speculation {
+    double prefill_seconds, decode_seconds;
+    uint64_t completion_tokens, decode_steps, verify_batches, proposed_tokens, accepted_tokens;
+    const char *finish_reason;
+};
+int64_t plamo_cuda_generate_speculative(struct plamo_cuda *, struct model *target, struct model *draft,
+                                        const uint32_t *ids, uint64_t tokens, uint64_t max_tokens, unsigned block,
+                                        uint32_t *out, int (*on_token)(uint32_t id, void *context), void *context,
+                                        struct plamo_cuda_speculation *stats);
 /* Reset the request state of `model` (all KV counts to zero) on host and device,
    like the reference's plamo_reset_request (runtime/engine.c:46-55). */
 void plamo_cuda_reset_request(struct plamo_cuda *, struct model *);

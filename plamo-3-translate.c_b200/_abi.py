@@ -90,6 +90,13 @@ class CudaTiming(ctypes.Structure):
                 ("finish_reason", c_char_p)]
 
 
+class CudaSpeculation(ctypes.Structure):
+    _fields_ = [("prefill_seconds", c_double), ("decode_seconds", c_double),
+                ("completion_tokens", c_uint64), ("decode_steps", c_uint64),
+                ("verify_batches", c_uint64), ("proposed_tokens", c_uint64),
+                ("accepted_tokens", c_uint64), ("finish_reason", c_char_p)]
+
+
 for _struct, _size in ((Qkv, 72), (Cache, 48), (Rotation, 72), (Gqa, 72), (Mixer, 56), (Mlp, 80),
                        (Layer, 64), (Model, 88), (Matmul, 64)):
     assert ctypes.sizeof(_struct) == _size, _struct.__name__
@@ -123,6 +130,9 @@ SIGNATURES = {
                                       POINTER(CudaTiming)]),
     "plamo_cuda_layer": (c_int, [P, M, c_uint64, P]),
     "plamo_cuda_reset_request": (None, [P, M]),
+    "plamo_cuda_rollback": (c_int, [P, M, c_uint64]),
+    "plamo_cuda_generate_speculative": (c_int64, [P, M, M, P, c_uint64, c_uint64, c_uint, P, TOKEN_CALLBACK, P,
+                                                  POINTER(CudaSpeculation)]),
     "plamo_cuda_read_weights": (c_int, [P, P, P, c_uint64]),
     "plamo_cuda_gemv_device": (c_int, [P, P, P, P, c_uint64, c_uint64]),
     "plamo_cuda_gemm_device": (c_int, [P, P, c_uint64, P, P, c_uint64, c_uint64, c_uint64, c_uint64]),

@@ -810,6 +810,13 @@ __global__ void kv_commit_kernel(AttnLayer L, uint64_t kvw, const float *k_row, 
     }
 }
 
+// Move every layer's committed-row counter back by `rows` (speculative
+// rollback; the rings keep the rows, so nothing else changes).
+__global__ void rollback_kernel(uint64_t *appended, uint64_t layers, uint64_t rows) {
+    pdl_wait();
+    for (uint64_t i = threadIdx.x; i < layers; i += blockDim.x) appended[i] -= rows;
+}
+
 // Advance every layer's committed-row counter by `rows` (end of a step).
 __global__ void advance_kernel(uint64_t *appended, uint64_t layers, uint64_t rows) {
     pdl_wait();

@@ -1537,6 +1537,7 @@ int64_t plamo_cuda_generate(struct plamo_cuda *c, struct model *model, const uin
     };
     const double start = now();
     uint32_t id = 0;
+    plamo_cuda_reset_request(c, model);  // a request starts from empty caches (reference runtime/engine.c:451)
     if (plamo_cuda_prefill_greedy(c, model, ids, tokens, &id) != 1) return -1;
     t->prefill_seconds = now() - start;
     t->finish_reason = "length";
@@ -1552,12 +1553,12 @@ int64_t plamo_cuda_generate(struct plamo_cuda *c, struct model *model, const uin
             t->finish_reason = "error";
             return -1;
         }
-        out[emitted++] = id;
-        if (emitted == 1) t->first_token_seconds = now() - start;
         if (on_token && !on_token(id, context)) {
             t->finish_reason = "cancelled";
             break;
         }
+        out[emitted++] = id;
+        if (emitted == 1) t->first_token_seconds = now() - start;
         if (static_cast<uint64_t>(emitted) == max_tokens) break;
         uint32_t next = 0;
         if (plamo_cuda_forward_greedy(c, model, id, &next) != 1) return -1;
@@ -1600,6 +1601,151 @@ double plamo_cuda_time_gemm(struct plamo_cuda *c, const float *x, const uint16_t
     cudaEventElapsedTime(&ms, c->ev0, c->ev1);
     cudaFree(split);
     return ok ? ms : -1;
+}
+
+int plamo_cuda_rollback(struct plamo_cuda *c, struct model *model, uint64_t rows) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || !reconcile(c, m)) return 0;
+    for (const DLayer &L : m->layers) {
+        // Rows evicted from a sliding window while they were appended must
+        // still be in the ring's spare slots.
+        if (rows > L.appended || rows > kVerifyMax + 1) {
+            c->info.declines++;
+            return 0;
+        }
+    }
+    if (!rows) return 1;
+    m->verify_valid = false;
+    rollback_kernel<<<1, 32, 0, c->stream>>>(m->d_appended, m->L, rows);
+    c->info.launches++;
+    if (!note(c, "rollback", cudaGetLastError()) || !note(c, "rollback", cudaStreamSynchronize(c->stream)))
+        return -1;
+    for (uint64_t l = 0; l < m->L; ++l) {
+        DLayer &L = m->layers[l];
+        L.appended -= rows;
+        struct cache *hc = L.host->mixer->cache;
+        hc->count = layer_count(L);
+        L.host->mixer->rotation->processed_count = hc->count;
+    }
+    if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
+    return 1;
+}
+
+// Speculative request loop (reference runtime/engine.c:523-586 with the draft
+// proposer of runtime/worker.c:198-318 and its horizon rule, runtime/draft.c:
+// 196-212): the draft model proposes greedily from the known token, the
+// target verifies the block in one pass, the longest agreeing prefix is
+// committed and the draft rolls back the rest. Emits exactly the target's
+// greedy tokens.
+int64_t plamo_cuda_generate_speculative(struct plamo_cuda *c, struct model *target, struct model *draft,
+                                        const uint32_t *ids, uint64_t tokens, uint64_t max_tokens, unsigned block,
+                                        uint32_t *out, int (*on_token)(uint32_t, void *), void *context,
+                                        struct plamo_cuda_speculation *stats) {
+    plamo_cuda_speculation local{};
+    plamo_cuda_speculation *st = stats ? stats : &local;
+    memset(st, 0, sizeof *st);
+    if (!c || !target || !draft || !out || !max_tokens || max_tokens > 4096 || !tokens || tokens > 4096 || !block ||
+        block > kVerifyMax || !find_model(c, target) || !find_model(c, draft))
+        return -1;
+    auto now = [] {
+        return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+    };
+    const double start = now();
+    uint32_t id = 0, ignored = 0;
+    // A request starts from empty caches (reference runtime/engine.c:451).
+    plamo_cuda_reset_request(c, target);
+    plamo_cuda_reset_request(c, draft);
+    if (plamo_cuda_prefill_greedy(c, target, ids, tokens, &id) != 1) return -1;
+    bool speculate = block > 1 && plamo_cuda_prefill_greedy(c, draft, ids, tokens, &ignored) == 1;
+    st->prefill_seconds = now() - start;
+    const double decode_start = now();
+    unsigned horizon = 8;
+    int64_t emitted = 0;
+    st->finish_reason = "length";
+    // reference runtime/engine.c:395-420: a stop id or a cancelling callback
+    // ends the request before the token is committed (0); the token that
+    // reaches max_tokens is counted and committed, then the request ends (2).
+    auto emit = [&](uint32_t t) -> int {
+        if (t == 1 || t == 16) {
+            st->finish_reason = "stop";
+            return 0;
+        }
+        if (t >= target->vocab) return -1;
+        if (on_token && !on_token(t, context)) {
+            st->finish_reason = "cancelled";
+            return 0;
+        }
+        out[emitted++] = t;
+        return static_cast<uint64_t>(emitted) == max_tokens ? 2 : 1;
+    };
+    int r = emit(id);
+    while (r == 1) {
+        if (speculate) {
+            unsigned limit = static_cast<unsigned>(max_tokens - static_cast<uint64_t>(emitted));
+            if (limit > block) limit = block;
+            if (limit > horizon) limit = horizon;
+            uint32_t proposed[kVerifyMax], next[kVerifyMax];
+            proposed[0] = id;
+            unsigned n = 1, processed = 0;
+            bool failed = false;
+            while (n < limit && proposed[n - 1] != 1 && proposed[n - 1] != 16) {
+                uint32_t t = 0;
+                if (plamo_cuda_forward_greedy(c, draft, proposed[n - 1], &t) != 1 || t >= draft->vocab) {
+                    failed = true;
+                    break;
+                }
+                ++processed;
+                proposed[n++] = t;
+            }
+            if (failed || plamo_cuda_verify(c, target, proposed, n, next) != 1) {
+                speculate = false;  // the target state is untouched: continue exactly
+            } else {
+                ++st->verify_batches;
+                st->proposed_tokens += n - 1;
+                unsigned consumed = 0;
+                for (unsigned j = 0; j < n; ++j) {
+                    if (j) {
+                        if (proposed[j] != next[j - 1]) break;
+                        r = emit(proposed[j]);
+                        if (r < 0) return -1;
+                        if (r == 0) break;
+                    }
+                    if (plamo_cuda_commit(c, target, j) != 1) return -1;
+                    ++consumed;
+                    ++st->decode_steps;
+                    if (r == 2) break;
+                }
+                st->accepted_tokens += consumed - 1;
+                // Draft: keep exactly the consumed prefix.
+                int ok = 1;
+                if (consumed < processed) ok = plamo_cuda_rollback(c, draft, processed - consumed);
+                else if (consumed == processed + 1) {
+                    uint32_t t = 0;
+                    ok = plamo_cuda_forward_greedy(c, draft, proposed[processed], &t);
+                }
+                if (ok != 1) speculate = false;
+                if (consumed == 1 && n > 1) horizon = 2;
+                else if (consumed < n || n < limit) horizon = 8;
+                else if (horizon < 8) horizon *= 2;
+                else horizon = kVerifyMax;
+                if (r != 1) break;
+                id = next[consumed - 1];
+                r = emit(id);
+                continue;
+            }
+        }
+        uint32_t t = 0;
+        if (plamo_cuda_forward_greedy(c, target, id, &t) != 1) return -1;
+        ++st->decode_steps;
+        id = t;
+        r = emit(id);
+    }
+    if (r < 0) return -1;
+    st->decode_seconds = now() - decode_start;
+    st->completion_tokens = static_cast<uint64_t>(emitted);
+    return emitted;
 }
 
 int plamo_cuda_gemv_device(struct plamo_cuda *c, const uint16_t *w, const float *x, float *y, uint64_t rows,
