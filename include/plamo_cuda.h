@@ -167,6 +167,32 @@ int64_t plamo_cuda_generate_speculative(struct plamo_cuda *, struct model *targe
    like the reference's plamo_reset_request (runtime/engine.c:46-55). */
 void plamo_cuda_reset_request(struct plamo_cuda *, struct model *);
 
+/* Device prompt (template prefix) cache: the snapshots of reference
+   runtime/prompt_cache.h:8-16, held in device memory. Capture copies the
+   committed KV rows [0, tokens) of every layer of a prepared model after a
+   fresh prefill of exactly `tokens` ids (1..PLAMO_CUDA_PREFIX_LIMIT); restore
+   writes them back into the device rings of the same model, sets every layer's
+   count (host and device) to the snapshot's tokens and returns that count, so a
+   following prefill of ids[tokens...] continues the prompt. The acceptance
+   rules are the reference's (runtime/prompt_cache.c:15-81): capture returns
+   NULL unless every layer holds exactly `tokens` rows and the reference's
+   16 MiB snapshot bound admits the model; restore returns 0 (touching nothing)
+   unless `model` is the captured one, `tokens` exceeds the snapshot's, the
+   snapshot ids are a prefix of `ids`, and every layer's width and capacity fit
+   (all layers are checked before any is written). A snapshot is immutable,
+   independent of later requests and owned by the caller; free it with
+   plamo_cuda_prompt_cache_free before closing its context. bytes() counts the
+   device memory it holds (K and V rows; rotated keys are derived on the fly). */
+#define PLAMO_CUDA_PREFIX_LIMIT 64
+struct plamo_cuda_prompt_cache;
+struct plamo_cuda_prompt_cache *plamo_cuda_prompt_cache_capture(struct plamo_cuda *, const struct model *,
+                                                                const uint32_t *ids, uint64_t tokens);
+uint64_t plamo_cuda_prompt_cache_restore(struct plamo_cuda *, const struct plamo_cuda_prompt_cache *,
+                                         struct model *, const uint32_t *ids, uint64_t tokens);
+uint64_t plamo_cuda_prompt_cache_tokens(const struct plamo_cuda_prompt_cache *);
+uint64_t plamo_cuda_prompt_cache_bytes(const struct plamo_cuda_prompt_cache *);
+void plamo_cuda_prompt_cache_free(struct plamo_cuda_prompt_cache *);
+
 /* Standalone BF16 GEMV on device buffers: y[rows] = W[rows, cols] . x[cols]
    with FP32 accumulation (the decode projection kernel). Asynchronous on the
    context's stream. */

@@ -14,6 +14,7 @@ from ctypes import POINTER, c_char, c_char_p, c_double, c_int, c_int64, c_uint, 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libplamo_cuda.so")
 LINEAR_STATIC_FLOATS = 4 << 20  # PLAMO_CUDA_LINEAR_STATIC_FLOATS
+PREFIX_LIMIT = 64  # PLAMO_CUDA_PREFIX_LIMIT
 
 
 class Qkv(ctypes.Structure):
@@ -131,6 +132,11 @@ SIGNATURES = {
     "plamo_cuda_layer": (c_int, [P, M, c_uint64, P]),
     "plamo_cuda_reset_request": (None, [P, M]),
     "plamo_cuda_rollback": (c_int, [P, M, c_uint64]),
+    "plamo_cuda_prompt_cache_capture": (c_void_p, [P, M, P, c_uint64]),
+    "plamo_cuda_prompt_cache_restore": (c_uint64, [P, P, M, P, c_uint64]),
+    "plamo_cuda_prompt_cache_tokens": (c_uint64, [P]),
+    "plamo_cuda_prompt_cache_bytes": (c_uint64, [P]),
+    "plamo_cuda_prompt_cache_free": (None, [P]),
     "plamo_cuda_generate_speculative": (c_int64, [P, M, M, P, c_uint64, c_uint64, c_uint, P, TOKEN_CALLBACK, P,
                                                   POINTER(CudaSpeculation)]),
     "plamo_cuda_read_weights": (c_int, [P, P, P, c_uint64]),

@@ -89,6 +89,7 @@ struct AttnParams {
     float *part;       // [tokens][qh][splits][dim + 2] partial (acc, m, l)
     uint32_t *tickets; // [tokens][kh] arrival counters (zero between launches)
     uint32_t splits;
+    uint32_t t0;       // first query token of this launch (blockIdx.y counts from it)
 };
 
 // One CTA per (kv head, query token, key split). Keys of the split are
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     extern __shared__ __align__(16) float sm[];
     const uint32_t D = static_cast<uint32_t>(p.S.dim), half = D / 2;
     const uint32_t QH = static_cast<uint32_t>(p.S.qh), KH = static_cast<uint32_t>(p.S.kh), G = QH / KH;
-    const uint64_t kh = blockIdx.x, t = blockIdx.y, split = blockIdx.z;
+    const uint64_t kh = blockIdx.x, t = blockIdx.y + p.t0, split = blockIdx.z;
     const uint32_t KS = D + 1;          // padded key row: conflict-free column reads
     float *qs = sm;                     // [G][D]
     float *kt = qs + G * D;             // [tile][D + 1]
@@ -240,6 +241,194 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
 inline size_t attention_smem_bytes(uint64_t G, uint64_t D) {
     return (G * D + kAttnTile * (D + 1) + kAttnTile * D + G * kAttnTile + G * D + 3 * G) *
            sizeof(float);
+}
+
+// ---------------------------------------------------------------------------
+// Prompt attention, blocked over queries (dim 128). attention_kernel stages
+// and rotates every key once per query token; here one CTA takes 64 query
+// rows (64/G consecutive tokens x the G heads of one kv head) and every
+// staged, rotated key tile serves all of them, from registers:
+//   scores  - each thread 4 rows x 2 keys, Q transposed in shared memory
+//             (one 128-bit load per 4 rows), keys in padded rows;
+//   softmax - row max by shuffles over the 16 threads of a row group, the
+//             reference exp per element, row sums sequential in key order;
+//   values  - each thread 8 rows x 4 dims, acc *= correction then sequential
+//             FMA over the tile's keys.
+// The arithmetic is attention_kernel's with one split, operation for
+// operation: 32-key tiles from the window start, sequential FMA dots over dim
+// times 1/sqrt(dim), running max, l = l*c + e in key order, acc = acc*c then
+// FMA in key order, out = acc / l. Keys past a row's causal end enter as
+// exp(-inf) = 0, which leaves l, the max and acc unchanged, so every output
+// is bit-identical to attention_kernel's and independent of how the prompt is
+// batched. All queries of one launch must share the window start 0 (full
+// layers, or sliding layers whose window is not yet full); the host sends the
+// other queries of a sliding layer to attention_kernel.
+constexpr int kPaThreads = 256;
+constexpr int kPaRows = 64;             // query rows (token x head) per CTA
+constexpr int kPaTile = kAttnTile;      // keys per tile
+constexpr int kPaD = 128;
+constexpr int kPaQS = kPaRows + 4;      // transposed Q / P row stride (floats, 16-byte multiple)
+constexpr int kPaKS = kPaD + 1;         // padded key row: conflict-free column reads
+
+struct PromptAttnParams {
+    AttnLayer L;
+    const float *q;    // [tokens][qh][128], rotated
+    const float *qkv;  // new rows: K at qh*128, V at (qh+kh)*128 of each token row
+    float *out;        // [tokens][qh][128]
+    uint32_t qh, kh, qkv_stride;
+    uint32_t tokens;     // queries [0, tokens) of this call
+    uint32_t per_block;  // query tokens per CTA: 64 / G
+};
+
+inline size_t prompt_attention_smem_bytes() {
+    return (kPaD * kPaQS + kPaTile * kPaKS + kPaTile * kPaD + kPaTile * kPaQS + 2 * kPaRows) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttnParams p) {
+    extern __shared__ __align__(16) float sm[];
+    float *qT = sm;                       // [128][kPaQS]  Q rows, transposed
+    float *kt = qT + kPaD * kPaQS;        // [tile][kPaKS] rotated keys
+    float *vt = kt + kPaTile * kPaKS;     // [tile][128]   values
+    float *pT = vt + kPaTile * kPaD;      // [tile][kPaQS] exp(score - max), transposed
+    float *corr = pT + kPaTile * kPaQS;   // [64] per-row correction of the tile
+    float *lsum = corr + kPaRows;         // [64] final row sums
+    constexpr uint32_t D = kPaD, half = kPaD / 2;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t G = p.qh / p.kh, BQ = p.per_block;
+    const uint32_t kh = blockIdx.y;
+    const uint32_t t0 = (gridDim.x - 1 - blockIdx.x) * BQ;  // latest (longest) blocks start first
+    const uint32_t tq = min(BQ, p.tokens - t0), vrows = tq * G;
+    const uint32_t kvw = p.kh * D;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(D)));
+    const float ninf = -__int_as_float(0x7f800000);
+
+    pdl_wait();
+    const uint32_t P = static_cast<uint32_t>(*p.L.appended);
+    const uint32_t ring = static_cast<uint32_t>(p.L.ring);
+    const uint32_t hi_max = P + t0 + tq;  // keys [0, hi_max)
+
+    for (uint32_t i = tid; i < kPaRows * D; i += kPaThreads) {
+        const uint32_t r = i / D, d = i - r * D;
+        float v = 0.0f;
+        if (r < vrows) {
+            const uint32_t qi = r / G, g = r - qi * G;
+            v = p.q[(static_cast<size_t>(t0 + qi) * p.qh + kh * G + g) * D + d];
+        }
+        qT[d * kPaQS + r] = v;
+    }
+
+    // Score-phase roles: rows ty*4 .. ty*4+3, keys tx and tx+16.
+    const uint32_t ty = tid >> 4, tx = tid & 15;
+    uint32_t hi[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t r = ty * 4 + i;
+        hi[i] = r < vrows ? P + t0 + r / G + 1 : 0;
+    }
+    float mrow[4] = {ninf, ninf, ninf, ninf};
+    // Value-phase roles: rows warp*8 .. warp*8+7, dims lane*4 .. lane*4+3.
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+    float l = 0.0f;  // row `tid` (tid < 64)
+
+    for (uint32_t base = 0; base < hi_max; base += kPaTile) {
+        const uint32_t trow = min(static_cast<uint32_t>(kPaTile), hi_max - base);
+        for (uint32_t i = tid; i < trow * half; i += kPaThreads) {
+            const uint32_t r = i / half, d = i - r * half, key = base + r;
+            const float *ksrc = key < P ? p.L.ring_k + static_cast<size_t>(key % ring) * kvw + kh * D
+                                        : p.qkv + static_cast<size_t>(key - P) * p.qkv_stride + p.qh * D + kh * D;
+            const float *c = p.L.table + static_cast<size_t>(key) * D, *s = c + half;
+            const float a = ksrc[d], b = ksrc[d + half];
+            kt[r * kPaKS + d] = __fsub_rn(__fmul_rn(a, c[d]), __fmul_rn(b, s[d]));
+            kt[r * kPaKS + d + half] = __fadd_rn(__fmul_rn(b, c[d]), __fmul_rn(a, s[d]));
+        }
+        for (uint32_t i = tid; i < trow * (D / 4); i += kPaThreads) {
+            const uint32_t r = i / (D / 4), c4 = i - r * (D / 4), key = base + r;
+            const float *vsrc = key < P
+                                    ? p.L.ring_v + static_cast<size_t>(key % ring) * kvw + kh * D
+                                    : p.qkv + static_cast<size_t>(key - P) * p.qkv_stride + (p.qh + p.kh) * D + kh * D;
+            *reinterpret_cast<float4 *>(vt + r * D + c4 * 4) = ld4(vsrc + c4 * 4);
+        }
+        __syncthreads();
+
+        float s[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
+        const float *k0 = kt + tx * kPaKS, *k1 = kt + (tx + 16) * kPaKS;
+#pragma unroll 8
+        for (uint32_t d = 0; d < D; ++d) {
+            const float4 q = *reinterpret_cast<const float4 *>(qT + d * kPaQS + ty * 4);
+            const float a = k0[d], b = k1[d];
+            s[0][0] = fmaf(q.x, a, s[0][0]);
+            s[1][0] = fmaf(q.y, a, s[1][0]);
+            s[2][0] = fmaf(q.z, a, s[2][0]);
+            s[3][0] = fmaf(q.w, a, s[3][0]);
+            s[0][1] = fmaf(q.x, b, s[0][1]);
+            s[1][1] = fmaf(q.y, b, s[1][1]);
+            s[2][1] = fmaf(q.z, b, s[2][1]);
+            s[3][1] = fmaf(q.w, b, s[3][1]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint32_t key = base + tx + 16 * j;
+                s[i][j] = key < hi[i] ? __fmul_rn(s[i][j], scale) : ninf;
+            }
+            float m = fmaxf(s[i][0], s[i][1]);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            m = fmaxf(mrow[i], m);
+            const float c = plamo_exp(__fsub_rn(mrow[i], m));
+            mrow[i] = m;
+            pT[tx * kPaQS + ty * 4 + i] = plamo_exp(__fsub_rn(s[i][0], m));
+            pT[(tx + 16) * kPaQS + ty * 4 + i] = plamo_exp(__fsub_rn(s[i][1], m));
+            if (tx == 0) corr[ty * 4 + i] = c;
+        }
+        __syncthreads();
+
+        if (tid < kPaRows) {
+            l = __fmul_rn(l, corr[tid]);
+            for (uint32_t r = 0; r < trow; ++r) l = __fadd_rn(l, pT[r * kPaQS + tid]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float c = corr[warp * 8 + i];
+            acc[i][0] = __fmul_rn(acc[i][0], c);
+            acc[i][1] = __fmul_rn(acc[i][1], c);
+            acc[i][2] = __fmul_rn(acc[i][2], c);
+            acc[i][3] = __fmul_rn(acc[i][3], c);
+        }
+        for (uint32_t r = 0; r < trow; ++r) {
+            const float4 v = *reinterpret_cast<const float4 *>(vt + r * D + lane * 4);
+            const float4 pa = *reinterpret_cast<const float4 *>(pT + r * kPaQS + warp * 8);
+            const float4 pb = *reinterpret_cast<const float4 *>(pT + r * kPaQS + warp * 8 + 4);
+            const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                acc[i][0] = fmaf(pr[i], v.x, acc[i][0]);
+                acc[i][1] = fmaf(pr[i], v.y, acc[i][1]);
+                acc[i][2] = fmaf(pr[i], v.z, acc[i][2]);
+                acc[i][3] = fmaf(pr[i], v.w, acc[i][3]);
+            }
+        }
+        __syncthreads();
+    }
+
+    if (tid < kPaRows) lsum[tid] = l;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t r = warp * 8 + i;
+        if (r >= vrows) continue;
+        const uint32_t qi = r / G, g = r - qi * G;
+        const float inv = lsum[r];
+        float4 o = make_float4(__fdiv_rn(acc[i][0], inv), __fdiv_rn(acc[i][1], inv), __fdiv_rn(acc[i][2], inv),
+                               __fdiv_rn(acc[i][3], inv));
+        *reinterpret_cast<float4 *>(p.out + (static_cast<size_t>(t0 + qi) * p.qh + kh * G + g) * D + lane * 4) = o;
+    }
+    pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------

@@ -117,9 +117,25 @@ struct plamo_cuda {
     bool bulk_gemv;
     int gemv_ring_kb;
     bool tc_gemm;
+    bool prompt_attn;  // blocked prompt attention (PLAMO_CUDA_PROMPT_ATTN=0 disables)
     int gemv_ctas;
     uint32_t *sink;
     float *static_scratch;  // device address of g_linear_static_scratch (set on first use)
+};
+
+// A template-prefix snapshot (reference runtime/prompt_cache.c:5-13 keeps the
+// model, the ids and each layer's width and RoPE scale beside the rows). The
+// rows live in HBM as [layer][K|V][tokens][kv width]: the device rings hold
+// unrotated keys, so the rotated copy the reference also stores is not needed.
+struct plamo_cuda_prompt_cache {
+    const struct model *model;
+    const plamo_cuda *owner;
+    int device;
+    uint64_t tokens, layers, kvw, bytes;
+    uint32_t ids[PLAMO_CUDA_PREFIX_LIMIT];
+    std::vector<uint64_t> width;
+    std::vector<uint32_t> scale_bits;
+    float *rows;
 };
 
 namespace {
@@ -371,7 +387,7 @@ template <int N>
 bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &mm,
                const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T) {
     int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, (c->smem_optin - 2048) / tc_stage_bytes(N)));
-    const dim3 grid((R + kTcM - 1) / kTcM, (T + N - 1) / N);
+    const dim3 grid((T + N - 1) / N, (R + kTcM - 1) / kTcM);
     return launch(c, gemm_tc_kernel<N>, grid, dim3(kTcThreads), tc_smem_bytes(N, stages), mw, mh, mm, ml, p,
                   stages);
 }
@@ -701,6 +717,40 @@ bool check_device_error(plamo_cuda *c, DModel *m) {
 }
 
 // ---- layer-major prompt / verification ------------------------------------
+// Attention of T prompt (or candidate) tokens of layer l. From 16 tokens on,
+// queries whose window starts at row 0 (all of a full layer; a sliding
+// layer's until its window fills) go to the blocked kernel, the rest to the
+// per-token kernel; both give the same bits.
+bool prompt_attention(plamo_cuda *c, DModel *m, uint64_t l, uint64_t T, size_t attn_smem) {
+    const DLayer &L = m->layers[l];
+    const AttnLayer al = attn_layer(m, l);
+    const AttnShape shape{T, m->QH, m->KH, m->D, m->QW};
+    const uint64_t G = m->QH / m->KH;
+    uint64_t blocked = 0;
+    if (c->prompt_attn && T >= 16 && m->D == kPaD && G <= kPaRows)
+        blocked = L.sliding ? (L.capacity > L.appended ? std::min(T, L.capacity - L.appended) : 0) : T;
+    if (blocked) {
+        const uint32_t per_block = static_cast<uint32_t>(kPaRows / G);
+        PromptAttnParams pp{al,
+                            m->p_q,
+                            m->p_qkv,
+                            m->p_attn,
+                            static_cast<uint32_t>(m->QH),
+                            static_cast<uint32_t>(m->KH),
+                            static_cast<uint32_t>(m->QW),
+                            static_cast<uint32_t>(blocked),
+                            per_block};
+        const dim3 grid(static_cast<uint32_t>((blocked + per_block - 1) / per_block), static_cast<uint32_t>(m->KH));
+        if (!launch(c, prompt_attention_kernel, grid, dim3(kPaThreads), prompt_attention_smem_bytes(), pp))
+            return false;
+    }
+    if (blocked == T) return true;
+    const uint32_t splits = T >= 16 ? 1u : m->splits;
+    AttnParams ap{al, shape, m->p_q, m->p_qkv, m->p_attn, m->p_part, m->p_tickets, splits,
+                  static_cast<uint32_t>(blocked)};
+    return launch(c, attention_kernel, dim3(m->KH, T - blocked, splits), dim3(kAttnThreads), attn_smem, ap);
+}
+
 // mode 0: prefill (rows stored into the rings); 1: verification (rows kept
 // per layer in v_kv, nothing committed).
 bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all_logits) {
@@ -726,10 +776,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
         AttnLayer al = attn_layer(m, l);
         if (!launch(c, qk_prep_kernel, dim3(m->QH + m->KH, T), dim3(128), 0, m->p_qkv, m->p_q, al, shape))
             return false;
-        const uint32_t splits = T >= 16 ? 1u : m->splits;
-        AttnParams ap{al, shape, m->p_q, m->p_qkv, m->p_attn, m->p_part, m->p_tickets, splits};
-        if (!launch(c, attention_kernel, dim3(m->KH, T, splits), dim3(kAttnThreads), attn_smem, ap))
-            return false;
+        if (!prompt_attention(c, m, l, T, attn_smem)) return false;
         if (mode == 0) {
             const uint64_t first = T > L.ring ? T - L.ring : 0;
             if (!launch(c, kv_store_kernel, dim3(T - first), dim3(256), 0, al, shape,
@@ -846,6 +893,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->bulk_gemv = !bulk || strcmp(bulk, "0");
     const char *tc = getenv("PLAMO_CUDA_TC_GEMM");
     c->tc_gemm = !tc || strcmp(tc, "0");
+    const char *pa = getenv("PLAMO_CUDA_PROMPT_ATTN");
+    c->prompt_attn = !pa || strcmp(pa, "0");
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
     c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
@@ -870,6 +919,7 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>(optin);
     set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin);
     allow_smem(attention_kernel, optin);
+    allow_smem(prompt_attention_kernel, optin);
     allow_smem(decode_attention128_kernel, optin);
     allow_smem(gemm_tc_kernel<16>, optin);
     allow_smem(gemm_tc_kernel<32>, optin);
@@ -1631,6 +1681,117 @@ int plamo_cuda_rollback(struct plamo_cuda *c, struct model *model, uint64_t rows
     }
     if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
     return 1;
+}
+
+// Capture (reference runtime/prompt_cache.c:15-51). The acceptance test is the
+// reference's, including its snapshot bound: a 16 MiB budget that starts with
+// the reference record's own size and charges 12 bytes per cached element
+// (K, V and rotated K), so the same models and prefixes are admitted.
+struct plamo_cuda_prompt_cache *plamo_cuda_prompt_cache_capture(struct plamo_cuda *c, const struct model *model,
+                                                                const uint32_t *ids, uint64_t tokens) {
+    constexpr uint64_t kLimit = uint64_t{16} << 20;
+    constexpr uint64_t kReferenceRecord = 8 + 3 * 8 + PLAMO_CUDA_PREFIX_LIMIT * 4 + 128 * 16;
+    if (!c || !model || !ids || !tokens || tokens > PLAMO_CUDA_PREFIX_LIMIT || !model->count || model->count > 128)
+        return nullptr;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, const_cast<struct model *>(model));
+    if (!m || !reconcile(c, m)) return nullptr;
+    uint64_t budget = kReferenceRecord;
+    for (uint64_t l = 0; l < model->count; ++l) {
+        const struct mixer *mx = model->layers[l]->mixer;
+        const struct cache *hc = mx->cache;
+        const DLayer &L = m->layers[l];
+        if (!hc->width || hc->count != tokens || hc->capacity < tokens || mx->rotation->cache != hc ||
+            mx->rotation->processed_count != tokens || !hc->k || !hc->v || !mx->rotation->out ||
+            hc->width > (kLimit - budget) / (tokens * 12))
+            return nullptr;
+        budget += hc->width * tokens * 12;
+        // The device rows must be logical rows 0..tokens-1 in slots 0..tokens-1.
+        if (hc->width != m->KVW || L.appended != tokens || L.ring < tokens) return nullptr;
+    }
+    auto s = std::make_unique<plamo_cuda_prompt_cache>();
+    s->model = model;
+    s->owner = c;
+    s->device = c->device;
+    s->tokens = tokens;
+    s->layers = model->count;
+    s->kvw = m->KVW;
+    s->bytes = model->count * 2 * tokens * m->KVW * 4;
+    memcpy(s->ids, ids, tokens * 4);
+    if (!note(c, "prompt cache alloc", cudaMalloc(&s->rows, s->bytes))) return nullptr;
+    const uint64_t words = tokens * m->KVW;
+    bool ok = true;
+    for (uint64_t l = 0; l < model->count && ok; ++l) {
+        const DLayer &L = m->layers[l];
+        s->width.push_back(model->layers[l]->mixer->cache->width);
+        s->scale_bits.push_back(model->layers[l]->mixer->rotation->scale_bits);
+        ok = note(c, "prompt cache capture", cudaMemcpyAsync(s->rows + (2 * l) * words, L.ring_k, words * 4,
+                                                             cudaMemcpyDeviceToDevice, c->stream)) &&
+             note(c, "prompt cache capture", cudaMemcpyAsync(s->rows + (2 * l + 1) * words, L.ring_v, words * 4,
+                                                             cudaMemcpyDeviceToDevice, c->stream));
+    }
+    ok = ok && note(c, "prompt cache capture", cudaStreamSynchronize(c->stream));
+    if (!ok) {
+        cudaFree(s->rows);
+        return nullptr;
+    }
+    return s.release();
+}
+
+// Restore (reference runtime/prompt_cache.c:53-81): every destination is
+// checked before any is written, so a miss changes nothing.
+uint64_t plamo_cuda_prompt_cache_restore(struct plamo_cuda *c, const struct plamo_cuda_prompt_cache *s,
+                                         struct model *model, const uint32_t *ids, uint64_t tokens) {
+    if (!c || !s || s->model != model || !ids || tokens <= s->tokens || model->count != s->layers ||
+        memcmp(ids, s->ids, s->tokens * 4))
+        return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (s->owner != c || !m || m->KVW != s->kvw) return 0;
+    for (uint64_t l = 0; l < model->count; ++l) {
+        const struct mixer *mx = model->layers[l]->mixer;
+        const struct cache *hc = mx->cache;
+        const DLayer &L = m->layers[l];
+        if (hc->width != s->width[l] || hc->capacity < s->tokens || mx->rotation->cache != hc || !hc->k || !hc->v ||
+            !mx->rotation->out || L.capacity < s->tokens || L.ring < s->tokens)
+            return 0;
+    }
+    m->verify_valid = false;  // a pending verification's rows are gone
+    const uint64_t words = s->tokens * s->kvw;
+    bool ok = true;
+    for (uint64_t l = 0; l < model->count && ok; ++l) {
+        DLayer &L = m->layers[l];
+        ok = note(c, "prompt cache restore", cudaMemcpyAsync(L.ring_k, s->rows + (2 * l) * words, words * 4,
+                                                             cudaMemcpyDeviceToDevice, c->stream)) &&
+             note(c, "prompt cache restore", cudaMemcpyAsync(L.ring_v, s->rows + (2 * l + 1) * words, words * 4,
+                                                             cudaMemcpyDeviceToDevice, c->stream));
+        L.appended = s->tokens;
+        L.stale = false;
+        struct mixer *mx = model->layers[l]->mixer;
+        mx->cache->count = mx->rotation->processed_count = s->tokens;
+        mx->rotation->scale_bits = s->scale_bits[l];
+    }
+    std::vector<uint64_t> counts(m->L, s->tokens);
+    ok = ok && note(c, "counter upload", cudaMemcpyAsync(m->d_appended, counts.data(), m->L * 8,
+                                                         cudaMemcpyHostToDevice, c->stream)) &&
+         note(c, "prompt cache restore", cudaStreamSynchronize(c->stream));
+    if (ok && c->config.copy_kv_to_host) ok = sync_kv(c, m);
+    if (!ok) {
+        // A failed copy leaves the rows unknown: drop the request state.
+        plamo_cuda_reset_request(c, model);
+        return 0;
+    }
+    return s->tokens;
+}
+
+uint64_t plamo_cuda_prompt_cache_tokens(const struct plamo_cuda_prompt_cache *s) { return s ? s->tokens : 0; }
+uint64_t plamo_cuda_prompt_cache_bytes(const struct plamo_cuda_prompt_cache *s) { return s ? s->bytes : 0; }
+
+void plamo_cuda_prompt_cache_free(struct plamo_cuda_prompt_cache *s) {
+    if (!s) return;
+    cudaSetDevice(s->device);
+    cudaFree(s->rows);
+    delete s;
 }
 
 // Speculative request loop (reference runtime/engine.c:523-586 with the draft

@@ -125,7 +125,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const uint32_t stage_bytes = kTcM * 128 + kTcTerms * N * 128;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t row0 = blockIdx.x * kTcM, tok0 = blockIdx.y * N;
+    // Token tiles run fastest: the CTAs that share one weight tile start
+    // together, so it crosses HBM once and the others read it from L2.
+    const uint32_t row0 = blockIdx.y * kTcM, tok0 = blockIdx.x * N;
     const uint32_t kblocks = (p.K + kTcK - 1) / kTcK;
 
     if (threadIdx.x == 0) {

@@ -5,7 +5,9 @@ host, so its own known-answer C tests are compiled, unchanged and where they
 lie, against the oracle (oracle/Makefile `ref-tests`) and must all pass:
 math, activation, token, qkv, rope, cache, cache_rope, rope_table, trig,
 attention, model, mixer (closed-form layer/model), matmul (bitwise tiling),
-prefill (40 bitwise prefill cases) and cache_rope_cached.
+prefill (40 bitwise prefill cases) and cache_rope_cached. The reference's
+portable prompt cache (runtime/prompt_cache.c) is built from its source with
+its own test, which pins the semantics the device prompt cache mirrors.
 """
 import os
 import subprocess
@@ -25,7 +27,8 @@ def test_reference_known_answer_tests_pass_against_oracle():
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     passes = [line for line in r.stdout.splitlines() if "PASS" in line]
-    assert len(passes) == 16, r.stdout
+    assert len(passes) == 17, r.stdout
+    assert "template prefix snapshots: PASS" in r.stdout
 
 
 def test_rope_frequencies_match_oracle_constants():
