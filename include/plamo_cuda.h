@@ -238,6 +238,42 @@ int plamo_cuda_fill_synthetic_bf16(struct plamo_cuda *, uint16_t *device_dst, ui
                                    uint64_t seed, float mean, float std);
 int plamo_cuda_fill_synthetic_f32(struct plamo_cuda *, float *device_dst, uint64_t count,
                                   uint64_t seed, float mean, float std);
+/* A shard of a synthetic [*, full_cols] tensor: registers under host_key the
+   rows row_start[i] .. row_start[i]+row_count[i]-1 (segments in order) and
+   columns col0 .. col0+cols-1 of the tensor plamo_cuda_preload_synthetic
+   would generate with the same seed, bit for bit. */
+int plamo_cuda_preload_synthetic_rows(struct plamo_cuda *, const void *host_key, uint64_t cols,
+                                      uint64_t full_cols, uint64_t col0, const uint64_t *row_start,
+                                      const uint64_t *row_count, unsigned segments, uint64_t seed,
+                                      float mean, float std);
+
+/* Tensor parallelism (no counterpart in the reference, which runs on one
+   GPU): one process and one context per GPU, `size` ranks (2..8). Each rank
+   prepares its shard of the model: the descriptor tree of the full model with
+   qh/size query heads, kh/size KV heads and intermediate/size MLP rows (rank
+   r holds query heads [r*qh/size, ...), KV heads [r*kh/size, ...), gate and
+   up rows [r*I/size, ...) and the matching o_proj and down_proj columns), the
+   full embedding, `vocab` = the full vocabulary, and `head` pointing at the
+   rank's `vocab_rows` head rows starting at global row `vocab_offset`.
+   tp_prepare prepares that shard, allocates this rank's exchange buffer and
+   returns its CUDA IPC handle; after every rank has called it, tp_connect
+   maps the peers' buffers (handles indexed by rank, `size` entries). From then
+   on forward / prefill / verify / generate of the shard run tensor-parallel:
+   the o_proj and down_proj partial sums are pushed into every peer's buffer
+   by the projection kernels themselves and summed in rank order by the
+   consumer's prologue (one exchange per attention block and per MLP block,
+   P2P stores over NVLink, no multicast), and the greedy token is the first
+   maximum over the ranks' head slices. Every rank must make the same calls
+   in the same order; a peer that does not arrive within 2 s makes the call
+   fail (-1). The host logits hold only this rank's slice
+   [vocab_offset, vocab_offset + vocab_rows). */
+#define PLAMO_CUDA_TP_MAX 8
+struct plamo_cuda_tp_handle {
+    unsigned char bytes[64];
+};
+int plamo_cuda_tp_prepare(struct plamo_cuda *, struct model *shard, unsigned rank, unsigned size,
+                          uint64_t vocab_offset, uint64_t vocab_rows, struct plamo_cuda_tp_handle *handle);
+int plamo_cuda_tp_connect(struct plamo_cuda *, struct model *shard, const struct plamo_cuda_tp_handle *handles);
 
 #ifdef __cplusplus
 }

@@ -7,8 +7,10 @@ the reference's engine would hand to its GPU backend.
 from . import _abi
 from ._abi import load, LIB_PATH
 from .model import (PROFILES, Backend, HostModel, LayerSpec, Profile, concentration,
-                    default_layer_specs, rope_frequencies, schema, synthetic_parameters)
+                    default_layer_specs, rope_frequencies, schema, synthetic_parameters,
+                    tp_all_gather_handles, tp_segments, tp_shard_profile, tp_vocab_slice)
 
 __all__ = ["_abi", "load", "LIB_PATH", "PROFILES", "Backend", "HostModel", "LayerSpec", "Profile",
            "concentration", "default_layer_specs", "rope_frequencies", "schema",
-           "synthetic_parameters"]
+           "synthetic_parameters", "tp_all_gather_handles", "tp_segments",
+           "tp_shard_profile", "tp_vocab_slice"]

@@ -102,6 +102,12 @@ for _struct, _size in ((Qkv, 72), (Cache, 48), (Rotation, 72), (Gqa, 72), (Mixer
                        (Layer, 64), (Model, 88), (Matmul, 64)):
     assert ctypes.sizeof(_struct) == _size, _struct.__name__
 
+class TpHandle(ctypes.Structure):
+    """struct plamo_cuda_tp_handle: a CUDA IPC handle of a rank's exchange buffer."""
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+TP_MAX = 8  # PLAMO_CUDA_TP_MAX
 TOKEN_CALLBACK = ctypes.CFUNCTYPE(c_int, c_uint32, c_void_p)
 P = c_void_p
 M = POINTER(Model)
@@ -157,6 +163,11 @@ SIGNATURES = {
                                                ctypes.c_float]),
     "plamo_cuda_fill_synthetic_f32": (c_int, [P, P, c_uint64, c_uint64, ctypes.c_float,
                                               ctypes.c_float]),
+    "plamo_cuda_preload_synthetic_rows": (c_int, [P, P, c_uint64, c_uint64, c_uint64, P, P, c_uint,
+                                                  c_uint64, ctypes.c_float, ctypes.c_float]),
+    "plamo_cuda_tp_prepare": (c_int, [P, M, c_uint, c_uint, c_uint64, c_uint64,
+                                      POINTER(TpHandle)]),
+    "plamo_cuda_tp_connect": (c_int, [P, M, POINTER(TpHandle)]),
 }
 
 _lib = None

@@ -10,6 +10,7 @@
 #include "attention.cuh"
 #include "rows.cuh"
 #include "gemm_tc.cuh"
+#include "tp.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -66,9 +67,30 @@ struct DLayer {
     uint64_t host_hash; // FNV-1a of the newest host K row written by this backend
 };
 
+// Tensor-parallel state of a shard (see tp.cuh). The exchange buffer has the
+// same layout on every rank:
+//   decode partials [2L][tp][H] f32, decode flags [2L][tp] u32 (point 2l after
+//   o_proj of layer l, 2l+1 after its down_proj); prompt partials
+//   [2][tp][tmax*H] f32 (alternating points), prompt flags [2L][tp] u32;
+//   argmax slots [verify max][tp][4] u32.
+struct TpState {
+    bool active = false;
+    uint32_t rank = 0, size = 0;
+    uint64_t voff = 0;
+    char *xbuf = nullptr;
+    char *peer[kTpMax] = {};
+    uint64_t off_dparts = 0, off_dflags = 0, off_pparts = 0, off_pflags = 0, off_args = 0, bytes = 0;
+    uint32_t *tickets = nullptr;  // [4L] local: decode points, then prompt points
+    uint32_t *epoch = nullptr;
+    float *lval = nullptr;        // this rank's per-row best value [verify max]
+    uint32_t *lidx = nullptr;     // and local index
+};
+
 struct DModel {
     struct model *host;
     uint64_t H, QH, KH, D, I, V, L, QW, AW, KVW;
+    uint64_t Vh;  // head rows held here: V, or the rank's slice of a tensor-parallel shard
+    TpState tp;
     const uint16_t *emb, *norm, *head;
     std::vector<DLayer> layers;
     uint64_t *d_appended;
@@ -464,6 +486,8 @@ void *dalloc(plamo_cuda *c, DModel *m, uint64_t bytes) {
 void free_model(plamo_cuda *c, DModel *m) {
     if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
     if (m->graph) cudaGraphDestroy(m->graph);
+    for (uint32_t r = 0; r < m->tp.size; ++r)
+        if (r != m->tp.rank && m->tp.peer[r]) cudaIpcCloseMemHandle(m->tp.peer[r]);
     for (void *p : m->allocations) cudaFree(p);
     m->allocations.clear();
     (void)c;
@@ -594,6 +618,61 @@ bool launch_decode_attention(plamo_cuda *c, DModel *m, uint64_t l) {
     return launch(c, decode_attention_kernel<0>, grid, block, smem, dp);
 }
 
+// Exchange point `index` of the decode step (0..2L-1) or of a prompt.
+TpPoint tp_point(DModel *m, bool prompt, uint64_t index) {
+    const TpState &t = m->tp;
+    TpPoint p{};
+    p.tp = t.size;
+    p.stride = prompt ? m->tmax * m->H : m->H;
+    const uint64_t parts = prompt ? t.off_pparts + (index % 2) * t.size * p.stride * 4
+                                  : t.off_dparts + index * t.size * p.stride * 4;
+    const uint64_t flags = (prompt ? t.off_pflags : t.off_dflags) + index * t.size * 4;
+    p.parts = reinterpret_cast<const float *>(t.xbuf + parts);
+    p.flags = reinterpret_cast<const uint32_t *>(t.xbuf + flags);
+    for (uint32_t r = 0; r < t.size; ++r) {
+        p.peer_parts[r] = reinterpret_cast<float *>(t.peer[r] + parts) + t.rank * p.stride;
+        p.peer_flags[r] = reinterpret_cast<uint32_t *>(t.peer[r] + flags) + t.rank;
+    }
+    p.ticket = t.tickets + (prompt ? 2 * m->L : 0) + index;
+    p.epoch = t.epoch;
+    p.error = m->d_error;
+    return p;
+}
+
+TpArg tp_arg(DModel *m) {
+    const TpState &t = m->tp;
+    TpArg a{};
+    a.tp = t.size;
+    a.rank = t.rank;
+    a.slots = reinterpret_cast<uint32_t *>(t.xbuf + t.off_args);
+    for (uint32_t r = 0; r < t.size; ++r) a.peer_slots[r] = reinterpret_cast<uint32_t *>(t.peer[r] + t.off_args);
+    a.epoch = t.epoch;
+    a.error = m->d_error;
+    return a;
+}
+
+// Greedy token of one row from the head's per-block candidates: the local
+// merge, then (tensor-parallel) the first maximum over the ranks' slices.
+bool greedy_choice(plamo_cuda *c, DModel *m, uint32_t grid) {
+    const bool tp = m->tp.active;
+    if (!launch(c, argmax_merge_kernel, dim3(1), dim3(256), 0, static_cast<const float *>(m->arg_val),
+                static_cast<const uint32_t *>(m->arg_idx), static_cast<const uint32_t *>(m->arg_nan), grid,
+                tp ? m->tp.lidx : m->d_next, tp ? nullptr : m->d_token, tp ? m->tp.lval : nullptr))
+        return false;
+    if (!tp) return true;
+    return launch(c, tp_argmax_kernel, dim3(1), dim3(32), 0, static_cast<const float *>(m->tp.lval),
+                  static_cast<const uint32_t *>(m->tp.lidx), 1u, static_cast<uint32_t>(m->tp.voff), tp_arg(m),
+                  m->d_next, m->d_token);
+}
+
+// Prompt all-reduce of a [T][H] partial block in place.
+bool tp_allreduce_rows(plamo_cuda *c, DModel *m, float *rows, uint64_t T, uint64_t index) {
+    const TpPoint t = tp_point(m, true, index);
+    const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>((T * m->H / 4 + 255) / 256, c->sm_count * 2ull));
+    return launch(c, tp_push_kernel, dim3(grid), dim3(256), 0, static_cast<const float *>(rows), T * m->H, t) &&
+           launch(c, tp_sum_kernel, dim3(grid), dim3(256), 0, rows, T * m->H, t);
+}
+
 bool record_decode(plamo_cuda *c, DModel *m) {
     int s = 0;
     for (uint64_t l = 0; l < m->L; ++l) {
@@ -620,6 +699,10 @@ bool record_decode(plamo_cuda *c, DModel *m) {
             p.off1 = kPostMlpOffset;
             p.state_out = m->state[s ^ 1];
             s ^= 1;
+            if (m->tp.active) {
+                p.tp_role = 1;
+                p.tp = tp_point(m, false, 2 * (l - 1) + 1);
+            }
             ok = gemv<PRO_RESID_NORM, EPI_STORE>(c, p);
         }
         if (!ok) return false;
@@ -630,6 +713,10 @@ bool record_decode(plamo_cuda *c, DModel *m) {
         o.cols = m->AW;
         o.x = m->attn;
         o.y = m->branch;
+        if (m->tp.active) {
+            o.tp_role = 2;
+            o.tp = tp_point(m, false, 2 * l);
+        }
         if (!gemv<PRO_X, EPI_STORE>(c, o)) return false;
         GemvParams g{};
         g.w = L.gu;
@@ -644,6 +731,10 @@ bool record_decode(plamo_cuda *c, DModel *m) {
         g.state_out = m->state[s ^ 1];
         s ^= 1;
         g.y = m->mid;
+        if (m->tp.active) {
+            g.tp_role = 1;
+            g.tp = tp_point(m, false, 2 * l);
+        }
         if (!gemv<PRO_RESID_NORM, EPI_SWIGLU>(c, g)) return false;
         GemvParams d{};
         d.w = L.down;
@@ -651,11 +742,15 @@ bool record_decode(plamo_cuda *c, DModel *m) {
         d.cols = m->I;
         d.x = m->mid;
         d.y = m->branch;
+        if (m->tp.active) {
+            d.tp_role = 2;
+            d.tp = tp_point(m, false, 2 * l + 1);
+        }
         if (!gemv<PRO_X, EPI_STORE>(c, d)) return false;
     }
     GemvParams h{};
     h.w = m->head;
-    h.rows = m->V;
+    h.rows = m->Vh;
     h.cols = m->H;
     h.state_in = m->state[s];
     h.branch = m->branch;
@@ -670,13 +765,15 @@ bool record_decode(plamo_cuda *c, DModel *m) {
     h.arg_val = m->arg_val;
     h.arg_idx = m->arg_idx;
     h.arg_nan = m->arg_nan;
+    if (m->tp.active) {
+        h.tp_role = 1;
+        h.tp = tp_point(m, false, 2 * m->L - 1);
+    }
     uint32_t grid = 0;
     if (!gemv<PRO_RESID_NORM, EPI_ARGMAX>(c, h, &grid)) return false;
-    if (!launch(c, argmax_merge_kernel, dim3(1), dim3(256), 0, static_cast<const float *>(m->arg_val),
-                static_cast<const uint32_t *>(m->arg_idx), static_cast<const uint32_t *>(m->arg_nan), grid,
-                m->d_next, m->d_token))
-        return false;
-    return launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended, m->L, uint64_t{1});
+    if (!greedy_choice(c, m, grid)) return false;
+    if (!launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended, m->L, uint64_t{1})) return false;
+    return !m->tp.active || launch(c, tp_epoch_kernel, dim3(1), dim3(32), 0, m->tp.epoch);
 }
 
 bool ensure_graph(plamo_cuda *c, DModel *m) {
@@ -710,7 +807,10 @@ bool check_device_error(plamo_cuda *c, DModel *m) {
     if (err) {
         cudaMemset(m->d_error, 0, 4);
         c->info.errors++;
-        snprintf(c->info.note, sizeof c->info.note, "device rejected a token id");
+        snprintf(c->info.note, sizeof c->info.note, "%s",
+                 err == 1   ? "device rejected a token id"
+                 : err == 4 ? "a tensor-parallel peer did not arrive within 2 s"
+                            : "a weight stream stalled for 2 s");
         return false;
     }
     return true;
@@ -791,6 +891,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
                 return false;
         }
         if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
+        if (m->tp.active && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l)) return false;
         if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(256), 0, m->p_states,
                     static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H))
             return false;
@@ -799,6 +900,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
                     m->p_gu, m->I, T))
             return false;
         if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
+        if (m->tp.active && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l + 1)) return false;
     }
     if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(256), 0, m->p_states,
                 static_cast<const float *>(m->p_branch), m->layers[m->L - 1].mpost, kPostMlpOffset,
@@ -809,13 +911,13 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
                     static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, m->norm,
                     1.0f, m->p_norm, H))
             return false;
-        return projection(c, m, m->p_norm, H, m->head, m->p_logits, m->V, T, m->V, H);
+        return projection(c, m, m->p_norm, H, m->head, m->p_logits, m->Vh, T, m->Vh, H);
     }
     // Final norm and head for the last prompt token only (reference
     // src/prefill.s:136-158), with the greedy choice on the device.
     GemvParams h{};
     h.w = m->head;
-    h.rows = m->V;
+    h.rows = m->Vh;
     h.cols = H;
     h.state_in = m->p_states + (T - 1) * H;
     h.norm2 = m->norm;
@@ -828,11 +930,9 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
     h.arg_nan = m->arg_nan;
     uint32_t grid = 0;
     if (!gemv<PRO_NORM, EPI_ARGMAX>(c, h, &grid)) return false;
-    if (!launch(c, argmax_merge_kernel, dim3(1), dim3(256), 0, static_cast<const float *>(m->arg_val),
-                static_cast<const uint32_t *>(m->arg_idx), static_cast<const uint32_t *>(m->arg_nan), grid,
-                m->d_next, m->d_token))
-        return false;
-    return launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended, m->L, T);
+    if (!greedy_choice(c, m, grid)) return false;
+    if (!launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended, m->L, T)) return false;
+    return !m->tp.active || launch(c, tp_epoch_kernel, dim3(1), dim3(32), 0, m->tp.epoch);
 }
 
 bool copy_outputs(plamo_cuda *c, DModel *m) {
@@ -840,7 +940,8 @@ bool copy_outputs(plamo_cuda *c, DModel *m) {
     return note(c, "state", cudaMemcpyAsync(h->state, m->final_state, m->H * 4, cudaMemcpyDeviceToHost, c->stream)) &&
            note(c, "normalized", cudaMemcpyAsync(h->normalized, m->normalized, m->H * 4, cudaMemcpyDeviceToHost,
                                                  c->stream)) &&
-           note(c, "logits", cudaMemcpyAsync(h->logits, m->logits, m->V * 4, cudaMemcpyDeviceToHost, c->stream));
+           note(c, "logits", cudaMemcpyAsync(h->logits + m->tp.voff, m->logits, m->Vh * 4, cudaMemcpyDeviceToHost,
+                                             c->stream));
 }
 
 bool sync_kv(plamo_cuda *c, DModel *m);
@@ -991,6 +1092,34 @@ int plamo_cuda_preload_synthetic(struct plamo_cuda *c, const void *host_key, uin
     return 1;
 }
 
+int plamo_cuda_preload_synthetic_rows(struct plamo_cuda *c, const void *host_key, uint64_t cols, uint64_t full_cols,
+                                      uint64_t col0, const uint64_t *row_start, const uint64_t *row_count,
+                                      unsigned segments, uint64_t seed, float mean, float std) {
+    if (!c || !host_key || !cols || col0 + cols > full_cols || !row_start || !row_count || !segments) return 0;
+    uint64_t rows = 0;
+    for (unsigned i = 0; i < segments; ++i) rows += row_count[i];
+    if (!rows) return 0;
+    cudaSetDevice(c->device);
+    char *dev = nullptr;
+    if (!note(c, "synthetic alloc", cudaMalloc(&dev, rows * cols * 2))) return 0;
+    uint16_t *dst = reinterpret_cast<uint16_t *>(dev);
+    for (unsigned i = 0; i < segments; ++i) {
+        if (!row_count[i]) continue;
+        fill_synthetic_rows_kernel<<<c->sm_count * 8, 256, 0, c->stream>>>(dst, row_count[i], cols, seed,
+                                                                          row_start[i], col0, full_cols, mean, std);
+        c->info.launches++;
+        dst += row_count[i] * cols;
+    }
+    if (!note(c, "synthetic", cudaGetLastError()) || !note(c, "synthetic", cudaStreamSynchronize(c->stream))) {
+        cudaFree(dev);
+        return 0;
+    }
+    c->ranges.push_back({reinterpret_cast<uintptr_t>(host_key), rows * cols * 2, dev});
+    c->info.weight_bytes += rows * cols * 2;
+    c->info.allocated_bytes += rows * cols * 2;
+    return 1;
+}
+
 int plamo_cuda_fill_synthetic_bf16(struct plamo_cuda *c, uint16_t *dst, uint64_t count, uint64_t seed, float mean,
                                    float std) {
     if (!c) return 0;
@@ -1017,11 +1146,15 @@ int plamo_cuda_warm_cache(struct plamo_cuda *c) {
     return note(c, "warm", cudaStreamSynchronize(c->stream));
 }
 
-int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
-    if (!c || !model || !model->count || !model->hidden || !model->vocab || !model->layers) return 0;
+// Device state of `model` whose head holds `head_rows` rows (the vocabulary,
+// or a tensor-parallel rank's slice of it).
+static int prepare_impl(struct plamo_cuda *c, struct model *model, uint64_t head_rows) {
+    if (!c || !model || !model->count || !model->hidden || !model->vocab || !model->layers || !head_rows ||
+        head_rows > model->vocab)
+        return 0;
     cudaSetDevice(c->device);
     if (DModel *old = find_model(c, model)) {
-        if (old->signature == model_signature(model)) return 1;
+        if (old->signature == model_signature(model) && old->Vh == head_rows && !old->tp.size) return 1;
         // Another descriptor now lives at this address: drop the stale state.
         cudaStreamSynchronize(c->stream);
         free_model(c, old);
@@ -1037,6 +1170,7 @@ int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     m->D = q0->dim;
     m->I = model->layers[0]->mlp->intermediate;
     m->V = model->vocab;
+    m->Vh = head_rows;
     m->L = model->count;
     m->QW = (m->QH + 2 * m->KH) * m->D;
     m->AW = m->QH * m->D;
@@ -1047,7 +1181,7 @@ int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     }
     const uint64_t H = m->H;
     m->emb = resolve(c, model->embedding, m->V * H * 2, true);
-    m->head = resolve(c, model->head, m->V * H * 2, true);
+    m->head = resolve(c, model->head, m->Vh * H * 2, true);
     m->norm = resolve(c, model->norm, H * 2, true);
     if (!m->emb || !m->head || !m->norm) return 0;
     m->d_appended = static_cast<uint64_t *>(dalloc(c, m.get(), m->L * 8));
@@ -1101,7 +1235,7 @@ int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     m->state[1] = static_cast<float *>(dalloc(c, m.get(), H * 4));
     m->final_state = m->state[0];
     m->normalized = static_cast<float *>(dalloc(c, m.get(), H * 4));
-    m->logits = static_cast<float *>(dalloc(c, m.get(), m->V * 4));
+    m->logits = static_cast<float *>(dalloc(c, m.get(), m->Vh * 4));
     m->qkv = static_cast<float *>(dalloc(c, m.get(), m->QW * 4));
     m->q = static_cast<float *>(dalloc(c, m.get(), m->AW * 4));
     m->attn = static_cast<float *>(dalloc(c, m.get(), m->AW * 4));
@@ -1127,7 +1261,7 @@ int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     m->p_attn = static_cast<float *>(dalloc(c, m.get(), T * m->AW * 4));
     m->p_branch = static_cast<float *>(dalloc(c, m.get(), T * H * 4));
     m->p_gu = static_cast<float *>(dalloc(c, m.get(), T * 2 * m->I * 4));
-    m->p_logits = static_cast<float *>(dalloc(c, m.get(), kVerifyMax * m->V * 4));
+    m->p_logits = static_cast<float *>(dalloc(c, m.get(), kVerifyMax * m->Vh * 4));
     m->p_part = static_cast<float *>(dalloc(c, m.get(), kVerifyMax * m->QH * m->splits * (m->D + 2) * 4));
     m->p_tickets = static_cast<uint32_t *>(dalloc(c, m.get(), T * m->KH * 4));
     m->p_ids = static_cast<uint32_t *>(dalloc(c, m.get(), T * 4));
@@ -1145,6 +1279,86 @@ int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
     }
     if (!note(c, "prepare", cudaStreamSynchronize(c->stream))) return 0;
     c->models[model] = std::move(m);
+    return 1;
+}
+
+int plamo_cuda_prepare_model(struct plamo_cuda *c, struct model *model) {
+    return model ? prepare_impl(c, model, model->vocab) : 0;
+}
+
+int plamo_cuda_tp_prepare(struct plamo_cuda *c, struct model *model, unsigned rank, unsigned size,
+                          uint64_t vocab_offset, uint64_t vocab_rows, struct plamo_cuda_tp_handle *handle) {
+    if (!c || !model || !handle || size < 2 || size > kTpMax || rank >= size || !vocab_rows ||
+        vocab_offset + vocab_rows > model->vocab || vocab_offset + vocab_rows > 0xffffffffull)
+        return 0;
+    cudaSetDevice(c->device);
+    if (DModel *old = find_model(c, model)) {  // always a fresh shard
+        cudaStreamSynchronize(c->stream);
+        free_model(c, old);
+        c->models.erase(model);
+    }
+    if (prepare_impl(c, model, vocab_rows) != 1) return 0;
+    DModel *m = find_model(c, model);
+    if (m->H % 4) {
+        snprintf(c->info.note, sizeof c->info.note, "tensor parallelism needs hidden %% 4 == 0");
+        return 0;
+    }
+    TpState &t = m->tp;
+    t.rank = rank;
+    t.size = size;
+    t.voff = vocab_offset;
+    auto align = [](uint64_t x) { return (x + 255) & ~uint64_t{255}; };
+    uint64_t off = 0;
+    t.off_dparts = off;
+    off = align(off + 2 * m->L * size * m->H * 4);
+    t.off_dflags = off;
+    off = align(off + 2 * m->L * size * 4);
+    t.off_pparts = off;
+    off = align(off + 2 * size * m->tmax * m->H * 4);
+    t.off_pflags = off;
+    off = align(off + 2 * m->L * size * 4);
+    t.off_args = off;
+    off = align(off + kVerifyMax * size * 16);
+    t.bytes = off;
+    t.xbuf = static_cast<char *>(dalloc(c, m, t.bytes));
+    t.tickets = static_cast<uint32_t *>(dalloc(c, m, 4 * m->L * 4));
+    t.epoch = static_cast<uint32_t *>(dalloc(c, m, 4));
+    t.lval = static_cast<float *>(dalloc(c, m, kVerifyMax * 4));
+    t.lidx = static_cast<uint32_t *>(dalloc(c, m, kVerifyMax * 4));
+    if (!t.xbuf || !t.tickets || !t.epoch || !t.lval || !t.lidx) return 0;
+    c->info.workspace_bytes += t.bytes;
+    cudaIpcMemHandle_t h{};
+    if (!note(c, "tp handle", cudaIpcGetMemHandle(&h, t.xbuf))) return 0;
+    static_assert(sizeof h <= sizeof handle->bytes, "IPC handle size");
+    memset(handle->bytes, 0, sizeof handle->bytes);
+    memcpy(handle->bytes, &h, sizeof h);
+    return 1;
+}
+
+int plamo_cuda_tp_connect(struct plamo_cuda *c, struct model *model, const struct plamo_cuda_tp_handle *handles) {
+    if (!c || !model || !handles) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || !m->tp.size || m->tp.active) return 0;
+    TpState &t = m->tp;
+    for (uint32_t r = 0; r < t.size; ++r) {
+        if (r == t.rank) {
+            t.peer[r] = t.xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h{};
+        memcpy(&h, handles[r].bytes, sizeof h);
+        void *p = nullptr;
+        if (!note(c, "tp open", cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess))) return -1;
+        t.peer[r] = static_cast<char *>(p);
+    }
+    t.active = true;
+    if (m->graph_exec) {  // re-record with the exchanges
+        cudaGraphExecDestroy(m->graph_exec);
+        cudaGraphDestroy(m->graph);
+        m->graph_exec = nullptr;
+        m->graph = nullptr;
+    }
     return 1;
 }
 
@@ -1272,8 +1486,14 @@ int plamo_cuda_verify(struct plamo_cuda *c, struct model *model, const uint32_t 
     if (!note(c, "ids", cudaMemcpyAsync(m->p_ids, ids, tokens * 4, cudaMemcpyHostToDevice, c->stream))) return -1;
     cudaEventRecord(c->ev0, c->stream);
     if (!record_prompt(c, m, tokens, 1, true)) return -1;
-    if (!launch(c, rows_argmax_kernel, dim3(tokens), dim3(256), 0, static_cast<const float *>(m->p_logits), m->V,
-                m->p_next))
+    const bool tp = m->tp.active;
+    if (!launch(c, rows_argmax_kernel, dim3(tokens), dim3(256), 0, static_cast<const float *>(m->p_logits), m->Vh,
+                tp ? m->tp.lidx : m->p_next, tp ? m->tp.lval : nullptr))
+        return -1;
+    if (tp && (!launch(c, tp_argmax_kernel, dim3(1), dim3(32), 0, static_cast<const float *>(m->tp.lval),
+                       static_cast<const uint32_t *>(m->tp.lidx), static_cast<uint32_t>(tokens),
+                       static_cast<uint32_t>(m->tp.voff), tp_arg(m), m->p_next, static_cast<uint32_t *>(nullptr)) ||
+               !launch(c, tp_epoch_kernel, dim3(1), dim3(32), 0, m->tp.epoch)))
         return -1;
     cudaEventRecord(c->ev1, c->stream);
     if (!note(c, "verify next", cudaMemcpyAsync(c->pinned_u32 + 16, m->p_next, tokens * 4, cudaMemcpyDeviceToHost,
@@ -1316,7 +1536,7 @@ int plamo_cuda_commit(struct plamo_cuda *c, struct model *model, uint64_t index)
                                                  cudaMemcpyDeviceToHost, c->stream)) ||
         !note(c, "commit norm", cudaMemcpyAsync(h->normalized, m->p_norm + index * m->H, m->H * 4,
                                                 cudaMemcpyDeviceToHost, c->stream)) ||
-        !note(c, "commit logits", cudaMemcpyAsync(h->logits, m->p_logits + index * m->V, m->V * 4,
+        !note(c, "commit logits", cudaMemcpyAsync(h->logits + m->tp.voff, m->p_logits + index * m->Vh, m->Vh * 4,
                                                   cudaMemcpyDeviceToHost, c->stream)) ||
         !note(c, "commit", cudaStreamSynchronize(c->stream)))
         return -1;
@@ -1348,7 +1568,7 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
     if (!c || !state) return 0;
     cudaSetDevice(c->device);
     DModel *m = find_model(c, model);
-    if (!m || index >= m->L) {
+    if (!m || index >= m->L || m->tp.size) {
         c->info.declines++;
         return 0;
     }

@@ -21,6 +21,7 @@
 //     projection overlaps the tail of the previous kernel.
 #pragma once
 #include "common.cuh"
+#include "tp.cuh"
 
 namespace plamo {
 
@@ -47,6 +48,11 @@ struct GemvParams {
     uint32_t *arg_idx;            // ARGMAX: per-block best index
     uint32_t *arg_nan;            // ARGMAX: per-block NaN flag
     uint32_t *error;              // set to nonzero on an invalid token
+    // Tensor parallelism: role 1 = the prologue's branch is the rank-ordered
+    // sum of the point's partials (PRO_RESID_NORM); role 2 = the STORE
+    // epilogue pushes its rows into every rank's slot of the point.
+    int tp_role;
+    TpPoint tp;
 };
 
 constexpr int kGemvThreads = 512;
@@ -123,13 +129,18 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
         const uint32_t n4 = static_cast<uint32_t>(n / 4);
         float4 st[kPV], br[kPV];
         uint2 w1[kPV];
+        const bool reduce = PRO == PRO_RESID_NORM && p.tp_role == 1;
+        if (reduce) {
+            if (threadIdx.x == 0) tp_wait_flags(p.tp);
+            __syncthreads();
+        }
 #pragma unroll
         for (int k = 0; k < kPV; ++k) {
             const uint32_t i = threadIdx.x + k * nt;
             if (i < n4) {
                 st[k] = ld4(p.state_in + 4 * i);
                 if (PRO == PRO_RESID_NORM) {
-                    br[k] = ld4(p.branch + 4 * i);
+                    br[k] = reduce ? tp_sum4(p.tp, 4 * i) : ld4(p.branch + 4 * i);
                     w1[k] = *reinterpret_cast<const uint2 *>(p.norm1 + 4 * i);
                 }
             }
@@ -175,14 +186,21 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
     } else if (PRO == PRO_NORM) {
         for (uint64_t i = threadIdx.x; i < n; i += nt) xs[i] = p.state_in[i];
     } else {  // PRO_RESID_NORM, any length: state + rmsnorm(branch, norm1, off1)
+        const bool reduce = p.tp_role == 1;
+        if (reduce) {
+            if (threadIdx.x == 0) tp_wait_flags(p.tp);
+            __syncthreads();
+        }
         float s = 0.0f;
         for (uint64_t i = threadIdx.x; i < n; i += nt) {
-            const float b = p.branch[i];
+            const float b = reduce ? tp_sum1(p.tp, i) : p.branch[i];
             s += b * b;
         }
         const float inv = rms_inverse(block_sum(s, red), n);
-        for (uint64_t i = threadIdx.x; i < n; i += nt)
-            xs[i] = __fadd_rn(p.state_in[i], rms_apply(p.branch[i], inv, p.norm1[i], p.off1));
+        for (uint64_t i = threadIdx.x; i < n; i += nt) {
+            const float b = reduce ? tp_sum1(p.tp, i) : p.branch[i];
+            xs[i] = __fadd_rn(p.state_in[i], rms_apply(b, inv, p.norm1[i], p.off1));
+        }
     }
     __syncthreads();
     float s = 0.0f;
@@ -228,6 +246,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
         const uint64_t unit = u0 + u;
         if (EPI == EPI_SWIGLU) {
             p.y[unit] = swiglu(t0, t1);
+        } else if (EPI == EPI_STORE && p.tp_role == 2) {
+            for (uint32_t r = 0; r < p.tp.tp; ++r) p.tp.peer_parts[r][unit] = t0;
         } else {
             p.y[unit] = t0;
             if (EPI == EPI_ARGMAX) {
@@ -239,6 +259,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
             }
         }
     }
+    if (EPI == EPI_STORE && p.tp_role == 2) tp_signal(p.tp);
     if (EPI == EPI_ARGMAX) {
         if (threadIdx.x == 0) any_nan = 0;
         __syncthreads();
@@ -559,7 +580,7 @@ inline size_t gemv_bulk_smem(uint64_t cols, uint64_t rows_per_block, int pair, i
 // (reference src/token.s:35-63). Writes the winner to *out and, when given,
 // to the next decode step's token slot.
 __global__ void argmax_merge_kernel(const float *val, const uint32_t *idx, const uint32_t *nan_flag,
-                                    uint32_t blocks, uint32_t *out, uint32_t *next_token) {
+                                    uint32_t blocks, uint32_t *out, uint32_t *next_token, float *out_val) {
     __shared__ float sv[32];
     __shared__ uint32_t si[32];
     __shared__ uint32_t sn[32];
@@ -601,11 +622,12 @@ __global__ void argmax_merge_kernel(const float *val, const uint32_t *idx, const
         const uint32_t result = nan_seen ? 0xffffffffu : bi;
         *out = result;
         if (next_token) *next_token = result;
+        if (out_val) *out_val = bv;
     }
 }
 
 // Greedy choice of every row of a [rows][n] logits block (verification).
-__global__ void rows_argmax_kernel(const float *logits, uint64_t n, uint32_t *out) {
+__global__ void rows_argmax_kernel(const float *logits, uint64_t n, uint32_t *out, float *out_val) {
     __shared__ float sv[32];
     __shared__ uint32_t si[32];
     __shared__ uint32_t sn[32];
@@ -647,6 +669,7 @@ __global__ void rows_argmax_kernel(const float *logits, uint64_t n, uint32_t *ou
             }
         }
         out[blockIdx.x] = nan_seen ? 0xffffffffu : bi;
+        if (out_val) out_val[blockIdx.x] = bv;
     }
 }
 

@@ -122,6 +122,18 @@ __global__ void fill_synthetic_bf16_kernel(uint16_t *dst, uint64_t count, uint64
         dst[i] = plamo_synthetic_bf16(seed, i, mean, std);
 }
 
+// Rows [row0, row0+rows) x columns [col0, col0+cols) of the synthetic
+// [*, full_cols] tensor `seed`, packed as [rows][cols].
+__global__ void fill_synthetic_rows_kernel(uint16_t *dst, uint64_t rows, uint64_t cols, uint64_t seed, uint64_t row0,
+                                           uint64_t col0, uint64_t full_cols, float mean, float std) {
+    const uint64_t count = rows * cols;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t r = i / cols, col = i - r * cols;
+        dst[i] = plamo_synthetic_bf16(seed, (row0 + r) * full_cols + col0 + col, mean, std);
+    }
+}
+
 __global__ void fill_synthetic_f32_kernel(float *dst, uint64_t count, uint64_t seed, float mean,
                                           float std) {
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < count;

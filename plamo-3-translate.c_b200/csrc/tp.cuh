@@ -1,0 +1,189 @@
+// Tensor-parallel exchange over peer memory (NVLink P2P through CUDA IPC
+// mappings; plain loads and stores, no multicast, no library collective).
+//
+// A tensor-parallel PLaMo-3 block ends in a row-split projection (o_proj over
+// this rank's heads, down_proj over this rank's MLP rows) whose output is a
+// partial sum of the hidden vector. Every rank owns an exchange buffer; for
+// each exchange point it holds one partial vector per source rank and one
+// flag per source rank. The producing projection stores its output rows
+// straight into slot `rank` of every peer's buffer (its own included) from
+// its epilogue, so the transfer overlaps the rest of the projection; the last
+// CTA to finish raises this rank's flag at every peer. The consuming kernel
+// (the next projection's prologue, or a row kernel for prompts) waits for
+// every rank's flag of the current epoch and sums the partials in rank order,
+// so every rank computes the same bits.
+//
+// Epochs: a device counter, advanced once at the end of every tensor-parallel
+// operation (decode step, prompt, verification) on every rank; a flag holds
+// epoch + 1 of the operation that raised it, so buffers and flags are reused
+// without resets. Every wait is bounded (2 s of %globaltimer): on timeout the
+// kernel records an error and continues with whatever is in the buffer.
+#pragma once
+#include "common.cuh"
+
+namespace plamo {
+
+constexpr int kTpMax = 8;
+
+struct TpPoint {
+    uint32_t tp;                    // ranks; 0 = not tensor-parallel
+    uint64_t stride;                // floats between source slots of `parts`
+    const float *parts;             // local [tp][stride] partials, slot r from rank r
+    const uint32_t *flags;          // local [tp] flag raised by each source rank
+    float *peer_parts[kTpMax];      // slot `rank` of every rank's parts
+    uint32_t *peer_flags[kTpMax];   // flag `rank` of every rank's flags
+    uint32_t *ticket;               // local CTA arrival counter of this point
+    const uint32_t *epoch;          // local epoch counter
+    uint32_t *error;                // set to 4 when a peer never arrived
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// One thread: wait until every rank's flag of this point shows the current
+// epoch. Returns false after ~2 s (error recorded).
+__device__ __forceinline__ bool tp_wait_flags(const TpPoint &t) {
+    const uint32_t want = *t.epoch + 1;
+    uint64_t start = 0;
+    for (uint32_t r = 0; r < t.tp; ++r) {
+        while (ld_acquire_sys(t.flags + r) != want) {
+            if (!start) start = global_ns();
+            else if (global_ns() - start > 2000000000ull) {
+                if (t.error) atomicExch(t.error, 4u);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Called by every thread of a producing CTA after its stores to the peers:
+// the last CTA of the grid raises this rank's flag at every peer.
+__device__ __forceinline__ void tp_signal(const TpPoint &t) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(t.ticket, 1u) == gridDim.x - 1) {
+            *t.ticket = 0;
+            __threadfence_system();
+            const uint32_t flag = *t.epoch + 1;
+            for (uint32_t r = 0; r < t.tp; ++r) st_release_sys(t.peer_flags[r], flag);
+        }
+    }
+}
+
+// Rank-ordered sum of the 4 floats at `i` of every source slot (L2 loads:
+// the rows arrive from other GPUs, L1 may hold the previous epoch's).
+__device__ __forceinline__ float4 tp_sum4(const TpPoint &t, uint64_t i) {
+    float4 s = __ldcg(reinterpret_cast<const float4 *>(t.parts + i));
+    for (uint32_t r = 1; r < t.tp; ++r) {
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(t.parts + r * t.stride + i));
+        s = make_float4(__fadd_rn(s.x, v.x), __fadd_rn(s.y, v.y), __fadd_rn(s.z, v.z), __fadd_rn(s.w, v.w));
+    }
+    return s;
+}
+__device__ __forceinline__ float tp_sum1(const TpPoint &t, uint64_t i) {
+    float s = __ldcg(t.parts + i);
+    for (uint32_t r = 1; r < t.tp; ++r) s = __fadd_rn(s, __ldcg(t.parts + r * t.stride + i));
+    return s;
+}
+
+// Prompt all-reduce, push half: copy n floats of this rank's partial rows
+// into slot `rank` of every peer (n % 4 == 0, 16-byte aligned), then signal.
+__global__ void tp_push_kernel(const float *src, uint64_t n, TpPoint t) {
+    pdl_wait();
+    const uint64_t n4 = n / 4;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4 *>(src)[i];
+        for (uint32_t r = 0; r < t.tp; ++r) reinterpret_cast<float4 *>(t.peer_parts[r])[i] = v;
+    }
+    tp_signal(t);
+}
+
+// Prompt all-reduce, sum half: dst = rank-ordered sum of every slot.
+__global__ void tp_sum_kernel(float *dst, uint64_t n, TpPoint t) {
+    pdl_wait();
+    if (threadIdx.x == 0) tp_wait_flags(t);
+    __syncthreads();
+    const uint64_t n4 = n / 4;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        reinterpret_cast<float4 *>(dst)[i] = tp_sum4(t, 4 * i);
+    pdl_launch_dependents();
+}
+
+// Greedy token across the ranks' head slices. Slot layout per source rank:
+// {value, global index, flag, pad}; index UINT32_MAX marks a NaN on that rank.
+struct TpArg {
+    uint32_t tp, rank;
+    uint32_t *slots;            // local [rows][tp][4]
+    uint32_t *peer_slots[kTpMax];  // every rank's [rows][tp][4] (slot `rank` is written)
+    const uint32_t *epoch;
+    uint32_t *error;
+};
+
+// rows = 1 (decode / prefill) or the candidates of a verification. Input:
+// this rank's per-row best (value, local index) and the head slice offset.
+// Output: the first maximal global index of every row, UINT32_MAX on NaN.
+__global__ void tp_argmax_kernel(const float *val, const uint32_t *idx, uint32_t rows, uint32_t offset, TpArg a,
+                                 uint32_t *out, uint32_t *next_token) {
+    pdl_wait();
+    const uint32_t flag = *a.epoch + 1;
+    for (uint32_t row = threadIdx.x; row < rows; row += blockDim.x) {
+        const uint32_t li = idx[row];
+        const uint32_t gi = li == 0xffffffffu ? li : li + offset;
+        const uint32_t vbits = __float_as_uint(val[row]);
+        for (uint32_t r = 0; r < a.tp; ++r) {
+            uint32_t *s = a.peer_slots[r] + (static_cast<size_t>(row) * a.tp + a.rank) * 4;
+            s[0] = vbits;
+            s[1] = gi;
+            st_release_sys(s + 2, flag);
+        }
+    }
+    __syncthreads();
+    for (uint32_t row = threadIdx.x; row < rows; row += blockDim.x) {
+        float bv = -__int_as_float(0x7f800000);
+        uint32_t bi = 0xffffffffu;
+        bool nan_seen = false;
+        const uint64_t start = global_ns();
+        for (uint32_t r = 0; r < a.tp; ++r) {
+            const uint32_t *s = a.slots + (static_cast<size_t>(row) * a.tp + r) * 4;
+            bool arrived = true;
+            while (ld_acquire_sys(s + 2) != flag)
+                if (global_ns() - start > 2000000000ull) {
+                    if (a.error) atomicExch(a.error, 4u);
+                    arrived = false;
+                    break;
+                }
+            if (!arrived) {
+                nan_seen = true;
+                break;
+            }
+            const float v = __uint_as_float(__ldcg(s));
+            const uint32_t i = __ldcg(s + 1);
+            if (i == 0xffffffffu) nan_seen = true;
+            else if (v > bv || (v == bv && i < bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+        const uint32_t result = nan_seen ? 0xffffffffu : bi;
+        out[row] = result;
+        if (next_token) *next_token = result;
+    }
+}
+
+// Advance the epoch (last kernel of every tensor-parallel operation).
+__global__ void tp_epoch_kernel(uint32_t *epoch) {
+    pdl_wait();
+    if (threadIdx.x == 0) *epoch += 1;
+}
+
+}  // namespace plamo

@@ -12,7 +12,7 @@ a host blob (uploaded by plamo_cuda_preload) or generated directly in HBM
 """
 import ctypes
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 
 import numpy as np
 
@@ -142,6 +142,54 @@ def default_layer_specs(p, full_capacity=None):
         else:
             specs.append(LayerSpec(True, p.window + 1, local, 1.0))
     return specs
+
+
+def tp_shard_profile(p, size):
+    """Profile of one tensor-parallel rank's shard: qh/size query heads,
+    kh/size KV heads and intermediate/size MLP rows; hidden size, layers,
+    vocabulary and the attention pattern are the full model's."""
+    if p.qh % size or p.kh % size or p.inter % size:
+        raise ValueError(f"{p.name}: heads {p.qh}/{p.kh} and intermediate {p.inter} must split {size} ways")
+    return replace(p, name=f"{p.name}-tp{size}", qh=p.qh // size, kh=p.kh // size, inter=p.inter // size)
+
+
+def tp_vocab_slice(vocab, size, rank):
+    """(first row, rows) of rank's head slice: ceil(vocab/size) rows each, the
+    last rank takes the rest."""
+    per = -(-vocab // size)
+    first = min(rank * per, vocab)
+    return first, min(per, vocab - first)
+
+
+def tp_segments(full, size, rank, name):
+    """How a rank's shard of tensor `name` is cut from the full model's tensor:
+    (cols, full_cols, col0, [(row_start, row_count), ...]) or None when the
+    tensor is replicated. Rank r holds query heads [r*qh/size, ...), KV heads
+    [r*kh/size, ...) (Q, K and V row blocks of qkv_proj), the matching o_proj
+    columns, gate and up rows [r*I/size, ...) and the matching down_proj
+    columns."""
+    d, h = full.dim, full.hidden
+    qr, kr, ir = full.qh // size, full.kh // size, full.inter // size
+    if name.endswith("mixer.qkv_proj.weight"):
+        return h, h, 0, [(rank * qr * d, qr * d), (full.qh * d + rank * kr * d, kr * d),
+                         ((full.qh + full.kh) * d + rank * kr * d, kr * d)]
+    if name.endswith("mixer.o_proj.weight"):
+        return qr * d, full.qh * d, rank * qr * d, [(0, h)]
+    if name.endswith("mlp.gate_up_proj.weight"):
+        return h, h, 0, [(rank * ir, ir), (full.inter + rank * ir, ir)]
+    if name.endswith("mlp.down_proj.weight"):
+        return ir, full.inter, rank * ir, [(0, h)]
+    return None
+
+
+def tp_all_gather_handles(handle, group=None):
+    """Every rank's exchange-buffer handle, indexed by rank, through the
+    caller's torch.distributed process group (any backend: the handles are
+    64-byte host records)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    return out
 
 
 def _align(n, a=256):
@@ -356,6 +404,44 @@ class Backend:
             if not self.lib.plamo_cuda_preload_synthetic(self.ctx, addr, count,
                                                          seed * 1000003 + k, mean, s):
                 raise RuntimeError(self.info().note.decode())
+
+    def preload_synthetic_tp(self, hm, full, rank, size, seed, std=0.02):
+        """Synthetic weights of a tensor-parallel shard `hm` (built from
+        tp_shard_profile(full, size)): every tensor is the rank's cut of the
+        tensor preload_synthetic generates for the full model, bit for bit."""
+        for k, (addr, count, name) in enumerate(hm.tensor_ranges()):
+            mean, s = synthetic_parameters(name, std)
+            cut = tp_segments(full, size, rank, name)
+            if cut is None:
+                ok = self.lib.plamo_cuda_preload_synthetic(self.ctx, addr, count, seed * 1000003 + k, mean, s)
+            else:
+                cols, full_cols, col0, segs = cut
+                starts = (ctypes.c_uint64 * len(segs))(*[a for a, _ in segs])
+                counts = (ctypes.c_uint64 * len(segs))(*[b for _, b in segs])
+                assert sum(b for _, b in segs) * cols == count, name
+                ok = self.lib.plamo_cuda_preload_synthetic_rows(self.ctx, addr, cols, full_cols, col0, starts,
+                                                                counts, len(segs), seed * 1000003 + k, mean, s)
+            if not ok:
+                raise RuntimeError(self.info().note.decode())
+
+    def tp_prepare(self, hm, rank, size):
+        """Point the shard's head at the rank's vocabulary slice, prepare it and
+        return this rank's exchange-buffer handle (bytes)."""
+        p = hm.profile
+        first, rows = tp_vocab_slice(p.vocab, size, rank)
+        head = "model.embed_tokens.weight" if p.tied else "lm_head.weight"
+        hm.model.head = hm.base + hm.offsets[head] + first * p.hidden * 2
+        handle = _abi.TpHandle()
+        if self.lib.plamo_cuda_tp_prepare(self.ctx, hm.ptr, rank, size, first, rows, ctypes.byref(handle)) != 1:
+            raise RuntimeError("tp_prepare failed: " + self.info().note.decode())
+        return bytes(handle.bytes)
+
+    def tp_connect(self, hm, handles):
+        arr = (_abi.TpHandle * len(handles))()
+        for i, h in enumerate(handles):
+            ctypes.memmove(arr[i].bytes, h, 64)
+        if self.lib.plamo_cuda_tp_connect(self.ctx, hm.ptr, arr) != 1:
+            raise RuntimeError("tp_connect failed: " + self.info().note.decode())
 
     def release(self, hm):
         """Drop the device copies of `hm` (its host memory may be reused)."""
