@@ -14,6 +14,14 @@ replica (own prompt) with no collective on the data path; rank 0 prints the
 aggregate (N x steps / max-over-ranks device time).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload 8b-decode|31b-tp]
+
+--workload 31b-tp: the 31B-shaped model (profile 31b,
+tied head) tensor-parallel over the N ranks of the launch (N = 1: one GPU, no
+tensor parallelism): a 128-token prompt, then batch-1 greedy decode of one
+token stream (strong scaling: the work per token is fixed, N GPUs share it);
+also the same request through the speculative loop with a 0.8B-shaped draft
+proposing 4 tokens per verification.
 """
 import argparse
 import ctypes
@@ -32,6 +40,8 @@ PKG_DIR = os.path.join(ROOT, "plamo-3-translate.c_b200")
 ORACLE = os.path.join(ROOT, "oracle", "liboracle.so")
 PROMPT = 455
 METRIC = "bs1 decode tok/s (8B-shaped)"
+TP_PROMPT = 128
+TP_METRIC = "bs1 decode tok/s (31B-shaped, tensor-parallel)"
 
 
 def load_package():
@@ -337,6 +347,119 @@ def run_ours(args, world, rank, local, dist):
     be.close()
 
 
+def shard_bytes_per_token(full, shard, vocab_rows, ctx_mean):
+    """Bytes one rank streams per decode token: its projections, its head
+    slice, the replicated norms and embedding row, and its K/V rows."""
+    h = full.hidden
+    per_layer = shard.qkv_rows * h + h * shard.attention_width + 3 * shard.inter * h
+    weights = 2 * (full.layers * per_layer + vocab_rows * h)
+    kv = full.layers * ctx_mean * shard.kh * shard.dim * 4 * 2
+    return weights + full.norm_bytes_per_token() + 2 * h + kv
+
+
+def run_tp31b(args, world, rank, local, dist):
+    pkg = load_package()
+    lib = pkg.load()
+    full = pkg.PROFILES["31b"]
+    shard = pkg.tp_shard_profile(full, world) if world > 1 else full
+    cap = 1024
+    be = pkg.Backend(device=local, max_context=cap, max_prefill=256)
+    ctx = be.ctx
+    hm = pkg.HostModel(shard, weights="synthetic", full_capacity=cap)
+    if world > 1:
+        be.preload_synthetic_tp(hm, full, rank, world, seed=5)
+        be.tp_connect(hm, pkg.tp_all_gather_handles(be.tp_prepare(hm, rank, world)))
+        vocab_rows = pkg.tp_vocab_slice(full.vocab, world, rank)[1]
+    else:
+        be.preload_synthetic(hm, seed=5)
+        be.prepare(hm)
+        vocab_rows = full.vocab
+    ids = np.random.default_rng(1).integers(3, 100000, size=TP_PROMPT).astype(np.uint32)
+    nxt = ctypes.c_uint32()
+    prefill_s = None
+    for _ in range(2):
+        lib.plamo_cuda_reset_request(ctx, hm.ptr)
+        before = be.info().gpu_seconds
+        assert lib.plamo_cuda_prefill_greedy(ctx, hm.ptr, ids.ctypes.data, TP_PROMPT,
+                                             ctypes.byref(nxt)) == 1, be.info().note
+        prefill_s = be.info().gpu_seconds - before
+    prefill_rate = TP_PROMPT / reduce_max(dist, prefill_s)
+
+    assert lib.plamo_cuda_time_decode(ctx, hm.ptr, args.warmup) > 0, be.info().note
+    barrier(dist)
+    lib.plamo_cuda_synchronize(ctx)
+    clocks = ClockSampler(local)
+    launches0 = lib.plamo_cuda_kernel_launches(ctx)
+    ms = lib.plamo_cuda_time_decode(ctx, hm.ptr, args.steps)
+    launches = lib.plamo_cuda_kernel_launches(ctx) - launches0
+    clock_info = clocks.stop()
+    assert ms > 0, be.info().note
+    lib.plamo_cuda_synchronize(ctx)
+    barrier(dist)
+    ms_max = reduce_max(dist, ms)
+    ms_per_step = ms_max / args.steps
+    value = args.steps / (ms_max / 1000.0)
+    ctx_mean = TP_PROMPT + args.warmup + (args.steps + 1) / 2.0
+    rank_bytes = shard_bytes_per_token(full, shard, vocab_rows, ctx_mean)
+    peak, peak_src = measured_peaks()
+    achieved = rank_bytes / (ms_per_step / 1000.0) / 1e9
+
+    # End to end through the request API on every rank (same ids, same tokens).
+    out = np.zeros(args.steps + 1, dtype=np.uint32)
+    timing = pkg._abi.CudaTiming()
+    barrier(dist)
+    n = lib.plamo_cuda_generate(ctx, hm.ptr, ids.ctypes.data, TP_PROMPT, args.steps + 1, out.ctypes.data,
+                                pkg._abi.TOKEN_CALLBACK(), None, ctypes.byref(timing))
+    assert n > 0, be.info().note
+    e2e_value = 1.0 / reduce_max(dist, timing.decode_seconds / max(int(timing.decode_steps), 1))
+
+    # Speculative: 0.8B-shaped draft (replicated on every rank), 4 proposals
+    # per verification of the tensor-parallel target.
+    draft_profile = pkg.PROFILES["0.8b"]
+    draft = pkg.HostModel(draft_profile, weights="synthetic", full_capacity=cap)
+    be.preload_synthetic(draft, seed=6)
+    be.prepare(draft)
+    spec_out = np.zeros(args.steps + 1, dtype=np.uint32)
+    stats = pkg._abi.CudaSpeculation()
+    barrier(dist)
+    k = lib.plamo_cuda_generate_speculative(ctx, hm.ptr, draft.ptr, ids.ctypes.data, TP_PROMPT, args.steps + 1, 4,
+                                            spec_out.ctypes.data, pkg._abi.TOKEN_CALLBACK(), None,
+                                            ctypes.byref(stats))
+    assert k > 0, be.info().note
+    spec_rate = max(int(stats.completion_tokens) - 1, 1) / reduce_max(dist, stats.decode_seconds)
+    same = bool(np.array_equal(spec_out[:k], out[:k]))
+    barrier(dist)
+
+    if rank == 0:
+        line = {
+            "metric": TP_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "31b-tp: plamo-3 profile 31b (tied head), 128-token prompt then greedy "
+                                   "decode, batch 1", "model": "plamo-3-31b-shaped (random init)",
+                       "global_batch": 1, "seq_len": TP_PROMPT,
+                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (weights streamed per step)"},
+            "prefill_tok_s": prefill_rate,
+            "roofline": {"bound": "hbm", "kernel": "decode step per rank (one CUDA graph launch per token)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "algorithmic_bytes": rank_bytes, "peak_source": peak_src},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "api": "plamo_cuda_generate on every rank"},
+            "speculative": {"value": spec_rate, "unit": "tok/s", "draft": "0.8b profile, 4 proposals",
+                            "verify_batches": int(stats.verify_batches),
+                            "accepted": int(stats.accepted_tokens), "proposed": int(stats.proposed_tokens),
+                            "tokens_equal_greedy": same,
+                            "note": "random-init draft and target: acceptance says nothing about real models"},
+            "gpu_launches": int(launches),
+            "clocks": clock_info,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    be.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,15 +467,31 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["8b-decode", "31b-tp"], default="8b-decode")
     args = ap.parse_args()
     if args.warmup < 1 or args.steps < 1:
         ap.error("steps and warmup must be positive")
     if args.impl == "reference":
+        if args.workload != "8b-decode":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference CPU path is timed on the "
+                                  "8b-decode workload only (the 31B host model alone is 63.5 GB)"}))
+            return
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
     world, rank, local, dist = dist_setup(args.gpus)
     try:
-        run_ours(args, world, rank, local, dist)
+        if args.workload == "31b-tp":
+            try:
+                run_tp31b(args, world, rank, local, dist)
+            except BaseException:
+                # Keep this rank's exchange buffer mapped until the peers'
+                # bounded waits (2 s) have given up writing to it.
+                if world > 1:
+                    time.sleep(5)
+                raise
+        else:
+            run_ours(args, world, rank, local, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()

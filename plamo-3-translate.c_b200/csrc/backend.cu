@@ -304,9 +304,12 @@ void allow_smem(K kernel, int optin) {
 
 template <int PRO, int EPI>
 void set_gemv_smem_limits(int optin) {
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 1>, optin);
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 2>, optin);
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 4>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 1, false>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 2, false>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 4, false>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 1, true>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 2, true>, optin);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 4, true>, optin);
     allow_smem(gemv_kernel<PRO, EPI, 4>, optin);
     allow_smem(gemv_kernel<PRO, EPI, 2>, optin);
     allow_smem(gemv_kernel<PRO, EPI, 1>, optin);
@@ -360,10 +363,17 @@ bool gemv(plamo_cuda *c, GemvParams p, uint32_t *grid_out = nullptr) {
         }
         if (grid_out) *grid_out = static_cast<uint32_t>(grid);
         const dim3 g(static_cast<uint32_t>(grid)), b(kBulkThreads);
+        if (p.cols % kSubElems) {
+            switch (gemv_bulk_sets(p.cols)) {
+            case 1: return launch(c, gemv_bulk_kernel<PRO, EPI, 1, true>, g, b, smem, p, stages);
+            case 2: return launch(c, gemv_bulk_kernel<PRO, EPI, 2, true>, g, b, smem, p, stages);
+            default: return launch(c, gemv_bulk_kernel<PRO, EPI, 4, true>, g, b, smem, p, stages);
+            }
+        }
         switch (gemv_bulk_sets(p.cols)) {
-        case 1: return launch(c, gemv_bulk_kernel<PRO, EPI, 1>, g, b, smem, p, stages);
-        case 2: return launch(c, gemv_bulk_kernel<PRO, EPI, 2>, g, b, smem, p, stages);
-        default: return launch(c, gemv_bulk_kernel<PRO, EPI, 4>, g, b, smem, p, stages);
+        case 1: return launch(c, gemv_bulk_kernel<PRO, EPI, 1, false>, g, b, smem, p, stages);
+        case 2: return launch(c, gemv_bulk_kernel<PRO, EPI, 2, false>, g, b, smem, p, stages);
+        default: return launch(c, gemv_bulk_kernel<PRO, EPI, 4, false>, g, b, smem, p, stages);
         }
     }
     const int U = gemv_chunks(p.w, p.cols);

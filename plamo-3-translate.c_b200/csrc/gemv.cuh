@@ -247,7 +247,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
         if (EPI == EPI_SWIGLU) {
             p.y[unit] = swiglu(t0, t1);
         } else if (EPI == EPI_STORE && p.tp_role == 2) {
-            for (uint32_t r = 0; r < p.tp.tp; ++r) p.tp.peer_parts[r][unit] = t0;
+            if (!tp_failed(p.tp.error))
+                for (uint32_t r = 0; r < p.tp.tp; ++r) p.tp.peer_parts[r][unit] = t0;
         } else {
             p.y[unit] = t0;
             if (EPI == EPI_ARGMAX) {
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// Bulk-streamed variant (cols % 512 == 0, 16-byte aligned rows).
+// Bulk-streamed variant (cols % 8 == 0, 16-byte aligned rows).
 //
 // A CTA's rows are one contiguous byte range of W (two for gate/up pairs). A
 // producer warp streams it through a ring of shared-memory stages with
@@ -396,24 +397,43 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
 // griddepcontrol.wait, so under programmatic dependent launch the stream
 // starts while the previous kernel drains. A chunk is a whole number of
 // rows (several short rows, or one long row), split into 512-element
-// sub-ranges; consumer warp w takes sub-ranges w, w+16, w+32, w+48 of every
-// chunk, which are always the same column slots, so each warp keeps its
-// slice of the input vector in registers for the whole kernel and reduces
-// each sub-range to one partial sum per (row, 512-column slot).
+// sub-ranges (the last one of a row shorter when cols % 512 != 0); consumer
+// warp w takes sub-ranges w, w+16, w+32, w+48 of every chunk, which are
+// always the same column slots, so each warp keeps its slice of the input
+// vector in registers for the whole kernel and reduces each sub-range to one
+// partial sum per (row, 512-column slot).
 constexpr int kBulkConsumers = 16;
 constexpr int kBulkThreads = (kBulkConsumers + 1) * 32;
 constexpr int kSubElems = 512;
 constexpr int kMaxStages = 12;
 constexpr int kMaxSets = 4;  // sub-ranges per warp per chunk
 
-// Sub-ranges per chunk for `slots` 512-column slots per row: whole rows, at
-// most 16 sub-ranges when rows are short, one row (<= 64 slots) otherwise.
-__host__ __device__ inline uint32_t bulk_chunk_subs(uint32_t slots) {
-    if (slots <= 16) return (16 / slots) * slots;
-    return slots;
+// Column slots of a row: ceil(cols / 512).
+__host__ __device__ inline uint32_t bulk_slots(uint64_t cols) {
+    return static_cast<uint32_t>((cols + kSubElems - 1) / kSubElems);
 }
 
-template <int PRO, int EPI, int SETS>
+// Sub-ranges per chunk for `slots` 512-column slots per row: a whole number
+// of rows (so every chunk starts at slot 0 and each warp's column slots stay
+// fixed), at most 16 * kMaxSets sub-ranges, chosen so the 16 consumer warps
+// get the most even shares (10 slots: 3 rows = 30 sub-ranges, 94% of the
+// warps busy instead of 10 of 16), then the smallest such chunk.
+__host__ __device__ inline uint32_t bulk_chunk_subs(uint32_t slots) {
+    uint32_t best = slots, best_den = 16 * ((slots + 15) / 16);
+    for (uint32_t r = 2; r * slots <= 16u * kMaxSets; ++r) {
+        const uint32_t subs = r * slots, den = 16 * ((subs + 15) / 16);
+        if (static_cast<uint64_t>(subs) * best_den > static_cast<uint64_t>(best) * den) {
+            best = subs;
+            best_den = den;
+        }
+    }
+    return best;
+}
+
+// PART: rows end inside a 512-column slot (cols % 512 != 0); the lanes past
+// a row's end read nothing and contribute zero. Without it the sub-range
+// addressing is the plain j * 512 of full slots.
+template <int PRO, int EPI, int SETS, bool PART>
 __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, int stages) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
@@ -427,9 +447,12 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
     const uint64_t u0 = units * blockIdx.x / gridDim.x;
     const uint64_t u1 = units * (blockIdx.x + 1) / gridDim.x;
     const uint64_t rows_local = u1 - u0;
-    const uint32_t slots = static_cast<uint32_t>(cols / kSubElems);
+    const uint32_t slots = PART ? bulk_slots(cols) : static_cast<uint32_t>(cols / kSubElems);
     const uint32_t csubs = bulk_chunk_subs(slots);
-    const uint32_t chunk_bytes = csubs * kSubElems * 2;
+    const uint32_t cols32 = static_cast<uint32_t>(cols);
+    // Full slots: a chunk is csubs 1 KB sub-ranges; partial: rpc rows.
+    const uint32_t rpc = PART ? csubs / slots : 0;
+    const uint32_t chunk_bytes = PART ? rpc * cols32 * 2 : csubs * kSubElems * 2;
     const uint32_t subs_per_range = static_cast<uint32_t>(rows_local) * slots;
     const uint32_t cpr = (subs_per_range + csubs - 1) / csubs;  // chunks per range
     const uint32_t total = kPair * cpr;
@@ -461,10 +484,12 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
         const uint32_t m = (kPair == 2 && k >= cpr) ? 1u : 0u;
         const uint32_t kc = k - m * cpr;
         const uint32_t left = subs_per_range - kc * csubs;
-        const uint32_t bytes = (left < csubs ? left : csubs) * kSubElems * 2;
+        const uint32_t bytes = PART ? (left < csubs ? left : csubs) / slots * cols32 * 2
+                                    : (left < csubs ? left : csubs) * kSubElems * 2;
         mbar_expect_tx(&full_bar[s], bytes);
-        bulk_load(ring + static_cast<size_t>(s) * chunk_bytes,
-                  range_base[m] + static_cast<uint64_t>(kc) * csubs * kSubElems, bytes, &full_bar[s], policy);
+        const uint16_t *src = PART ? range_base[m] + static_cast<uint64_t>(kc) * rpc * cols
+                                   : range_base[m] + static_cast<uint64_t>(kc) * csubs * kSubElems;
+        bulk_load(ring + static_cast<size_t>(s) * chunk_bytes, src, bytes, &full_bar[s], policy);
     };
     const uint32_t primed = total < static_cast<uint32_t>(stages) ? total : static_cast<uint32_t>(stages);
     uint32_t issued = 0;  // meaningful in the producer lane only
@@ -475,13 +500,28 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
     const bool ok = gemv_prologue<PRO>(p, xs, red);
     __syncthreads();
 
-    // Register copy of this warp's input slots: set i serves sub-range w+16i.
+    // Register copy of this warp's input slots: set i serves sub-range
+    // w+16i, which is row jr of a chunk at column slot js; the lane's two
+    // 8-column pieces lie at col0 and col0 + 256 (zero past the row's end).
     float xr[SETS][16];
+    uint32_t soff[SETS];  // PART: uint4 offset of the lane's first piece in a stage
+    bool v0[SETS], v1[SETS];
     if (!producer) {
 #pragma unroll
         for (int i = 0; i < SETS; ++i) {
             const uint32_t j = static_cast<uint32_t>(warp) + 16u * i;
-            if (j < csubs) {
+            if constexpr (PART) {
+                const uint32_t jr = j / slots, js = j - jr * slots;
+                const uint32_t col0 = js * kSubElems + lane * 8;
+                v0[i] = j < csubs && col0 < cols32;
+                v1[i] = j < csubs && col0 + 256 < cols32;
+                soff[i] = (jr * cols32 + col0) / 8;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    xr[i][e] = v0[i] ? xs[col0 + e] : 0.0f;
+                    xr[i][8 + e] = v1[i] ? xs[col0 + 256 + e] : 0.0f;
+                }
+            } else if (j < csubs) {
                 const float *xc = xs + (j % slots) * kSubElems + lane * 8;
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
@@ -529,8 +569,15 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
                 if (j < nsub) {
                     const uint32_t g = sub0 + j;
                     const uint32_t row = g / slots, slot = g - row * slots;
-                    const uint4 w0 = stage[j * 64 + lane];
-                    const uint4 w1 = stage[j * 64 + 32 + lane];
+                    uint4 w0, w1;
+                    if constexpr (PART) {
+                        const uint4 z = make_uint4(0, 0, 0, 0);
+                        w0 = v0[i] ? stage[soff[i]] : z;
+                        w1 = v1[i] ? stage[soff[i] + 32] : z;
+                    } else {
+                        w0 = stage[j * 64 + lane];
+                        w1 = stage[j * 64 + 32 + lane];
+                    }
                     const float a = dot8r(w0, xr[i], 0.0f);
                     const float b = dot8r(w1, xr[i] + 8, 0.0f);
                     const float sum = warp_sum(a + b);
@@ -561,19 +608,20 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
 // Bulk path applies when rows split into 512-column slots and a chunk (one
 // row at most 64 slots) fits the ring.
 inline bool gemv_bulk_shape(uint64_t cols) {
-    return cols % kSubElems == 0 && cols / kSubElems <= 16ull * kMaxSets;
+    return cols % 8 == 0 && bulk_slots(cols) <= 16ull * kMaxSets;
 }
 // Register sets a warp needs: one per 16 sub-ranges of a chunk.
 inline int gemv_bulk_sets(uint64_t cols) {
-    const uint32_t subs = bulk_chunk_subs(static_cast<uint32_t>(cols / kSubElems));
+    const uint32_t subs = bulk_chunk_subs(bulk_slots(cols));
     return subs <= 16 ? 1 : (subs <= 32 ? 2 : 4);
 }
 inline uint32_t gemv_bulk_chunk_bytes(uint64_t cols) {
-    return bulk_chunk_subs(static_cast<uint32_t>(cols / kSubElems)) * kSubElems * 2;
+    const uint32_t slots = bulk_slots(cols);
+    return bulk_chunk_subs(slots) / slots * static_cast<uint32_t>(cols) * 2;
 }
 inline size_t gemv_bulk_smem(uint64_t cols, uint64_t rows_per_block, int pair, int stages) {
     return static_cast<size_t>(stages) * gemv_bulk_chunk_bytes(cols) +
-           (((cols + 3) & ~3ull) + rows_per_block * (cols / kSubElems) * pair) * sizeof(float);
+           (((cols + 3) & ~3ull) + rows_per_block * bulk_slots(cols) * pair) * sizeof(float);
 }
 
 // Merge per-block argmax candidates: first maximal index, NaN -> UINT32_MAX

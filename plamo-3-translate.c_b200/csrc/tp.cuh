@@ -17,7 +17,10 @@
 // operation (decode step, prompt, verification) on every rank; a flag holds
 // epoch + 1 of the operation that raised it, so buffers and flags are reused
 // without resets. Every wait is bounded (2 s of %globaltimer): on timeout the
-// kernel records an error and continues with whatever is in the buffer.
+// kernel records error 4 and continues with whatever is in the buffer. Once
+// error 4 is recorded, the rest of the operation neither waits nor writes to
+// peers: a peer that stopped (or whose process is exiting) is left alone
+// within 2 s, and its memory is not touched after that.
 #pragma once
 #include "common.cuh"
 
@@ -48,7 +51,12 @@ __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
 
 // One thread: wait until every rank's flag of this point shows the current
 // epoch. Returns false after ~2 s (error recorded).
+__device__ __forceinline__ bool tp_failed(const uint32_t *error) {
+    return error && *reinterpret_cast<const volatile uint32_t *>(error) == 4u;
+}
+
 __device__ __forceinline__ bool tp_wait_flags(const TpPoint &t) {
+    if (tp_failed(t.error)) return false;
     const uint32_t want = *t.epoch + 1;
     uint64_t start = 0;
     for (uint32_t r = 0; r < t.tp; ++r) {
@@ -73,7 +81,8 @@ __device__ __forceinline__ void tp_signal(const TpPoint &t) {
             *t.ticket = 0;
             __threadfence_system();
             const uint32_t flag = *t.epoch + 1;
-            for (uint32_t r = 0; r < t.tp; ++r) st_release_sys(t.peer_flags[r], flag);
+            if (!tp_failed(t.error))
+                for (uint32_t r = 0; r < t.tp; ++r) st_release_sys(t.peer_flags[r], flag);
         }
     }
 }
@@ -98,7 +107,7 @@ __device__ __forceinline__ float tp_sum1(const TpPoint &t, uint64_t i) {
 // into slot `rank` of every peer (n % 4 == 0, 16-byte aligned), then signal.
 __global__ void tp_push_kernel(const float *src, uint64_t n, TpPoint t) {
     pdl_wait();
-    const uint64_t n4 = n / 4;
+    const uint64_t n4 = tp_failed(t.error) ? 0 : n / 4;
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const float4 v = reinterpret_cast<const float4 *>(src)[i];
@@ -136,7 +145,8 @@ __global__ void tp_argmax_kernel(const float *val, const uint32_t *idx, uint32_t
                                  uint32_t *out, uint32_t *next_token) {
     pdl_wait();
     const uint32_t flag = *a.epoch + 1;
-    for (uint32_t row = threadIdx.x; row < rows; row += blockDim.x) {
+    const bool failed = tp_failed(a.error);
+    for (uint32_t row = threadIdx.x; row < rows && !failed; row += blockDim.x) {
         const uint32_t li = idx[row];
         const uint32_t gi = li == 0xffffffffu ? li : li + offset;
         const uint32_t vbits = __float_as_uint(val[row]);
@@ -153,7 +163,7 @@ __global__ void tp_argmax_kernel(const float *val, const uint32_t *idx, uint32_t
         uint32_t bi = 0xffffffffu;
         bool nan_seen = false;
         const uint64_t start = global_ns();
-        for (uint32_t r = 0; r < a.tp; ++r) {
+        for (uint32_t r = 0; r < a.tp && !failed; ++r) {
             const uint32_t *s = a.slots + (static_cast<size_t>(row) * a.tp + r) * 4;
             bool arrived = true;
             while (ld_acquire_sys(s + 2) != flag)

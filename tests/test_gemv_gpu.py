@@ -62,7 +62,9 @@ def test_config1_gemv_matches_reference_matvec(backend, rows, cols):
 
 @pytest.mark.parametrize("rows,cols", [(1, 1), (3, 7), (4, 4), (3, 4), (5, 12), (8, 12), (16, 128),
                                        (12, 64), (128, 4096), (64, 16384), (7, 256), (9, 512),
-                                       (33, 1536), (17, 3072), (5, 25600), (300, 2048)])
+                                       (33, 1536), (17, 3072), (5, 25600), (300, 2048),
+                                       # rows ending inside a 512-column slot (tensor-parallel shards)
+                                       (40, 3200), (33, 6400), (21, 1000), (64, 9992), (300, 5128)])
 def test_gemv_odd_shapes(backend, rows, cols):
     rng = np.random.default_rng(rows * 1000 + cols)
     w = synthetic.bf16_round(rng.normal(0, 0.05, size=(rows, cols)).astype(np.float32))

@@ -6,7 +6,8 @@ slice of the head), with synthetic weights cut bit for bit from the full
 model's. The ranks exchange their buffer handles over a gloo group, then run
 the same calls: the prompt logits, gathered from the ranks' slices, must meet
 the reference's GPU acceptance rule against the oracle's full-model prefill,
-and the greedy tokens must equal the oracle's.
+and the greedy tokens must equal the oracle's, also when a draft model
+proposes them and the tensor-parallel target verifies blocks of 4.
 
 Ranks leave only between calls (every call synchronises its stream), after a
 barrier, so no rank frees its exchange buffer while a peer may still write
@@ -15,6 +16,7 @@ to it.
 import ctypes
 import os
 import socket
+import time
 import traceback
 
 import numpy as np
@@ -66,10 +68,25 @@ def _rank(rank, size, port, ids, max_tokens, out):
         timing = pkg._abi.CudaTiming()
         n = b.lib.plamo_cuda_generate(b.ctx, hm.ptr, ids.ctypes.data, len(ids), max_tokens, toks.ctypes.data,
                                       pkg._abi.TOKEN_CALLBACK(), None, ctypes.byref(timing))
+        # Speculative decoding with the target tensor-parallel: a draft model
+        # (the full model's heads on every rank: the shard profile's own
+        # shapes, unrelated weights) proposes 4 tokens per verification.
+        draft = pkg.HostModel(shard, weights="synthetic")
+        b.preload_synthetic(draft, SEED + 50)
+        b.prepare(draft)
+        spec = np.zeros(max_tokens, dtype=np.uint32)
+        stats = pkg._abi.CudaSpeculation()
+        k = b.lib.plamo_cuda_generate_speculative(b.ctx, hm.ptr, draft.ptr, ids.ctypes.data, len(ids), max_tokens,
+                                                  4, spec.ctypes.data, pkg._abi.TOKEN_CALLBACK(), None,
+                                                  ctypes.byref(stats))
         out[rank] = dict(rc=rc, logits=logits, states=states, tokens=[int(t) for t in toks[:max(n, 0)]], n=n,
+                         spec=[int(t) for t in spec[:max(k, 0)]], verify_batches=int(stats.verify_batches),
                          note=b.info().note.decode(), errors=b.info().errors)
     except Exception:
         out[rank] = dict(error=traceback.format_exc())
+        # Keep the exchange buffer mapped until the peers' bounded waits
+        # (2 s) have given up writing to it.
+        time.sleep(5)
     finally:
         try:
             dist.barrier()
@@ -117,3 +134,5 @@ def test_tensor_parallel_matches_oracle(size):
         assert oracle_forward(ref, t) == 1
     for rank, r in enumerate(res):
         assert r["tokens"] == want_tokens, f"rank {rank}"
+        assert r["spec"] == want_tokens, f"rank {rank} speculative"
+        assert r["verify_batches"] > 0
