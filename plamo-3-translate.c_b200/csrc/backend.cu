@@ -670,7 +670,7 @@ bool greedy_choice(plamo_cuda *c, DModel *m, uint32_t grid) {
                 tp ? m->tp.lidx : m->d_next, tp ? nullptr : m->d_token, tp ? m->tp.lval : nullptr))
         return false;
     if (!tp) return true;
-    return launch(c, tp_argmax_kernel, dim3(1), dim3(32), 0, static_cast<const float *>(m->tp.lval),
+    return launch(c, tp_argmax_kernel, dim3(1), dim3(128), 0, static_cast<const float *>(m->tp.lval),
                   static_cast<const uint32_t *>(m->tp.lidx), 1u, static_cast<uint32_t>(m->tp.voff), tp_arg(m),
                   m->d_next, m->d_token);
 }
@@ -1500,7 +1500,7 @@ int plamo_cuda_verify(struct plamo_cuda *c, struct model *model, const uint32_t 
     if (!launch(c, rows_argmax_kernel, dim3(tokens), dim3(256), 0, static_cast<const float *>(m->p_logits), m->Vh,
                 tp ? m->tp.lidx : m->p_next, tp ? m->tp.lval : nullptr))
         return -1;
-    if (tp && (!launch(c, tp_argmax_kernel, dim3(1), dim3(32), 0, static_cast<const float *>(m->tp.lval),
+    if (tp && (!launch(c, tp_argmax_kernel, dim3(1), dim3(128), 0, static_cast<const float *>(m->tp.lval),
                        static_cast<const uint32_t *>(m->tp.lidx), static_cast<uint32_t>(tokens),
                        static_cast<uint32_t>(m->tp.voff), tp_arg(m), m->p_next, static_cast<uint32_t *>(nullptr)) ||
                !launch(c, tp_epoch_kernel, dim3(1), dim3(32), 0, m->tp.epoch)))

@@ -45,8 +45,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // One thread: wait until every rank's flag of this point shows the current
@@ -72,18 +72,20 @@ __device__ __forceinline__ bool tp_wait_flags(const TpPoint &t) {
 }
 
 // Called by every thread of a producing CTA after its stores to the peers:
-// the last CTA of the grid raises this rank's flag at every peer.
+// the last CTA of the grid raises this rank's flag at every peer, one thread
+// per peer (fence, then the flag), so the peers are signalled concurrently.
 __device__ __forceinline__ void tp_signal(const TpPoint &t) {
+    __shared__ uint32_t last;
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence_system();
-        if (atomicAdd(t.ticket, 1u) == gridDim.x - 1) {
-            *t.ticket = 0;
-            __threadfence_system();
-            const uint32_t flag = *t.epoch + 1;
-            if (!tp_failed(t.error))
-                for (uint32_t r = 0; r < t.tp; ++r) st_release_sys(t.peer_flags[r], flag);
-        }
+        last = atomicAdd(t.ticket, 1u) == gridDim.x - 1;
+        if (last) *t.ticket = 0;
+    }
+    __syncthreads();
+    if (last && threadIdx.x < t.tp && !tp_failed(t.error)) {
+        __threadfence_system();
+        st_relaxed_sys(t.peer_flags[threadIdx.x], *t.epoch + 1);
     }
 }
 
@@ -146,16 +148,15 @@ __global__ void tp_argmax_kernel(const float *val, const uint32_t *idx, uint32_t
     pdl_wait();
     const uint32_t flag = *a.epoch + 1;
     const bool failed = tp_failed(a.error);
-    for (uint32_t row = threadIdx.x; row < rows && !failed; row += blockDim.x) {
+    // One thread per (row, peer): value and index, fence, flag.
+    for (uint32_t i = threadIdx.x; i < rows * a.tp && !failed; i += blockDim.x) {
+        const uint32_t row = i / a.tp, r = i - row * a.tp;
         const uint32_t li = idx[row];
-        const uint32_t gi = li == 0xffffffffu ? li : li + offset;
-        const uint32_t vbits = __float_as_uint(val[row]);
-        for (uint32_t r = 0; r < a.tp; ++r) {
-            uint32_t *s = a.peer_slots[r] + (static_cast<size_t>(row) * a.tp + a.rank) * 4;
-            s[0] = vbits;
-            s[1] = gi;
-            st_release_sys(s + 2, flag);
-        }
+        uint32_t *s = a.peer_slots[r] + (static_cast<size_t>(row) * a.tp + a.rank) * 4;
+        s[0] = __float_as_uint(val[row]);
+        s[1] = li == 0xffffffffu ? li : li + offset;
+        __threadfence_system();
+        st_relaxed_sys(s + 2, flag);
     }
     __syncthreads();
     for (uint32_t row = threadIdx.x; row < rows; row += blockDim.x) {
