@@ -40,6 +40,7 @@ PKG_DIR = os.path.join(ROOT, "plamo-3-translate.c_b200")
 ORACLE = os.path.join(ROOT, "oracle", "liboracle.so")
 PROMPT = 455
 METRIC = "bs1 decode tok/s (8B-shaped)"
+BATCH = 8  # independent requests per GPU in the multi-request measurement
 TP_PROMPT = 128
 TP_METRIC = "bs1 decode tok/s (31B-shaped, tensor-parallel)"
 
@@ -307,6 +308,8 @@ def run_ours(args, world, rank, local, dist):
     e2e_s = reduce_max(dist, timing.decode_seconds / steps_e2e)
     e2e_value = world / e2e_s
 
+    batch_info = run_batch(args, pkg, lib, be, hm, profile, world, rank, dist, peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
@@ -342,9 +345,65 @@ def run_ours(args, world, rank, local, dist):
             "gpu_launches": int(launches),
             "clocks": clock_info,
             "cpu_baseline": cpu,
+            "batch": batch_info,
         }
         print(json.dumps(line), flush=True)
     be.close()
+
+
+def run_batch(args, pkg, lib, be, hm, profile, world, rank, dist, peak):
+    """BASELINE config 4's second form: 8 independent requests per GPU (each its
+    own 455-token prompt and KV cache) decoded together, one pass over the
+    weights per step (plamo_cuda_batch_*). Aggregate tok/s over all ranks."""
+    ctx = be.ctx
+    reqs = [hm] + [pkg.HostModel(profile, weights_of=hm, full_capacity=8208) for _ in range(BATCH - 1)]
+    for r in reqs[1:]:
+        be.prepare(r)
+    toks = np.zeros(BATCH, dtype=np.uint32)
+    nxt = ctypes.c_uint32()
+    for i, r in enumerate(reqs):
+        lib.plamo_cuda_reset_request(ctx, r.ptr)
+        ids = np.random.default_rng(1000 + rank * BATCH + i).integers(3, 100000, size=PROMPT).astype(np.uint32)
+        assert lib.plamo_cuda_prefill_greedy(ctx, r.ptr, ids.ctypes.data, PROMPT, ctypes.byref(nxt)) == 1, \
+            be.info().note
+        toks[i] = nxt.value
+    arr = (ctypes.c_void_p * BATCH)(*[ctypes.addressof(r.model) for r in reqs])
+    batch = lib.plamo_cuda_batch_open(ctx, arr, BATCH)
+    assert batch, be.info().note
+    try:
+        out = np.zeros(BATCH, dtype=np.uint32)
+        assert lib.plamo_cuda_batch_step(batch, toks.ctypes.data, out.ctypes.data) == 1, be.info().note
+        assert lib.plamo_cuda_time_batch(batch, args.warmup) > 0, be.info().note
+        barrier(dist)
+        ms = lib.plamo_cuda_time_batch(batch, args.steps)
+        assert ms > 0, be.info().note
+        barrier(dist)
+        ms_max = reduce_max(dist, ms)
+        ms_step = ms_max / args.steps
+        value = world * BATCH * args.steps / (ms_max / 1000.0)
+        ctx_mean = PROMPT + 1 + args.warmup + (args.steps + 1) / 2.0
+        kv = BATCH * profile.layers * ctx_mean * profile.kh * profile.dim * 4 * 2
+        step_bytes = (profile.weight_bytes_per_token() + profile.norm_bytes_per_token() +
+                      BATCH * 2 * profile.hidden + kv)
+        achieved = step_bytes / (ms_step / 1000.0) / 1e9
+        # End to end through the public step call: host tokens in, host tokens out.
+        tokens = out.copy()
+        barrier(dist)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            assert lib.plamo_cuda_batch_step(batch, tokens.ctypes.data, out.ctypes.data) == 1, be.info().note
+            tokens = out.copy()
+        e2e_s = reduce_max(dist, (time.perf_counter() - t0) / args.steps)
+    finally:
+        lib.plamo_cuda_batch_close(batch)
+    for r in reqs[1:]:
+        lib.plamo_cuda_release_model(ctx, r.ptr)
+    return {"requests_per_gpu": BATCH, "value": value, "unit": "tok/s", "ms_per_step": ms_step,
+            "roofline": {"bound": "hbm", "kernel": "batched decode step (one CUDA graph per step)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "algorithmic_bytes": step_bytes},
+            "e2e": {"value": world * BATCH / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * BATCH,
+                    "d2h_bytes_per_step": 4 * BATCH, "api": "plamo_cuda_batch_step (host wall clock per step)"}}
 
 
 def shard_bytes_per_token(full, shard, vocab_rows, ctx_mean):

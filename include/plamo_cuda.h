@@ -167,6 +167,25 @@ int64_t plamo_cuda_generate_speculative(struct plamo_cuda *, struct model *targe
    like the reference's plamo_reset_request (runtime/engine.c:46-55). */
 void plamo_cuda_reset_request(struct plamo_cuda *, struct model *);
 
+/* Multi-request decode (no counterpart in the reference, which serves one
+   request at a time): `count` (1..PLAMO_CUDA_VERIFY_MAX) prepared models with
+   identical shapes over the same preloaded weights - each its own descriptor
+   tree and KV cache, one per request - advance one token each per step and
+   share one pass over the weights: the projections run as tcgen05 GEMMs over
+   the `count` rows, attention runs per request on its own cache (head dim
+   128). step() appends tokens[i] to request i and writes its greedy next token
+   to next[i], like plamo_cuda_forward_greedy on each model (host state and
+   logits are not copied; host KV counts are). One CUDA graph per step.
+   Returns 1, 0 (declined: a cache is full or a token is outside the
+   vocabulary; nothing changed) or -1. time_batch runs `steps` steps feeding
+   each step's tokens into the next on the device and returns the device
+   milliseconds. */
+struct plamo_cuda_batch;
+struct plamo_cuda_batch *plamo_cuda_batch_open(struct plamo_cuda *, struct model *const *models, unsigned count);
+int plamo_cuda_batch_step(struct plamo_cuda_batch *, const uint32_t *tokens, uint32_t *next);
+double plamo_cuda_time_batch(struct plamo_cuda_batch *, uint64_t steps);
+void plamo_cuda_batch_close(struct plamo_cuda_batch *);
+
 /* Device prompt (template prefix) cache: the snapshots of reference
    runtime/prompt_cache.h:8-16, held in device memory. Capture copies the
    committed KV rows [0, tokens) of every layer of a prepared model after a

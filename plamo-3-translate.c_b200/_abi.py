@@ -168,6 +168,10 @@ SIGNATURES = {
     "plamo_cuda_tp_prepare": (c_int, [P, M, c_uint, c_uint, c_uint64, c_uint64,
                                       POINTER(TpHandle)]),
     "plamo_cuda_tp_connect": (c_int, [P, M, POINTER(TpHandle)]),
+    "plamo_cuda_batch_open": (c_void_p, [P, P, c_uint]),
+    "plamo_cuda_batch_step": (c_int, [P, P, P]),
+    "plamo_cuda_time_batch": (c_double, [P, c_uint64]),
+    "plamo_cuda_batch_close": (None, [P]),
 }
 
 _lib = None

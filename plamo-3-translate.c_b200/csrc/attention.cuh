@@ -486,8 +486,7 @@ inline size_t decode_attention128_smem(uint32_t G) {
                             + 3 * G);
 }
 
-__global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)
-    decode_attention128_kernel(DecodeAttnParams p) {
+__device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams &p) {
     constexpr uint32_t D = 128, H = 64, KS = kD128Stride;
     extern __shared__ __align__(16) float sm[];
     const uint32_t G = p.qh / p.kh;
@@ -707,6 +706,18 @@ __global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads
         }
     }
     cluster.sync();
+}
+
+__global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)
+    decode_attention128_kernel(DecodeAttnParams p) {
+    decode_attention128_body(p);
+}
+
+// Several independent requests in one launch (blockIdx.z = request): each
+// has its own KV rings, counter and projection row.
+__global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)
+    decode_attention128_batch_kernel(const DecodeAttnParams *ps) {
+    decode_attention128_body(ps[blockIdx.z]);
 }
 
 // DT: compile-time head dim (128) for the vectorised path, 0 for any even dim.

@@ -32,6 +32,10 @@ namespace {
 constexpr float kPostMixerOffset = 0.2f;                 // reference src/layer.s:51
 constexpr float kPostMlpOffset = 0.08944271909999159f;   // reference src/model.s:112
 constexpr uint64_t kVerifyMax = PLAMO_CUDA_VERIFY_MAX;
+// Split-K scratch per model: splits x tokens x rows of the small-token
+// projections (<= 16 tokens, fewer row tiles than SMs: at most
+// 2 x 148 x 128 rows' worth per token).
+constexpr uint64_t kSplitkFloats = 16ull * 40960;
 
 // Device staging of plamo_cuda_linear_static: a fixed array in the module
 // instead of cudaMalloc'd buffers. Every GPU that loads this library holds it
@@ -105,6 +109,7 @@ struct DModel {
     float *p_states, *p_norm, *p_qkv, *p_q, *p_attn, *p_branch, *p_gu, *p_logits, *p_part;
     uint32_t *p_ids, *p_next, *p_tickets;
     uint16_t *p_split;  // BF16 hi/mid/lo terms of a projection input, 3 x [T][K]
+    float *p_splitk;    // split-K partial tiles of small-token projections
     float *v_kv;  // [L][kVerifyMax][2][KVW]
     uint64_t verify_count = 0, verify_committed = 0;
     bool verify_valid = false;
@@ -135,9 +140,11 @@ struct plamo_cuda {
     uint64_t pinned_capacity;
     int sm_count;
     int smem_optin;
+    int smem_per_sm;
     bool pdl;
     bool bulk_gemv;
     int gemv_ring_kb;
+    int tc_stages;  // tcgen05 projection ring depth (0: as many as shared memory holds)
     bool tc_gemm;
     bool prompt_attn;  // blocked prompt attention (PLAMO_CUDA_PROMPT_ATTN=0 disables)
     int gemv_ctas;
@@ -158,6 +165,20 @@ struct plamo_cuda_prompt_cache {
     std::vector<uint64_t> width;
     std::vector<uint32_t> scale_bits;
     float *rows;
+};
+
+// Requests decoded together (plamo_cuda_batch_*): model 0 lends its weights
+// and prompt workspace, every model keeps its own KV.
+struct plamo_cuda_batch {
+    plamo_cuda *c;
+    std::vector<struct model *> hosts;
+    uint32_t B;
+    DecodeAttnParams *d_attn;  // [L][B]
+    uint64_t **d_counters;     // [B] each model's per-layer row counters
+    uint32_t *d_tokens;        // [B] this step's tokens, then the greedy next ones
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    uint64_t nodes;
 };
 
 namespace {
@@ -417,9 +438,16 @@ bool bf16_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, u
 
 template <int N>
 bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &mm,
-               const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T) {
-    int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, (c->smem_optin - 2048) / tc_stage_bytes(N)));
-    const dim3 grid((T + N - 1) / N, (R + kTcM - 1) / kTcM);
+               const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T, uint32_t splits) {
+    // Up to 32 tokens a tile streams weights with little math per byte: two
+    // CTAs share each SM (half the shared memory each; their accumulator rings
+    // take 256 of the 512 TMEM columns each), so two weight pipelines are in
+    // flight per SM and a grid of up to 2 x 148 tiles is resident at once.
+    const size_t budget = N <= 32 ? static_cast<size_t>(c->smem_per_sm) / 2 - 8192
+                                  : static_cast<size_t>(c->smem_optin) - 2048;
+    int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, budget / tc_stage_bytes(N)));
+    if (c->tc_stages) stages = std::min(stages, c->tc_stages);
+    const dim3 grid((T + N - 1) / N, (R + kTcM - 1) / kTcM, splits);
     return launch(c, gemm_tc_kernel<N>, grid, dim3(kTcThreads), tc_smem_bytes(N, stages), mw, mh, mm, ml, p,
                   stages);
 }
@@ -428,8 +456,10 @@ bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, cons
 // tensor cores when the shapes allow TMA (16-byte aligned rows), else on the
 // FP32 CUDA-core kernel otherwise. split: BF16 scratch of 3*T*K elements
 // (the hi, mid and lo terms).
+// part/part_floats: scratch for split-K partial tiles (nullptr: no split K).
 bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys, uint64_t T,
-                     uint64_t R, uint64_t K, uint16_t *split, uint32_t *error) {
+                     uint64_t R, uint64_t K, uint16_t *split, uint32_t *error, float *part = nullptr,
+                     uint64_t part_floats = 0) {
     if (!T || !R) return true;
     const bool tc = c->tc_gemm && split && K % 8 == 0 && K >= kTcK && reinterpret_cast<uintptr_t>(W) % 16 == 0 &&
                     T < (1ull << 31) && R < (1ull << 31) && tensor_maps_available();
@@ -446,19 +476,37 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
         snprintf(c->info.note, sizeof c->info.note, "tensor map encode failed");
         return gemm(c, X, xs, W, Y, ys, T, R, K);
     }
-    TcGemmParams p{Y, ys, static_cast<uint32_t>(T), static_cast<uint32_t>(R), static_cast<uint32_t>(K), error};
+    TcGemmParams p{Y, ys, static_cast<uint32_t>(T), static_cast<uint32_t>(R), static_cast<uint32_t>(K), error, part};
     const uint32_t r32 = static_cast<uint32_t>(R), t32 = static_cast<uint32_t>(T);
-    switch (N) {
-    case 16: return launch_tc<16>(c, mw, mh, mm, ml, p, r32, t32);
-    case 32: return launch_tc<32>(c, mw, mh, mm, ml, p, r32, t32);
-    case 64: return launch_tc<64>(c, mw, mh, mm, ml, p, r32, t32);
-    default: return launch_tc<128>(c, mw, mh, mm, ml, p, r32, t32);
+    // Split K when a handful of tokens leaves SMs without a row tile: as many
+    // splits as keep every CTA resident at two per SM (one wave), at least 4
+    // K blocks per split.
+    uint32_t splits = 1;
+    const uint64_t tiles = ((T + N - 1) / N) * ((R + kTcM - 1) / kTcM);
+    const uint64_t kall = (K + kTcK - 1) / kTcK;
+    if (part && T <= 16 && tiles < static_cast<uint64_t>(c->sm_count)) {
+        uint64_t want = 2ull * c->sm_count / tiles;
+        want = std::min<uint64_t>({want, kall / 4, 16});
+        while (want > 1 && want * T * R > part_floats) --want;
+        splits = static_cast<uint32_t>(std::max<uint64_t>(want, 1));
     }
+    bool ok;
+    switch (N) {
+    case 16: ok = launch_tc<16>(c, mw, mh, mm, ml, p, r32, t32, splits); break;
+    case 32: ok = launch_tc<32>(c, mw, mh, mm, ml, p, r32, t32, splits); break;
+    case 64: ok = launch_tc<64>(c, mw, mh, mm, ml, p, r32, t32, splits); break;
+    default: ok = launch_tc<128>(c, mw, mh, mm, ml, p, r32, t32, splits); break;
+    }
+    if (!ok || splits == 1) return ok;
+    const uint32_t sum_blocks = static_cast<uint32_t>(std::min<uint64_t>((T * R + 255) / 256, 4096));
+    return launch(c, splitk_sum_kernel, dim3(sum_blocks), dim3(256), 0, static_cast<const float *>(part), splits, t32,
+                  r32, Y, ys);
 }
 
 bool projection(plamo_cuda *c, DModel *m, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys,
                 uint64_t T, uint64_t R, uint64_t K) {
-    return projection_with(c, X, xs, W, Y, ys, T, R, K, T <= m->tmax ? m->p_split : nullptr, m->d_error);
+    return projection_with(c, X, xs, W, Y, ys, T, R, K, T <= m->tmax ? m->p_split : nullptr, m->d_error,
+                           m->p_splitk, kSplitkFloats);
 }
 
 AttnLayer attn_layer(const DModel *m, uint64_t l) {
@@ -661,6 +709,19 @@ TpArg tp_arg(DModel *m) {
     return a;
 }
 
+// Greedy choice of every row of a [rows][V] logits block (per-chunk
+// candidates in the head GEMV's candidate buffers, then a merge per row).
+bool rows_argmax(plamo_cuda *c, DModel *m, const float *logits, uint64_t n, uint32_t rows, uint32_t *out,
+                 float *out_val) {
+    const uint32_t chunks = std::max<uint32_t>(1, std::min<uint32_t>(64, static_cast<uint32_t>(
+                                                                          static_cast<uint64_t>(c->sm_count) * 64 / rows)));
+    return launch(c, rows_argmax_partial_kernel, dim3(chunks, rows), dim3(256), 0, logits, n, m->arg_val,
+                  m->arg_idx, m->arg_nan) &&
+           launch(c, rows_argmax_merge_kernel, dim3(rows), dim3(32), 0, static_cast<const float *>(m->arg_val),
+                  static_cast<const uint32_t *>(m->arg_idx), static_cast<const uint32_t *>(m->arg_nan), chunks, out,
+                  out_val);
+}
+
 // Greedy token of one row from the head's per-block candidates: the local
 // merge, then (tensor-parallel) the first maximum over the ranks' slices.
 bool greedy_choice(plamo_cuda *c, DModel *m, uint32_t grid) {
@@ -786,6 +847,61 @@ bool record_decode(plamo_cuda *c, DModel *m) {
     return !m->tp.active || launch(c, tp_epoch_kernel, dim3(1), dim3(32), 0, m->tp.epoch);
 }
 
+// Advance the row counters of every request of a batch by one.
+__global__ void batch_advance_kernel(uint64_t *const *counters, uint64_t layers, uint32_t requests) {
+    pdl_wait();
+    for (uint32_t i = threadIdx.x; i < layers * requests; i += blockDim.x) counters[i / layers][i % layers] += 1;
+}
+
+// One decode step of every request of a batch, layer-major over B rows: the
+// prompt kernels for the norms and the (tcgen05, split-K) projections, the
+// fused decode attention per request on its own cache, the head over all
+// rows and a greedy choice per row into the token buffer.
+bool record_batch(plamo_cuda *c, plamo_cuda_batch *b, DModel *m) {
+    const uint64_t T = b->B, H = m->H;
+    const uint32_t G = static_cast<uint32_t>(m->QH / m->KH);
+    if (!launch(c, embed_rows_kernel, dim3(T), dim3(256), 0, m->emb, static_cast<const uint32_t *>(b->d_tokens), m->V,
+                H, m->p_states, m->d_error))
+        return false;
+    for (uint64_t l = 0; l < m->L; ++l) {
+        const DLayer &L = m->layers[l];
+        bool ok;
+        if (l == 0)
+            ok = launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
+                        static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, L.pre,
+                        1.0f, m->p_norm, H);
+        else
+            ok = launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
+                        static_cast<const float *>(m->p_branch), m->layers[l - 1].mpost, kPostMlpOffset, L.pre,
+                        1.0f, m->p_norm, H);
+        if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H)) return false;
+        if (!launch(c, decode_attention128_batch_kernel, dim3(static_cast<uint32_t>(m->KH), kDecSplits, b->B),
+                    dim3(kDecThreads), decode_attention128_smem(G),
+                    static_cast<const DecodeAttnParams *>(b->d_attn + l * b->B)))
+            return false;
+        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
+        if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
+                    static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H))
+            return false;
+        if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H)) return false;
+        if (!launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((m->I * T + 255) / 256, 4096)), dim3(256), 0,
+                    m->p_gu, m->I, T))
+            return false;
+        if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
+    }
+    if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(512), 0, m->p_states,
+                static_cast<const float *>(m->p_branch), m->layers[m->L - 1].mpost, kPostMlpOffset,
+                static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H) ||
+        !launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
+                static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, m->norm, 1.0f,
+                m->p_norm, H) ||
+        !projection(c, m, m->p_norm, H, m->head, m->p_logits, m->V, T, m->V, H) ||
+        !rows_argmax(c, m, m->p_logits, m->V, static_cast<uint32_t>(T), b->d_tokens, nullptr))
+        return false;
+    return launch(c, batch_advance_kernel, dim3(1), dim3(256), 0, static_cast<uint64_t *const *>(b->d_counters), m->L,
+                  b->B);
+}
+
 bool ensure_graph(plamo_cuda *c, DModel *m) {
     if (m->graph_exec) return true;
     if (!note(c, "capture", cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal)))
@@ -875,11 +991,11 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
         const DLayer &L = m->layers[l];
         bool ok;
         if (l == 0)
-            ok = launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(256), 0, m->p_states,
+            ok = launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
                         static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, L.pre,
                         1.0f, m->p_norm, H);
         else
-            ok = launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(256), 0, m->p_states,
+            ok = launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
                         static_cast<const float *>(m->p_branch), m->layers[l - 1].mpost, kPostMlpOffset, L.pre,
                         1.0f, m->p_norm, H);
         if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H)) return false;
@@ -902,7 +1018,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
         }
         if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
         if (m->tp.active && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l)) return false;
-        if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(256), 0, m->p_states,
+        if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
                     static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H))
             return false;
         if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H)) return false;
@@ -912,12 +1028,12 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
         if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
         if (m->tp.active && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l + 1)) return false;
     }
-    if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(256), 0, m->p_states,
+    if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(512), 0, m->p_states,
                 static_cast<const float *>(m->p_branch), m->layers[m->L - 1].mpost, kPostMlpOffset,
                 static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H))
         return false;
     if (need_all_logits) {
-        if (!launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(256), 0, m->p_states,
+        if (!launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
                     static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, m->norm,
                     1.0f, m->p_norm, H))
             return false;
@@ -1006,6 +1122,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_gemm = !tc || strcmp(tc, "0");
     const char *pa = getenv("PLAMO_CUDA_PROMPT_ATTN");
     c->prompt_attn = !pa || strcmp(pa, "0");
+    const char *tc_st = getenv("PLAMO_CUDA_TC_STAGES");
+    c->tc_stages = tc_st ? std::max(2, std::min(atoi(tc_st), kTcMaxStages)) : 0;
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
     c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
@@ -1022,6 +1140,9 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg.device);
     c->smem_optin = optin;
+    int per_sm = 0;
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, cfg.device);
+    c->smem_per_sm = per_sm > 0 ? per_sm : optin;
     set_gemv_smem_limits<PRO_X, EPI_STORE>(optin);
     set_gemv_smem_limits<PRO_NORM, EPI_STORE>(optin);
     set_gemv_smem_limits<PRO_RESID_NORM, EPI_STORE>(optin);
@@ -1037,6 +1158,7 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     allow_smem(gemm_tc_kernel<64>, optin);
     allow_smem(gemm_tc_kernel<128>, optin);
     allow_smem(decode_attention_kernel<128>, optin);
+    allow_smem(decode_attention128_batch_kernel, optin);
     allow_smem(decode_attention_kernel<0>, optin);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         if (error && cap) snprintf(error, cap, "cannot configure kernels: %s", cudaGetErrorString(e));
@@ -1279,6 +1401,7 @@ static int prepare_impl(struct plamo_cuda *c, struct model *model, uint64_t head
     m->v_kv = static_cast<float *>(dalloc(c, m.get(), m->L * kVerifyMax * 2 * m->KVW * 4));
     const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(H, m->AW), m->I);
     m->p_split = static_cast<uint16_t *>(dalloc(c, m.get(), 3 * T * kmax * 2));
+    m->p_splitk = static_cast<float *>(dalloc(c, m.get(), kSplitkFloats * 4));
     for (void *p : m->allocations)
         if (!p) return 0;
     c->info.workspace_bytes += c->info.allocated_bytes - before;
@@ -1497,8 +1620,8 @@ int plamo_cuda_verify(struct plamo_cuda *c, struct model *model, const uint32_t 
     cudaEventRecord(c->ev0, c->stream);
     if (!record_prompt(c, m, tokens, 1, true)) return -1;
     const bool tp = m->tp.active;
-    if (!launch(c, rows_argmax_kernel, dim3(tokens), dim3(256), 0, static_cast<const float *>(m->p_logits), m->Vh,
-                tp ? m->tp.lidx : m->p_next, tp ? m->tp.lval : nullptr))
+    if (!rows_argmax(c, m, m->p_logits, m->Vh, static_cast<uint32_t>(tokens), tp ? m->tp.lidx : m->p_next,
+                     tp ? m->tp.lval : nullptr))
         return -1;
     if (tp && (!launch(c, tp_argmax_kernel, dim3(1), dim3(128), 0, static_cast<const float *>(m->tp.lval),
                        static_cast<const uint32_t *>(m->tp.lidx), static_cast<uint32_t>(tokens),
@@ -1629,7 +1752,7 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
     d.x = m->mid;
     d.y = m->branch;
     ok = ok && gemv<PRO_X, EPI_STORE>(c, d);
-    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(1), dim3(256), 0, m->state[1],
+    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(1), dim3(512), 0, m->state[1],
                       static_cast<const float *>(m->branch), L.mpost, kPostMlpOffset,
                       static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), m->H);
     ok = ok && launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended + index, uint64_t{1}, uint64_t{1});
@@ -1784,13 +1907,13 @@ int plamo_cuda_mlp(struct plamo_cuda *c, const struct mlp *p, float *states, uin
               note(c, "mlp alloc", cudaMalloc(&g, tokens * 2 * I * 4)) &&
               note(c, "mlp alloc", cudaMalloc(&b, tokens * H * 4));
     ok = ok && note(c, "mlp in", cudaMemcpyAsync(s, states, tokens * H * 4, cudaMemcpyHostToDevice, c->stream));
-    ok = ok && launch(c, norm_rows_kernel<ROW_NORM>, dim3(tokens), dim3(256), 0, s, static_cast<const float *>(nullptr),
+    ok = ok && launch(c, norm_rows_kernel<ROW_NORM>, dim3(tokens), dim3(512), 0, s, static_cast<const float *>(nullptr),
                       static_cast<const uint16_t *>(nullptr), 0.0f, pre, 1.0f, n, H);
     ok = ok && gemm(c, n, H, gu, g, 2 * I, tokens, 2 * I, H);
     ok = ok && launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((I * tokens + 255) / 256, 4096)), dim3(256), 0,
                       g, I, tokens);
     ok = ok && gemm(c, g, 2 * I, down, b, H, tokens, H, I);
-    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(tokens), dim3(256), 0, s, static_cast<const float *>(b),
+    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(tokens), dim3(512), 0, s, static_cast<const float *>(b),
                       post, kPostMlpOffset, static_cast<const uint16_t *>(nullptr), 0.0f,
                       static_cast<float *>(nullptr), H);
     ok = ok && note(c, "mlp out", cudaMemcpyAsync(states, s, tokens * H * 4, cudaMemcpyDeviceToHost, c->stream)) &&
@@ -1855,11 +1978,17 @@ int plamo_cuda_gemm_device(struct plamo_cuda *c, const float *x, uint64_t xs, co
     if (!c) return 0;
     cudaSetDevice(c->device);
     uint16_t *split = nullptr;
+    float *part = nullptr;
     const uint64_t n = std::max<uint64_t>(tokens * cols, 1);
-    if (!note(c, "gemm scratch", cudaMalloc(&split, 3 * n * 2))) return -1;
-    const bool ok = projection_with(c, x, xs, w, y, ys, tokens, rows, cols, split, nullptr) &&
+    if (!note(c, "gemm scratch", cudaMalloc(&split, 3 * n * 2)) ||
+        !note(c, "gemm scratch", cudaMalloc(&part, kSplitkFloats * 4))) {
+        cudaFree(split);
+        return -1;
+    }
+    const bool ok = projection_with(c, x, xs, w, y, ys, tokens, rows, cols, split, nullptr, part, kSplitkFloats) &&
                     note(c, "gemm", cudaStreamSynchronize(c->stream));
     cudaFree(split);
+    cudaFree(part);
     return ok ? 1 : -1;
 }
 
@@ -1868,19 +1997,175 @@ double plamo_cuda_time_gemm(struct plamo_cuda *c, const float *x, const uint16_t
     if (!c || !repeats) return -1;
     cudaSetDevice(c->device);
     uint16_t *split = nullptr;
+    float *part = nullptr;
     const uint64_t n = std::max<uint64_t>(tokens * cols, 1);
-    if (!note(c, "gemm scratch", cudaMalloc(&split, 3 * n * 2))) return -1;
+    if (!note(c, "gemm scratch", cudaMalloc(&split, 3 * n * 2)) ||
+        !note(c, "gemm scratch", cudaMalloc(&part, kSplitkFloats * 4))) {
+        cudaFree(split);
+        return -1;
+    }
     cudaStreamSynchronize(c->stream);
     cudaEventRecord(c->ev0, c->stream);
     bool ok = true;
     for (uint64_t i = 0; i < repeats && ok; ++i)
-        ok = projection_with(c, x, cols, w, y, rows, tokens, rows, cols, split, nullptr);
+        ok = projection_with(c, x, cols, w, y, rows, tokens, rows, cols, split, nullptr, part, kSplitkFloats);
     cudaEventRecord(c->ev1, c->stream);
     ok = ok && note(c, "time gemm", cudaStreamSynchronize(c->stream));
     float ms = 0;
     cudaEventElapsedTime(&ms, c->ev0, c->ev1);
     cudaFree(split);
+    cudaFree(part);
     return ok ? ms : -1;
+}
+
+struct plamo_cuda_batch *plamo_cuda_batch_open(struct plamo_cuda *c, struct model *const *models, unsigned count) {
+    if (!c || !models || !count || count > kVerifyMax) return nullptr;
+    cudaSetDevice(c->device);
+    std::vector<DModel *> ms;
+    for (unsigned i = 0; i < count; ++i) {
+        DModel *m = models[i] ? find_model(c, models[i]) : nullptr;
+        if (!m || m->tp.size || m->D != 128 || m->QH / m->KH > 32 || m->tmax < count) return nullptr;
+        for (DModel *o : ms)
+            if (o == m) return nullptr;  // one cache per request
+        ms.push_back(m);
+    }
+    const DModel *m0 = ms[0];
+    for (const DModel *m : ms) {
+        if (m->H != m0->H || m->QH != m0->QH || m->KH != m0->KH || m->I != m0->I || m->V != m0->V ||
+            m->L != m0->L || m->emb != m0->emb || m->head != m0->head || m->norm != m0->norm)
+            return nullptr;
+        for (uint64_t l = 0; l < m->L; ++l) {
+            const DLayer &a = m->layers[l], &z = m0->layers[l];
+            if (a.qkv_w != z.qkv_w || a.o_w != z.o_w || a.gu != z.gu || a.down != z.down || a.pre != z.pre ||
+                a.post != z.post || a.mpre != z.mpre || a.mpost != z.mpost || a.qn != z.qn || a.kn != z.kn ||
+                a.scale != z.scale || a.sliding != z.sliding)
+                return nullptr;
+        }
+    }
+    auto b = std::make_unique<plamo_cuda_batch>();
+    b->c = c;
+    b->B = count;
+    b->graph = nullptr;
+    b->exec = nullptr;
+    b->nodes = 0;
+    for (unsigned i = 0; i < count; ++i) b->hosts.push_back(models[i]);
+    std::vector<DecodeAttnParams> params;
+    for (uint64_t l = 0; l < m0->L; ++l)
+        for (unsigned i = 0; i < count; ++i)
+            params.push_back(DecodeAttnParams{attn_layer(ms[i], l), static_cast<uint32_t>(m0->QH),
+                                              static_cast<uint32_t>(m0->KH), static_cast<uint32_t>(m0->D),
+                                              m0->p_qkv + i * m0->QW, m0->p_attn + i * m0->AW});
+    std::vector<uint64_t *> counters;
+    for (DModel *m : ms) counters.push_back(m->d_appended);
+    b->d_attn = nullptr;
+    b->d_counters = nullptr;
+    b->d_tokens = nullptr;
+    bool ok = note(c, "batch alloc", cudaMalloc(&b->d_attn, params.size() * sizeof(DecodeAttnParams))) &&
+              note(c, "batch alloc", cudaMalloc(&b->d_counters, count * sizeof(uint64_t *))) &&
+              note(c, "batch alloc", cudaMalloc(&b->d_tokens, 64 * 4)) &&
+              note(c, "batch params", cudaMemcpy(b->d_attn, params.data(), params.size() * sizeof(DecodeAttnParams),
+                                                 cudaMemcpyHostToDevice)) &&
+              note(c, "batch params", cudaMemcpy(b->d_counters, counters.data(), count * sizeof(uint64_t *),
+                                                 cudaMemcpyHostToDevice));
+    if (ok) {
+        ok = note(c, "capture", cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        if (ok) {
+            const uint64_t before = c->info.launches;
+            const bool rec = record_batch(c, b.get(), ms[0]);
+            const cudaError_t e = cudaStreamEndCapture(c->stream, &b->graph);
+            b->nodes = c->info.launches - before;
+            c->info.launches = before;
+            ok = rec && note(c, "capture end", e) &&
+                 note(c, "instantiate", cudaGraphInstantiate(&b->exec, b->graph, 0));
+        }
+    }
+    if (!ok) {
+        plamo_cuda_batch_close(b.release());
+        return nullptr;
+    }
+    return b.release();
+}
+
+// Preflight of `steps` batch steps: every request prepared, reconciled with
+// its host counts and able to take the rows.
+static bool batch_ready(plamo_cuda_batch *b, uint64_t steps, std::vector<DModel *> &ms) {
+    plamo_cuda *c = b->c;
+    for (struct model *h : b->hosts) {
+        DModel *m = find_model(c, h);
+        if (!m || !reconcile(c, m) || !fits(m, steps)) return false;
+        m->verify_valid = false;
+        ms.push_back(m);
+    }
+    return true;
+}
+
+int plamo_cuda_batch_step(struct plamo_cuda_batch *b, const uint32_t *tokens, uint32_t *next) {
+    if (!b || !tokens || !next) return 0;
+    plamo_cuda *c = b->c;
+    cudaSetDevice(c->device);
+    std::vector<DModel *> ms;
+    for (uint32_t i = 0; i < b->B; ++i)
+        if (tokens[i] >= b->hosts[0]->vocab) {
+            c->info.declines++;
+            return 0;
+        }
+    if (!batch_ready(b, 1, ms)) {
+        c->info.declines++;
+        return 0;
+    }
+    memcpy(c->pinned_u32 + 32, tokens, b->B * 4);
+    cudaEventRecord(c->ev0, c->stream);
+    bool ok = note(c, "batch tokens", cudaMemcpyAsync(b->d_tokens, c->pinned_u32 + 32, b->B * 4,
+                                                      cudaMemcpyHostToDevice, c->stream)) &&
+              note(c, "batch graph", cudaGraphLaunch(b->exec, c->stream));
+    cudaEventRecord(c->ev1, c->stream);
+    ok = ok && note(c, "batch next", cudaMemcpyAsync(c->pinned_u32 + 32, b->d_tokens, b->B * 4,
+                                                     cudaMemcpyDeviceToHost, c->stream)) &&
+         note(c, "batch step", cudaStreamSynchronize(c->stream));
+    if (!ok || !check_device_error(c, ms[0])) return -1;
+    c->info.graph_launches++;
+    c->info.launches += b->nodes;
+    c->info.forwards += b->B;
+    c->info.gpu_seconds += elapsed(c);
+    memcpy(next, c->pinned_u32 + 32, b->B * 4);
+    for (DModel *m : ms) {
+        publish_counts(m, 1);
+        if (c->config.copy_kv_to_host && !sync_kv(c, m)) return -1;
+    }
+    return 1;
+}
+
+double plamo_cuda_time_batch(struct plamo_cuda_batch *b, uint64_t steps) {
+    if (!b || !steps) return -1;
+    plamo_cuda *c = b->c;
+    cudaSetDevice(c->device);
+    std::vector<DModel *> ms;
+    if (!batch_ready(b, steps, ms)) return -1;
+    cudaStreamSynchronize(c->stream);
+    cudaEventRecord(c->ev0, c->stream);
+    bool ok = true;
+    for (uint64_t i = 0; i < steps && ok; ++i) ok = note(c, "batch graph", cudaGraphLaunch(b->exec, c->stream));
+    cudaEventRecord(c->ev1, c->stream);
+    ok = ok && note(c, "time batch", cudaStreamSynchronize(c->stream));
+    if (!ok || !check_device_error(c, ms[0])) return -1;
+    c->info.graph_launches += steps;
+    c->info.launches += b->nodes * steps;
+    for (DModel *m : ms) publish_counts(m, steps);
+    float ms_total = 0;
+    cudaEventElapsedTime(&ms_total, c->ev0, c->ev1);
+    return ms_total;
+}
+
+void plamo_cuda_batch_close(struct plamo_cuda_batch *b) {
+    if (!b) return;
+    cudaSetDevice(b->c->device);
+    cudaStreamSynchronize(b->c->stream);
+    if (b->exec) cudaGraphExecDestroy(b->exec);
+    if (b->graph) cudaGraphDestroy(b->graph);
+    cudaFree(b->d_attn);
+    cudaFree(b->d_counters);
+    cudaFree(b->d_tokens);
+    delete b;
 }
 
 int plamo_cuda_rollback(struct plamo_cuda *c, struct model *model, uint64_t rows) {

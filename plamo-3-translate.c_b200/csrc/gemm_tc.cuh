@@ -11,7 +11,7 @@
 //
 // The tensor cores truncate while they accumulate, so error grows with the
 // number of MMAs chained into one accumulator. Each 64-wide K block therefore
-// gets a fresh accumulator (two in TMEM, double-buffered) and the epilogue
+// gets a fresh accumulator (a ring of 2..16 in TMEM, see tc_acc_count) and the epilogue
 // warps fold every block into FP32 registers with round-to-nearest adds: no
 // tensor-core chain is longer than one block, whatever K is.
 //
@@ -24,6 +24,12 @@
 //   warps 2-5   epilogue: tcgen05.ld of their TMEM lane quadrant, stores of
 //               Y[token][row] (coalesced along rows).
 // All waits are bounded; a timeout sets an error flag and the CTA drains.
+//
+// Split K (gridDim.z > 1, for a few tokens over few row tiles, e.g. the
+// projections of a verification block or of a batch of decode requests): CTA
+// z folds K blocks [z*kb/splits, (z+1)*kb/splits) and writes its partial tile
+// to part[z]; splitk_sum_kernel adds the partials in z order, so the result
+// does not depend on scheduling.
 #pragma once
 #include <cuda.h>
 
@@ -35,8 +41,15 @@ namespace plamo {
 constexpr int kTcM = 128;
 constexpr int kTcK = 64;  // BF16 elements per stage row: 128 bytes, one swizzle atom
 constexpr int kTcThreads = 192;
-constexpr int kTcMaxStages = 6;
-constexpr int kTcAcc = 2;    // TMEM accumulators (double buffer), one K block each
+constexpr int kTcMaxStages = 10;
+constexpr int kTcAccMax = 16;
+// TMEM accumulators (one K block each) in a ring of 256 columns: with few
+// tokens per tile a K block is quick to multiply, so the MMAs may run up to
+// 16 blocks ahead of the epilogue's folds instead of stalling on it.
+template <int N>
+__host__ __device__ constexpr int tc_acc_count() {
+    return N <= 16 ? 16 : N <= 32 ? 8 : N <= 64 ? 4 : 2;
+}
 constexpr int kTcTerms = 3;  // BF16 terms of each FP32 activation
 
 struct TcGemmParams {
@@ -44,6 +57,7 @@ struct TcGemmParams {
     uint64_t ys;
     uint32_t T, R, K;
     uint32_t *error;
+    float *part;  // split K: [splits][T][R] partial tiles
 };
 
 // ---- tcgen05 / TMA primitives ------------------------------------------------
@@ -103,6 +117,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive FP32 accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 inline size_t tc_stage_bytes(uint32_t n) { return static_cast<size_t>(kTcM) * 128 + kTcTerms * 128ull * n; }
 inline size_t tc_smem_bytes(uint32_t n, int stages) { return stages * tc_stage_bytes(n) + 1024; }
 
@@ -115,8 +143,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(128) unsigned char tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kTcMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kTcMaxStages];
-    __shared__ __align__(8) uint64_t acc_full[kTcAcc];
-    __shared__ __align__(8) uint64_t acc_empty[kTcAcc];
+    constexpr int kTcAcc = tc_acc_count<N>();
+    __shared__ __align__(8) uint64_t acc_full[kTcAccMax];
+    __shared__ __align__(8) uint64_t acc_empty[kTcAccMax];
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
 
@@ -128,7 +157,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // Token tiles run fastest: the CTAs that share one weight tile start
     // together, so it crosses HBM once and the others read it from L2.
     const uint32_t row0 = blockIdx.y * kTcM, tok0 = blockIdx.x * N;
-    const uint32_t kblocks = (p.K + kTcK - 1) / kTcK;
+    const uint32_t kall = (p.K + kTcK - 1) / kTcK;
+    const uint32_t kb0 = kall * blockIdx.z / gridDim.z;
+    const uint32_t kblocks = kall * (blockIdx.z + 1) / gridDim.z - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -170,7 +201,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             unsigned char *st = base + s * stage_bytes;
             mbar_expect_tx(&full_bar[s], stage_bytes);
-            const int kx = static_cast<int>(kb * kTcK);
+            const int kx = static_cast<int>((kb0 + kb) * kTcK);
             tma_load_2d(st, &map_w, kx, static_cast<int>(row0), &full_bar[s]);
             tma_load_2d(st + kTcM * 128, &map_hi, kx, static_cast<int>(tok0), &full_bar[s]);
             tma_load_2d(st + kTcM * 128 + N * 128, &map_mid, kx, static_cast<int>(tok0), &full_bar[s]);
@@ -235,12 +266,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 break;
             }
             tc_fence_after();
+            if constexpr (N == 16) {
+                float v[16];
+                tmem_ld16(tmem + lanes + a * N, v);
 #pragma unroll
-            for (int c = 0; c < N; c += 32) {
-                float v[32];
-                tmem_ld32(tmem + lanes + a * N + c, v);
+                for (int i = 0; i < 16; ++i) sum[i] = __fadd_rn(sum[i], v[i]);
+            } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sum[c + i] = __fadd_rn(sum[c + i], v[i]);
+                for (int c = 0; c < N; c += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + lanes + a * N + c, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) sum[c + i] = __fadd_rn(sum[c + i], v[i]);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -248,10 +286,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         const uint32_t row = row0 + quad * 32 + lane;
         if (ok && row < p.R) {
+            float *out = gridDim.z > 1 ? p.part + static_cast<uint64_t>(blockIdx.z) * p.T * p.R : p.y;
+            const uint64_t stride = gridDim.z > 1 ? p.R : p.ys;
 #pragma unroll
             for (int j = 0; j < N; ++j) {
                 const uint32_t t = tok0 + j;
-                if (t < p.T) p.y[static_cast<uint64_t>(t) * p.ys + row] = sum[j];
+                if (t < p.T) out[static_cast<uint64_t>(t) * stride + row] = sum[j];
             }
         }
     }
@@ -260,6 +300,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+    }
+}
+
+// y[t][r] = sum over z (in order) of part[z][t][r].
+__global__ void splitk_sum_kernel(const float *part, uint32_t splits, uint32_t T, uint32_t R, float *y, uint64_t ys) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint64_t total = static_cast<uint64_t>(T) * R, plane = total;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        float s = part[i];
+        for (uint32_t z = 1; z < splits; ++z) s = __fadd_rn(s, part[z * plane + i]);
+        const uint64_t t = i / R, r = i - t * R;
+        y[t * ys + r] = s;
     }
 }
 

@@ -674,16 +674,20 @@ __global__ void argmax_merge_kernel(const float *val, const uint32_t *idx, const
     }
 }
 
-// Greedy choice of every row of a [rows][n] logits block (verification).
-__global__ void rows_argmax_kernel(const float *logits, uint64_t n, uint32_t *out, float *out_val) {
+// Greedy choice of every row of a [rows][n] logits block, two passes: grid
+// (chunks, rows) of per-chunk candidates, then one merge block per row.
+__global__ void rows_argmax_partial_kernel(const float *logits, uint64_t n, float *val, uint32_t *idx,
+                                           uint32_t *nan_flag) {
     __shared__ float sv[32];
     __shared__ uint32_t si[32];
     __shared__ uint32_t sn[32];
     pdl_wait();
-    const float *x = logits + blockIdx.x * n;
+    const uint32_t row = blockIdx.y, chunk = blockIdx.x, chunks = gridDim.x;
+    const uint64_t c0 = n * chunk / chunks, c1 = n * (chunk + 1) / chunks;
+    const float *x = logits + row * n;
     float bv = -__int_as_float(0x7f800000);
     uint32_t bi = 0xffffffffu, nan_seen = 0;
-    for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    for (uint64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
         const float v = x[i];
         if (v != v) nan_seen = 1;
         else if (arg_better(v, static_cast<uint32_t>(i), bv, bi)) {
@@ -716,9 +720,32 @@ __global__ void rows_argmax_kernel(const float *logits, uint64_t n, uint32_t *ou
                 bi = si[w];
             }
         }
-        out[blockIdx.x] = nan_seen ? 0xffffffffu : bi;
-        if (out_val) out_val[blockIdx.x] = bv;
+        val[row * chunks + chunk] = bv;
+        idx[row * chunks + chunk] = bi;
+        nan_flag[row * chunks + chunk] = nan_seen;
     }
+    pdl_launch_dependents();
+}
+
+// One block per row: merge that row's chunk candidates (argmax_merge_kernel's
+// rule) into out[row] (UINT32_MAX on NaN) and, when given, out_val[row].
+__global__ void rows_argmax_merge_kernel(const float *val, const uint32_t *idx, const uint32_t *nan_flag,
+                                         uint32_t chunks, uint32_t *out, float *out_val) {
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    const uint32_t row = blockIdx.x;
+    float bv = -__int_as_float(0x7f800000);
+    uint32_t bi = 0xffffffffu, nan_seen = 0;
+    for (uint32_t c = 0; c < chunks; ++c) {
+        const uint32_t k = row * chunks + c;
+        nan_seen |= nan_flag[k];
+        if (arg_better(val[k], idx[k], bv, bi)) {
+            bv = val[k];
+            bi = idx[k];
+        }
+    }
+    out[row] = nan_seen ? 0xffffffffu : bi;
+    if (out_val) out_val[row] = bv;
 }
 
 }  // namespace plamo

@@ -27,12 +27,71 @@ enum RowMode { ROW_NORM = 0, ROW_RESID = 1, ROW_RESID_NORM = 2 };
 //   ROW_NORM:       out = rmsnorm(states, w2, off2)
 //   ROW_RESID:      states += rmsnorm(branch, w1, off1)
 //   ROW_RESID_NORM: both, the norm reading the updated state.
+// Rows of a multiple of 4 floats take 128-bit loads, each thread holding its
+// float4s in registers between the two norms (up to 4 per thread).
 template <int MODE>
 __global__ void norm_rows_kernel(float *states, const float *branch, const uint16_t *w1, float off1,
                                  const uint16_t *w2, float off2, float *out, uint64_t hidden) {
     __shared__ float red[32];
     pdl_wait();
     float *x = states + static_cast<uint64_t>(blockIdx.x) * hidden;
+    const uint32_t nt = blockDim.x;
+    if (hidden % 4 == 0 && hidden <= 16ull * nt) {
+        const uint32_t n4 = static_cast<uint32_t>(hidden / 4);
+        float4 st[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t i = threadIdx.x + k * nt;
+            if (i < n4) st[k] = ld4(x + 4 * i);
+        }
+        if (MODE != ROW_NORM) {
+            const float *b = branch + static_cast<uint64_t>(blockIdx.x) * hidden;
+            float4 br[4];
+            uint2 wv[4];
+            float s = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t i = threadIdx.x + k * nt;
+                if (i < n4) {
+                    br[k] = ld4(b + 4 * i);
+                    wv[k] = *reinterpret_cast<const uint2 *>(w1 + 4 * i);
+                    s += sq4(br[k]);
+                }
+            }
+            const float inv = rms_inverse(block_sum(s, red), hidden);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t i = threadIdx.x + k * nt;
+                if (i < n4) {
+                    const float4 v = apply4(br[k], inv, norm4(wv[k], off1));
+                    st[k] = make_float4(__fadd_rn(st[k].x, v.x), __fadd_rn(st[k].y, v.y), __fadd_rn(st[k].z, v.z),
+                                        __fadd_rn(st[k].w, v.w));
+                    *reinterpret_cast<float4 *>(x + 4 * i) = st[k];
+                }
+            }
+        }
+        if (MODE != ROW_RESID) {
+            float s = 0.0f;
+            uint2 wv[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t i = threadIdx.x + k * nt;
+                if (i < n4) {
+                    wv[k] = *reinterpret_cast<const uint2 *>(w2 + 4 * i);
+                    s += sq4(st[k]);
+                }
+            }
+            const float inv = rms_inverse(block_sum(s, red), hidden);
+            float *o = out + static_cast<uint64_t>(blockIdx.x) * hidden;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t i = threadIdx.x + k * nt;
+                if (i < n4) *reinterpret_cast<float4 *>(o + 4 * i) = apply4(st[k], inv, norm4(wv[k], off2));
+            }
+        }
+        pdl_launch_dependents();
+        return;
+    }
     if (MODE != ROW_NORM) {
         const float *b = branch + static_cast<uint64_t>(blockIdx.x) * hidden;
         float s = 0.0f;

@@ -227,10 +227,12 @@ class HostModel:
 
     weights: "synthetic" (generated in HBM by `Backend.preload_synthetic`),
     a numpy uint16 blob laid out by `self.offsets`, or None to allocate a zero
-    blob the caller fills.
+    blob the caller fills. weights_of: another HostModel of the same profile
+    whose weights this one shares (same host keys, so the same device copies):
+    a second request with its own descriptors and KV cache.
     """
 
-    def __init__(self, profile, layer_specs=None, weights=None, full_capacity=None):
+    def __init__(self, profile, layer_specs=None, weights=None, full_capacity=None, weights_of=None):
         p = self.profile = profile
         self.specs = layer_specs or default_layer_specs(p, full_capacity)
         assert len(self.specs) == p.layers
@@ -242,7 +244,14 @@ class HostModel:
         self.blob_bytes = total
         self._keep = []
         self.synthetic = isinstance(weights, str) and weights == "synthetic"
-        if self.synthetic:
+        if weights_of is not None:
+            assert weights_of.blob_bytes == total and weights_of.profile == p
+            self.synthetic = weights_of.synthetic
+            self.reservation = getattr(weights_of, "reservation", None)
+            self.blob = weights_of.blob
+            self._keep.append(weights_of)
+            base = weights_of.base
+        elif self.synthetic:
             self.reservation = _Reservation(total)
             self.blob = None
             base = self.reservation.address

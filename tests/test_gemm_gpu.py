@@ -44,7 +44,9 @@ def gpu_gemm(backend, w, x):
 
 @pytest.mark.parametrize("T,R,K", [(1, 128, 64), (5, 200, 128), (16, 256, 4096), (17, 130, 72), (31, 384, 512),
                                    (64, 1000, 256), (100, 5120, 4096), (129, 512, 1024), (455, 640, 4096),
-                                   (455, 4096, 16384)])
+                                   (455, 4096, 16384),
+                                   # split K (few tokens over few row tiles): verify / batched decode shapes
+                                   (8, 5120, 4096), (12, 4096, 16384), (3, 1000, 520)])
 def test_tc_projection_matches_oracle(backend, T, R, K):
     rng = np.random.default_rng(T * 131 + R * 7 + K)
     w = np.ascontiguousarray(synthetic.bf16_round(rng.normal(0, 0.02, size=(R, K)).astype(np.float32)))
