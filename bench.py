@@ -54,6 +54,16 @@ def load_package():
     return mod
 
 
+def measured_traffic():
+    """ncu-measured DRAM traffic (profiles/traffic.json; commands in
+    profiles/dram_traffic_decode.md), or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f)
+
+
 def measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -326,6 +336,7 @@ def run_ours(args, world, rank, local, dist):
         del host, blob
 
     if rank == 0:
+        traffic = measured_traffic()
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -334,11 +345,16 @@ def run_ours(args, world, rank, local, dist):
             "prefill_tok_s": prefill_rate,
             "roofline": {"bound": "hbm", "kernel": "decode step (one CUDA graph launch per token)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": (step_bytes * traffic["decode_step_ratio"]["ratio"]) if traffic else None,
+                         "traffic_source": ("ncu DRAM bytes of a 2B decode step, traffic/algorithmic ratio "
+                                            "applied to this step") if traffic else None,
                          "algorithmic_bytes": step_bytes, "peak_source": peak_src},
             "gemv_roofline": {"bound": "hbm", "kernel": "gemv 32768x4096 bf16 (gate_up shape)",
                               "achieved": gemv_bytes / (gemv_ms / 1000) / 1e9, "peak": peak,
                               "unit": "GB/s", "frac": gemv_bytes / (gemv_ms / 1000) / 1e9 / peak,
+                              "traffic": (traffic["gemv_gate_up_8b"]["dram_read"] +
+                                          traffic["gemv_gate_up_8b"]["dram_write"]) if traffic else None,
                               "ms": gemv_ms},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4, "api": "plamo_cuda_generate (per-token host round trip)"},
@@ -519,6 +535,63 @@ def run_tp31b(args, world, rank, local, dist):
     be.close()
 
 
+def run_profile(args):
+    """Small fixed workloads for ncu captures (profiles/ gives the commands).
+    Each prints the launch count before the part to capture (ncu -s) and the
+    number of kernels it launches (ncu -c)."""
+    pkg = load_package()
+    lib = pkg.load()
+    be = pkg.Backend(device=0, max_context=8208, max_prefill=512)
+    ctx = be.ctx
+    shape = [int(x) for x in args.shape.split(",")] if args.shape else []
+    if args.profile in ("gemv", "gemm"):
+        if args.profile == "gemv":
+            (rows, cols), tokens = shape, 1
+        else:
+            tokens, rows, cols = shape
+        dw = lib.plamo_cuda_device_alloc(ctx, rows * cols * 2)
+        dx = lib.plamo_cuda_device_alloc(ctx, tokens * cols * 4)
+        dy = lib.plamo_cuda_device_alloc(ctx, tokens * rows * 4)
+        lib.plamo_cuda_fill_synthetic_bf16(ctx, dw, rows * cols, 9, 0.0, 0.02)
+        lib.plamo_cuda_fill_synthetic_f32(ctx, dx, tokens * cols, 8, 0.0, 1.0)
+        timed = (lambda n: lib.plamo_cuda_time_gemv(ctx, dw, dx, dy, rows, cols, n)) if args.profile == "gemv" \
+            else (lambda n: lib.plamo_cuda_time_gemm(ctx, dx, dw, dy, tokens, rows, cols, n))
+        timed(2)
+        before = lib.plamo_cuda_kernel_launches(ctx)
+        ms = timed(1)
+    else:
+        profile = pkg.PROFILES[args.model]
+        hm = pkg.HostModel(profile, weights="synthetic", full_capacity=8208)
+        be.preload_synthetic(hm, seed=4)
+        reqs = [hm] + [pkg.HostModel(profile, weights_of=hm, full_capacity=8208)
+                       for _ in range((args.requests if args.profile == "batch" else 1) - 1)]
+        nxt = ctypes.c_uint32()
+        toks = np.zeros(len(reqs), dtype=np.uint32)
+        prompt = PROMPT if args.profile == "step" else 16
+        for i, r in enumerate(reqs):
+            be.prepare(r)
+            ids = np.random.default_rng(1 + i).integers(3, 100000, size=prompt).astype(np.uint32)
+            assert lib.plamo_cuda_prefill_greedy(ctx, r.ptr, ids.ctypes.data, prompt, ctypes.byref(nxt)) == 1
+            toks[i] = nxt.value
+        if args.profile == "step":
+            assert lib.plamo_cuda_time_decode(ctx, hm.ptr, 3) > 0
+            before = lib.plamo_cuda_kernel_launches(ctx)
+            ms = lib.plamo_cuda_time_decode(ctx, hm.ptr, 1)
+        else:
+            arr = (ctypes.c_void_p * len(reqs))(*[ctypes.addressof(r.model) for r in reqs])
+            batch = lib.plamo_cuda_batch_open(ctx, arr, len(reqs))
+            out = np.zeros(len(reqs), dtype=np.uint32)
+            assert lib.plamo_cuda_batch_step(batch, toks.ctypes.data, out.ctypes.data) == 1
+            assert lib.plamo_cuda_time_batch(batch, 3) > 0
+            before = lib.plamo_cuda_kernel_launches(ctx)
+            ms = lib.plamo_cuda_time_batch(batch, 1)
+            lib.plamo_cuda_batch_close(batch)
+    kernels = lib.plamo_cuda_kernel_launches(ctx) - before
+    print(json.dumps({"profile": args.profile, "launches_before": int(before), "kernels": int(kernels),
+                      "ms": ms}), flush=True)
+    be.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -527,7 +600,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["8b-decode", "31b-tp"], default="8b-decode")
+    ap.add_argument("--profile", choices=["step", "batch", "gemv", "gemm"],
+                    help="run one small fixed workload for an ncu capture instead of the benchmark")
+    ap.add_argument("--model", default="8b", help="profile of --profile step/batch")
+    ap.add_argument("--requests", type=int, default=8, help="requests of --profile batch")
+    ap.add_argument("--shape", default="", help="rows,cols (gemv) or tokens,rows,cols (gemm)")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     if args.warmup < 1 or args.steps < 1:
         ap.error("steps and warmup must be positive")
     if args.impl == "reference":
