@@ -94,6 +94,17 @@ struct plamo_matmul {
     float *output;
     uint64_t rows, columns, tokens, input_stride, output_stride;
 };
+/* Checkpoint mapping and weight schema records (reference runtime/model.h:65-74). */
+struct plamo_mapping {
+    void *base;
+    uint64_t bytes;
+};
+struct plamo_weight_spec {
+    const char *name;
+    uint64_t rank;
+    const uint64_t *shape;
+    void **slot;
+};
 
 #ifdef __cplusplus
 #define PLAMO_STATIC_ASSERT static_assert
@@ -109,6 +120,8 @@ PLAMO_STATIC_ASSERT(sizeof(struct mixer) == 56, "mixer ABI");
 PLAMO_STATIC_ASSERT(sizeof(struct mlp) == 80, "MLP ABI");
 PLAMO_STATIC_ASSERT(sizeof(struct layer) == 64, "layer ABI");
 PLAMO_STATIC_ASSERT(sizeof(struct plamo_matmul) == 64, "matmul ABI");
+PLAMO_STATIC_ASSERT(sizeof(struct plamo_mapping) == 16, "mapping ABI");
+PLAMO_STATIC_ASSERT(sizeof(struct plamo_weight_spec) == 32, "weight schema ABI");
 PLAMO_STATIC_ASSERT(offsetof(struct layer, mixer) == 40, "layer ABI");
 PLAMO_STATIC_ASSERT(offsetof(struct cache, count) == 24, "cache ABI");
 PLAMO_STATIC_ASSERT(offsetof(struct rotation, processed_count) == 56, "rotation ABI");

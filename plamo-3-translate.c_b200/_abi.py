@@ -174,6 +174,36 @@ SIGNATURES = {
     "plamo_cuda_batch_close": (None, [P]),
 }
 
+class Mapping(ctypes.Structure):
+    """struct plamo_mapping (reference runtime/model.h:65-68)."""
+    _fields_ = [("base", c_void_p), ("bytes", c_uint64)]
+
+
+class WeightSpec(ctypes.Structure):
+    """struct plamo_weight_spec (reference runtime/model.h:69-74)."""
+    _fields_ = [("name", c_char_p), ("rank", c_uint64), ("shape", POINTER(c_uint64)),
+                ("slot", POINTER(c_void_p))]
+
+
+class Tensor(ctypes.Structure):
+    """struct plamo_tensor (reference tests/find.c:4-7)."""
+    _fields_ = [("data", c_void_p), ("bytes", c_uint64), ("rank", c_uint64), ("dims", c_uint64 * 4),
+                ("reserved", c_uint64)]
+
+
+assert ctypes.sizeof(Mapping) == 16 and ctypes.sizeof(WeightSpec) == 32 and ctypes.sizeof(Tensor) == 64
+
+# name -> (restype, argtypes); exactly the entry points of include/plamo_safetensors.h.
+LOADER_SIGNATURES = {
+    "plamo_safetensors_view": (c_int, [P, c_uint64, P]),
+    "plamo_parse_u64": (c_int, [P, P, P]),
+    "plamo_find_tensor": (c_int, [P, c_uint64, c_char_p, POINTER(Tensor)]),
+    "plamo_resolve_weight": (c_void_p, [POINTER(Mapping), c_uint64, c_char_p, c_uint64, POINTER(c_uint64)]),
+    "plamo_bind_weights": (c_int, [POINTER(Mapping), c_uint64, POINTER(WeightSpec)]),
+    "plamo_map_file": (c_int, [c_char_p, POINTER(Mapping)]),
+    "plamo_unmap_file": (None, [POINTER(Mapping)]),
+}
+
 _lib = None
 
 
@@ -186,7 +216,7 @@ def load(path=LIB_PATH):
         raise OSError(f"{path} is missing: run `make -C plamo-3-translate.c_b200` (or "
                       "__graft_entry__.build()); there is no non-CUDA implementation")
     lib = ctypes.CDLL(path)
-    for name, (restype, argtypes) in SIGNATURES.items():
+    for name, (restype, argtypes) in list(SIGNATURES.items()) + list(LOADER_SIGNATURES.items()):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes

@@ -12,6 +12,7 @@ a host blob (uploaded by plamo_cuda_preload) or generated directly in HBM
 """
 import ctypes
 import math
+import os
 from dataclasses import dataclass, field, replace
 
 import numpy as np
@@ -226,8 +227,9 @@ class HostModel:
     """The descriptor tree of one model plus the host buffers it points to.
 
     weights: "synthetic" (generated in HBM by `Backend.preload_synthetic`),
-    a numpy uint16 blob laid out by `self.offsets`, or None to allocate a zero
-    blob the caller fills. weights_of: another HostModel of the same profile
+    a numpy uint16 blob laid out by `self.offsets`, a dict {tensor name: host
+    address} (a mapped checkpoint, see open_checkpoint), or None to allocate a
+    zero blob the caller fills. weights_of: another HostModel of the same profile
     whose weights this one shares (same host keys, so the same device copies):
     a second request with its own descriptors and KV cache.
     """
@@ -244,7 +246,13 @@ class HostModel:
         self.blob_bytes = total
         self._keep = []
         self.synthetic = isinstance(weights, str) and weights == "synthetic"
-        if weights_of is not None:
+        self.addresses = weights if isinstance(weights, dict) else None
+        if self.addresses is not None:
+            missing = [name for name, _ in self.schema if name not in self.addresses]
+            assert not missing, missing
+            self.blob = None
+            base = 0
+        elif weights_of is not None:
             assert weights_of.blob_bytes == total and weights_of.profile == p
             self.synthetic = weights_of.synthetic
             self.reservation = getattr(weights_of, "reservation", None)
@@ -264,6 +272,8 @@ class HostModel:
         self.base = base
 
         def w(name):
+            if self.addresses is not None:
+                return self.addresses[name]
             return base + self.offsets[name]
 
         h, qw, aw, kvw = p.hidden, p.qkv_rows, p.attention_width, p.kh * p.dim
@@ -368,8 +378,68 @@ class HostModel:
 
     def tensor_ranges(self):
         """(address, element count, name) of every weight tensor."""
+        if self.addresses is not None:
+            return [(self.addresses[name], int(np.prod(shape)), name) for name, shape in self.schema]
         return [(self.base + self.offsets[name], int(np.prod(shape)), name)
                 for name, shape in self.schema]
+
+
+class Checkpoint:
+    """Mapped BF16 safetensors shards bound to a profile's weight schema
+    (reference src/model_open.s: map every shard, bind every schema entry with
+    its exact shape, all or nothing). `model` is the descriptor tree over the
+    mapped bytes; Backend.preload_model uploads them."""
+
+    def __init__(self, paths, profile, layer_specs=None, full_capacity=None):
+        lib = _abi.load()
+        self.maps = (_abi.Mapping * len(paths))()
+        self.count = 0
+        for i, path in enumerate(paths):
+            if not lib.plamo_map_file(os.fsencode(path), ctypes.byref(self.maps[i])):
+                self.close()
+                raise OSError(f"cannot map {path}")
+            self.count = i + 1
+        sch = schema(profile)
+        self._shapes = [(ctypes.c_uint64 * len(shape))(*shape) for _, shape in sch]
+        self._names = [name.encode() for name, _ in sch]
+        self._slots = (ctypes.c_void_p * len(sch))()
+        specs = (_abi.WeightSpec * (len(sch) + 1))()
+        for i, (name, shape) in enumerate(sch):
+            specs[i] = _abi.WeightSpec(self._names[i], len(shape), self._shapes[i],
+                                       ctypes.cast(ctypes.byref(self._slots, i * ctypes.sizeof(ctypes.c_void_p)),
+                                                   ctypes.POINTER(ctypes.c_void_p)))
+        if not lib.plamo_bind_weights(self.maps, self.count, specs):
+            self.close()
+            raise ValueError("checkpoint does not match the profile's weight schema (names, BF16, shapes)")
+        addresses = {name: self._slots[i] for i, (name, _) in enumerate(sch)}
+        self.model = HostModel(profile, layer_specs, weights=addresses, full_capacity=full_capacity)
+
+    def close(self):
+        lib = _abi.load()
+        for i in range(self.count):
+            lib.plamo_unmap_file(ctypes.byref(self.maps[i]))
+        self.count = 0
+
+
+def write_safetensors(path, tensors, metadata=None):
+    """Write {name: uint16 array (BF16 bits)} as one safetensors file (test and
+    tooling helper; the loader itself is C)."""
+    import json
+    header, offset, blobs = {}, 0, []
+    if metadata:
+        header["__metadata__"] = metadata
+    for name, arr in tensors.items():
+        arr = np.ascontiguousarray(arr, dtype=np.uint16)
+        header[name] = {"dtype": "BF16", "shape": list(arr.shape), "data_offsets": [offset, offset + arr.nbytes]}
+        offset += arr.nbytes
+        blobs.append(arr)
+    text = json.dumps(header, separators=(",", ":")).encode()
+    text += b" " * ((8 - len(text) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(len(text).to_bytes(8, "little"))
+        f.write(text)
+        for arr in blobs:
+            f.write(arr.tobytes())
 
 
 def synthetic_parameters(name, std=0.02):
@@ -455,7 +525,11 @@ class Backend:
     def release(self, hm):
         """Drop the device copies of `hm` (its host memory may be reused)."""
         self.lib.plamo_cuda_release_model(self.ctx, hm.ptr)
-        self.lib.plamo_cuda_release_weights(self.ctx, hm.base, hm.blob_bytes)
+        if hm.addresses is not None:
+            for addr, count, _ in hm.tensor_ranges():
+                self.lib.plamo_cuda_release_weights(self.ctx, addr, 2 * count)
+        else:
+            self.lib.plamo_cuda_release_weights(self.ctx, hm.base, hm.blob_bytes)
 
     def prepare(self, hm):
         if self.lib.plamo_cuda_prepare_model(self.ctx, hm.ptr) != 1:

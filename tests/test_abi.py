@@ -29,11 +29,24 @@ def test_library_exports_every_declared_symbol():
     assert sorted(pkg._abi.SIGNATURES) == names
 
 
+def test_library_exports_the_checkpoint_loader():
+    pkg = load_package()
+    pkg.load()
+    text = open(os.path.join(ROOT, "include", "plamo_safetensors.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = sorted(set(re.findall(r"\b(plamo_\w+)\s*\(", text)))
+    assert sorted(pkg._abi.LOADER_SIGNATURES) == names
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(plamo_\w+)", out))
+    assert not [n for n in names if n not in exported]
+
+
 def test_record_layouts_match_reference_abi():
     pkg = load_package()
     a = pkg._abi
     sizes = {a.Qkv: 72, a.Cache: 48, a.Rotation: 72, a.Gqa: 72, a.Mixer: 56, a.Mlp: 80,
-             a.Layer: 64, a.Model: 88, a.Matmul: 64}
+             a.Layer: 64, a.Model: 88, a.Matmul: 64, a.Mapping: 16, a.WeightSpec: 32, a.Tensor: 64}
     for s, n in sizes.items():
         assert ctypes.sizeof(s) == n
     assert a.Layer.mixer.offset == 40

@@ -136,3 +136,54 @@ def test_tensor_parallel_matches_oracle(size):
         assert r["tokens"] == want_tokens, f"rank {rank}"
         assert r["spec"] == want_tokens, f"rank {rank} speculative"
         assert r["verify_batches"] > 0
+
+
+def _absent_peer(rank, size, port, out):
+    """Rank 1 prepares and connects, then never runs the step: rank 0's step
+    must fail within its bounded waits (about 2 s per wait, then the rest of
+    the operation skips its waits) and report the missing peer."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=size, timeout=datetime.timedelta(seconds=120))
+    b = None
+    try:
+        pkg = load_package()
+        full = profile(pkg)
+        shard = pkg.tp_shard_profile(full, size)
+        b = pkg.Backend(device=rank, max_context=1024, max_prefill=256)
+        hm = pkg.HostModel(shard, weights="synthetic")
+        b.preload_synthetic_tp(hm, full, rank, size, SEED)
+        b.tp_connect(hm, pkg.tp_all_gather_handles(b.tp_prepare(hm, rank, size)))
+        if rank == 0:
+            ids = np.arange(3, 23, dtype=np.uint32)
+            t0 = time.perf_counter()
+            rc = b.lib.plamo_cuda_prefill(b.ctx, hm.ptr, ids.ctypes.data, len(ids), None)
+            out[rank] = dict(rc=rc, seconds=time.perf_counter() - t0, note=b.info().note.decode(),
+                             errors=b.info().errors)
+        else:
+            out[rank] = dict(rc=None)
+    except Exception:
+        out[rank] = dict(error=traceback.format_exc())
+        time.sleep(5)
+    finally:
+        try:
+            dist.barrier()  # rank 1 stays mapped until rank 0's call has returned
+        finally:
+            if b is not None:
+                b.close()
+            dist.destroy_process_group()
+
+
+def test_missing_peer_fails_the_call_instead_of_hanging():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with mp.get_context("spawn").Manager() as manager:
+        out = manager.dict()
+        mp.spawn(_absent_peer, args=(2, _free_port(), out), nprocs=2, join=True)
+        res = [dict(out[r]) for r in range(2)]
+    for r in res:
+        assert "error" not in r, r.get("error")
+    r0 = res[0]
+    assert r0["rc"] == -1
+    assert "did not arrive" in r0["note"]
+    assert r0["seconds"] < 60
