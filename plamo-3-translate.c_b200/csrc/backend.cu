@@ -73,7 +73,8 @@ struct DLayer {
 
 // Tensor-parallel state of a shard (see tp.cuh). The exchange buffer has the
 // same layout on every rank:
-//   decode partials [2L][tp][H] f32, decode flags [2L][tp] u32 (point 2l after
+//   decode partials [2L][tp][H] {f32 value, u32 tag} pairs (tagged, no flags
+//   needed), decode flags [2L][tp] u32 (unused by the tagged points) (point 2l after
 //   o_proj of layer l, 2l+1 after its down_proj); prompt partials
 //   [2][tp][tmax*H] f32 (alternating points), prompt flags [2L][tp] u32;
 //   argmax slots [verify max][tp][4] u32.
@@ -681,14 +682,15 @@ TpPoint tp_point(DModel *m, bool prompt, uint64_t index) {
     const TpState &t = m->tp;
     TpPoint p{};
     p.tp = t.size;
+    p.ll = prompt ? 0 : 1;  // decode points: {value, tag} pairs (8 bytes per element)
     p.stride = prompt ? m->tmax * m->H : m->H;
     const uint64_t parts = prompt ? t.off_pparts + (index % 2) * t.size * p.stride * 4
-                                  : t.off_dparts + index * t.size * p.stride * 4;
+                                  : t.off_dparts + index * t.size * p.stride * 8;
     const uint64_t flags = (prompt ? t.off_pflags : t.off_dflags) + index * t.size * 4;
     p.parts = reinterpret_cast<const float *>(t.xbuf + parts);
     p.flags = reinterpret_cast<const uint32_t *>(t.xbuf + flags);
     for (uint32_t r = 0; r < t.size; ++r) {
-        p.peer_parts[r] = reinterpret_cast<float *>(t.peer[r] + parts) + t.rank * p.stride;
+        p.peer_parts[r] = reinterpret_cast<float *>(t.peer[r] + parts + t.rank * p.stride * (p.ll ? 8 : 4));
         p.peer_flags[r] = reinterpret_cast<uint32_t *>(t.peer[r] + flags) + t.rank;
     }
     p.ticket = t.tickets + (prompt ? 2 * m->L : 0) + index;
@@ -1443,7 +1445,7 @@ int plamo_cuda_tp_prepare(struct plamo_cuda *c, struct model *model, unsigned ra
     auto align = [](uint64_t x) { return (x + 255) & ~uint64_t{255}; };
     uint64_t off = 0;
     t.off_dparts = off;
-    off = align(off + 2 * m->L * size * m->H * 4);
+    off = align(off + 2 * m->L * size * m->H * 8);
     t.off_dflags = off;
     off = align(off + 2 * m->L * size * 4);
     t.off_pparts = off;

@@ -130,7 +130,8 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
         float4 st[kPV], br[kPV];
         uint2 w1[kPV];
         const bool reduce = PRO == PRO_RESID_NORM && p.tp_role == 1;
-        if (reduce) {
+        const uint32_t tag = reduce && p.tp.ll ? *p.tp.epoch + 1 : 0;
+        if (reduce && !p.tp.ll) {
             if (threadIdx.x == 0) tp_wait_flags(p.tp);
             __syncthreads();
         }
@@ -140,7 +141,8 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
             if (i < n4) {
                 st[k] = ld4(p.state_in + 4 * i);
                 if (PRO == PRO_RESID_NORM) {
-                    br[k] = reduce ? tp_sum4(p.tp, 4 * i) : ld4(p.branch + 4 * i);
+                    br[k] = !reduce ? ld4(p.branch + 4 * i)
+                            : p.tp.ll ? tp_ll_sum4(p.tp, 4 * i, tag) : tp_sum4(p.tp, 4 * i);
                     w1[k] = *reinterpret_cast<const uint2 *>(p.norm1 + 4 * i);
                 }
             }
@@ -187,18 +189,19 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
         for (uint64_t i = threadIdx.x; i < n; i += nt) xs[i] = p.state_in[i];
     } else {  // PRO_RESID_NORM, any length: state + rmsnorm(branch, norm1, off1)
         const bool reduce = p.tp_role == 1;
-        if (reduce) {
+        const uint32_t tag = reduce && p.tp.ll ? *p.tp.epoch + 1 : 0;
+        if (reduce && !p.tp.ll) {
             if (threadIdx.x == 0) tp_wait_flags(p.tp);
             __syncthreads();
         }
         float s = 0.0f;
         for (uint64_t i = threadIdx.x; i < n; i += nt) {
-            const float b = reduce ? tp_sum1(p.tp, i) : p.branch[i];
+            const float b = !reduce ? p.branch[i] : p.tp.ll ? tp_ll_sum1(p.tp, i, tag) : tp_sum1(p.tp, i);
             s += b * b;
         }
         const float inv = rms_inverse(block_sum(s, red), n);
         for (uint64_t i = threadIdx.x; i < n; i += nt) {
-            const float b = reduce ? tp_sum1(p.tp, i) : p.branch[i];
+            const float b = !reduce ? p.branch[i] : p.tp.ll ? tp_ll_sum1(p.tp, i, tag) : tp_sum1(p.tp, i);
             xs[i] = __fadd_rn(p.state_in[i], rms_apply(b, inv, p.norm1[i], p.off1));
         }
     }
@@ -237,6 +240,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
     float bv = -__int_as_float(0x7f800000);
     uint32_t bi = 0xffffffffu;
     bool saw_nan = false;
+    const uint32_t ll_tag = EPI == EPI_STORE && p.tp_role == 2 && p.tp.ll ? *p.tp.epoch + 1 : 0;
     for (uint64_t u = threadIdx.x; u < u1 - u0; u += blockDim.x) {
         float t0 = 0.0f, t1 = 0.0f;
         for (uint64_t s = 0; s < slots; ++s) {
@@ -247,7 +251,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
         if (EPI == EPI_SWIGLU) {
             p.y[unit] = swiglu(t0, t1);
         } else if (EPI == EPI_STORE && p.tp_role == 2) {
-            if (!tp_failed(p.tp.error))
+            if (tp_failed(p.tp.error)) continue;
+            if (p.tp.ll) tp_ll_store(p.tp, unit, t0, ll_tag);
+            else
                 for (uint32_t r = 0; r < p.tp.tp; ++r) p.tp.peer_parts[r][unit] = t0;
         } else {
             p.y[unit] = t0;
@@ -260,7 +266,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
             }
         }
     }
-    if (EPI == EPI_STORE && p.tp_role == 2) tp_signal(p.tp);
+    if (EPI == EPI_STORE && p.tp_role == 2 && !p.tp.ll) tp_signal(p.tp);
     if (EPI == EPI_ARGMAX) {
         if (threadIdx.x == 0) any_nan = 0;
         __syncthreads();

@@ -13,6 +13,12 @@
 // every rank's flag of the current epoch and sums the partials in rank order,
 // so every rank computes the same bits.
 //
+// Decode points use a low-latency form instead of flags: every partial value
+// travels with its epoch tag as one 8-byte store {value, epoch + 1}, which
+// reaches the peer as a unit, so the consumer polls the values themselves and
+// proceeds the moment the last one lands - no fence, ticket or flag round
+// trip on the producer side (the protocol NCCL calls LL).
+//
 // Epochs: a device counter, advanced once at the end of every tensor-parallel
 // operation (decode step, prompt, verification) on every rank; a flag holds
 // epoch + 1 of the operation that raised it, so buffers and flags are reused
@@ -30,7 +36,8 @@ constexpr int kTpMax = 8;
 
 struct TpPoint {
     uint32_t tp;                    // ranks; 0 = not tensor-parallel
-    uint64_t stride;                // floats between source slots of `parts`
+    uint32_t ll;                    // 1: parts hold {value, tag} pairs, no flags
+    uint64_t stride;                // elements between source slots of `parts`
     const float *parts;             // local [tp][stride] partials, slot r from rank r
     const uint32_t *flags;          // local [tp] flag raised by each source rank
     float *peer_parts[kTpMax];      // slot `rank` of every rank's parts
@@ -87,6 +94,73 @@ __device__ __forceinline__ void tp_signal(const TpPoint &t) {
         __threadfence_system();
         st_relaxed_sys(t.peer_flags[threadIdx.x], *t.epoch + 1);
     }
+}
+
+__device__ __forceinline__ uint4 ld_volatile4(const void *p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 ld_volatile2(const void *p) {
+    uint2 v;
+    asm volatile("ld.volatile.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_volatile2(void *p, uint32_t a, uint32_t b) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+
+// Low-latency point: this rank's value of element `unit` to every rank.
+__device__ __forceinline__ void tp_ll_store(const TpPoint &t, uint64_t unit, float v, uint32_t tag) {
+    for (uint32_t r = 0; r < t.tp; ++r)
+        st_volatile2(reinterpret_cast<uint2 *>(t.peer_parts[r]) + unit, __float_as_uint(v), tag);
+}
+
+// Wait (bounded) until `ok(...)` holds for the polled words; false on timeout
+// or an earlier failure of this operation.
+template <typename Load, typename Ready>
+__device__ __forceinline__ bool tp_ll_poll(const TpPoint &t, Load load, Ready ready, uint64_t &start) {
+    for (;;) {
+        load();
+        if (ready()) return true;
+        if (tp_failed(t.error)) return false;
+        if (!start) start = global_ns();
+        else if (global_ns() - start > 2000000000ull) {
+            if (t.error) atomicExch(t.error, 4u);
+            return false;
+        }
+    }
+}
+
+// Rank-ordered sum of elements i..i+3 of every slot of a low-latency point.
+__device__ __forceinline__ float4 tp_ll_sum4(const TpPoint &t, uint64_t i, uint32_t tag) {
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    uint64_t start = 0;
+    for (uint32_t r = 0; r < t.tp; ++r) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint2 *>(t.parts) + r * t.stride + i);
+        uint4 a, b;
+        tp_ll_poll(
+            t, [&] { a = ld_volatile4(src), b = ld_volatile4(src + 1); },
+            [&] { return a.y == tag && a.w == tag && b.y == tag && b.w == tag; }, start);
+        const float4 v = make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(b.x),
+                                     __uint_as_float(b.z));
+        s = r ? make_float4(__fadd_rn(s.x, v.x), __fadd_rn(s.y, v.y), __fadd_rn(s.z, v.z), __fadd_rn(s.w, v.w)) : v;
+    }
+    return s;
+}
+__device__ __forceinline__ float tp_ll_sum1(const TpPoint &t, uint64_t i, uint32_t tag) {
+    float s = 0.0f;
+    uint64_t start = 0;
+    for (uint32_t r = 0; r < t.tp; ++r) {
+        const uint2 *src = reinterpret_cast<const uint2 *>(t.parts) + r * t.stride + i;
+        uint2 a;
+        tp_ll_poll(t, [&] { a = ld_volatile2(src); }, [&] { return a.y == tag; }, start);
+        s = r ? __fadd_rn(s, __uint_as_float(a.x)) : __uint_as_float(a.x);
+    }
+    return s;
 }
 
 // Rank-ordered sum of the 4 floats at `i` of every source slot (L2 loads:
