@@ -122,6 +122,11 @@ int plamo_cuda_invalidate(struct plamo_cuda *, struct model *);
    *next = UINT32_MAX when a logit is NaN. */
 int plamo_cuda_forward_greedy(struct plamo_cuda *, struct model *, uint64_t token,
                               uint32_t *next);
+/* forward_greedy that also returns the top-2 logit margin of the step (best
+   minus the largest value at any other index): the draft proposer's
+   confidence (reference runtime/worker.c:268-286). */
+int plamo_cuda_forward_greedy_margin(struct plamo_cuda *, struct model *, uint64_t token, uint32_t *next,
+                                     float *margin);
 /* Prefill and select the first generated token on the device. */
 int plamo_cuda_prefill_greedy(struct plamo_cuda *, struct model *, const uint32_t *ids,
                               uint64_t tokens, uint32_t *next);

@@ -132,6 +132,7 @@ SIGNATURES = {
     "plamo_cuda_release_model": (c_int, [P, M]),
     "plamo_cuda_release_weights": (c_int, [P, P, c_uint64]),
     "plamo_cuda_forward_greedy": (c_int, [P, M, c_uint64, POINTER(c_uint32)]),
+    "plamo_cuda_forward_greedy_margin": (c_int, [P, M, c_uint64, POINTER(c_uint32), POINTER(ctypes.c_float)]),
     "plamo_cuda_prefill_greedy": (c_int, [P, M, P, c_uint64, POINTER(c_uint32)]),
     "plamo_cuda_generate": (c_int64, [P, M, P, c_uint64, c_uint64, P, TOKEN_CALLBACK, P,
                                       POINTER(CudaTiming)]),

@@ -103,8 +103,9 @@ struct DModel {
     float *state[2], *final_state, *normalized, *logits;
     float *qkv, *q, *attn, *branch, *mid, *part;
     uint32_t *tickets, *arg_idx, *arg_nan, *d_token, *d_next, *d_error;
-    float *arg_val;
+    float *arg_val, *arg_val2;
     uint32_t splits, gemv_grid;
+    float last_margin = 0.0f;  // top-2 logit margin of the last greedy decode step
     // prompt / verification
     uint64_t tmax;
     float *p_states, *p_norm, *p_qkv, *p_q, *p_attn, *p_branch, *p_gu, *p_logits, *p_part;
@@ -146,6 +147,8 @@ struct plamo_cuda {
     bool bulk_gemv;
     int gemv_ring_kb;
     int tc_stages;  // tcgen05 projection ring depth (0: as many as shared memory holds)
+    float draft_margin;         // PLAMO_DRAFT_MIN_MARGIN, or -1: the reference's default rule
+    unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
     bool tc_gemm;
     bool prompt_attn;  // blocked prompt attention (PLAMO_CUDA_PROMPT_ATTN=0 disables)
     int gemv_ctas;
@@ -730,7 +733,9 @@ bool greedy_choice(plamo_cuda *c, DModel *m, uint32_t grid) {
     const bool tp = m->tp.active;
     if (!launch(c, argmax_merge_kernel, dim3(1), dim3(256), 0, static_cast<const float *>(m->arg_val),
                 static_cast<const uint32_t *>(m->arg_idx), static_cast<const uint32_t *>(m->arg_nan), grid,
-                tp ? m->tp.lidx : m->d_next, tp ? nullptr : m->d_token, tp ? m->tp.lval : nullptr))
+                tp ? m->tp.lidx : m->d_next, tp ? nullptr : m->d_token, tp ? m->tp.lval : nullptr,
+                static_cast<const float *>(tp ? nullptr : m->arg_val2),
+                tp ? nullptr : reinterpret_cast<float *>(m->d_next + 2)))
         return false;
     if (!tp) return true;
     return launch(c, tp_argmax_kernel, dim3(1), dim3(128), 0, static_cast<const float *>(m->tp.lval),
@@ -836,6 +841,7 @@ bool record_decode(plamo_cuda *c, DModel *m) {
     h.norm_out = m->normalized;
     h.y = m->logits;
     h.arg_val = m->arg_val;
+    h.arg_val2 = m->arg_val2;
     h.arg_idx = m->arg_idx;
     h.arg_nan = m->arg_nan;
     if (m->tp.active) {
@@ -1054,6 +1060,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
     h.norm_out = m->normalized;
     h.y = m->logits;
     h.arg_val = m->arg_val;
+    h.arg_val2 = m->arg_val2;
     h.arg_idx = m->arg_idx;
     h.arg_nan = m->arg_nan;
     uint32_t grid = 0;
@@ -1124,6 +1131,20 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_gemm = !tc || strcmp(tc, "0");
     const char *pa = getenv("PLAMO_CUDA_PROMPT_ATTN");
     c->prompt_attn = !pa || strcmp(pa, "0");
+    // Draft confidence settings, parsed as reference runtime/worker.c:199-208
+    // (invalid values fall back to the default rule).
+    c->draft_margin = -1.0f;
+    c->draft_min_tokens = 0;
+    if (const char *dm = getenv("PLAMO_DRAFT_MIN_MARGIN")) {
+        char *end = nullptr;
+        const float v = strtof(dm, &end);
+        if (*dm && end && !*end && std::isfinite(v) && v >= 0.0f) c->draft_margin = v;
+    }
+    if (const char *dt = getenv("PLAMO_DRAFT_MIN_TOKENS")) {
+        char *end = nullptr;
+        const unsigned long v = strtoul(dt, &end, 10);
+        if (*dt && end && !*end && v >= 1 && v <= kVerifyMax) c->draft_min_tokens = static_cast<unsigned>(v);
+    }
     const char *tc_st = getenv("PLAMO_CUDA_TC_STAGES");
     c->tc_stages = tc_st ? std::max(2, std::min(atoi(tc_st), kTcMaxStages)) : 0;
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
@@ -1379,10 +1400,11 @@ static int prepare_impl(struct plamo_cuda *c, struct model *model, uint64_t head
     m->tickets = static_cast<uint32_t *>(dalloc(c, m.get(), m->KH * 4));
     const uint64_t grid_max = static_cast<uint64_t>(c->sm_count) * 64;
     m->arg_val = static_cast<float *>(dalloc(c, m.get(), grid_max * 4));
+    m->arg_val2 = static_cast<float *>(dalloc(c, m.get(), grid_max * 4));
     m->arg_idx = static_cast<uint32_t *>(dalloc(c, m.get(), grid_max * 4));
     m->arg_nan = static_cast<uint32_t *>(dalloc(c, m.get(), grid_max * 4));
     m->d_token = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
-    // [next token, error flag]: one 8-byte read returns both.
+    // [next token, error flag, top-2 margin bits]: one read returns all.
     m->d_next = static_cast<uint32_t *>(dalloc(c, m.get(), 16));
     m->d_error = m->d_next + 1;
     // Prompt buffers.
@@ -1512,7 +1534,15 @@ int plamo_cuda_forward(struct plamo_cuda *c, struct model *model, uint64_t token
     return 1;
 }
 
+int plamo_cuda_forward_greedy_margin(struct plamo_cuda *c, struct model *model, uint64_t token, uint32_t *next,
+                                     float *margin);
+
 int plamo_cuda_forward_greedy(struct plamo_cuda *c, struct model *model, uint64_t token, uint32_t *next) {
+    return plamo_cuda_forward_greedy_margin(c, model, token, next, nullptr);
+}
+
+int plamo_cuda_forward_greedy_margin(struct plamo_cuda *c, struct model *model, uint64_t token, uint32_t *next,
+                                     float *margin) {
     if (!c) return 0;
     cudaSetDevice(c->device);
     DModel *m = find_model(c, model);
@@ -1533,7 +1563,7 @@ int plamo_cuda_forward_greedy(struct plamo_cuda *c, struct model *model, uint64_
     cudaEventRecord(c->ev0, c->stream);
     if (!launch_decode(c, m)) return -1;
     cudaEventRecord(c->ev1, c->stream);
-    if (!note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 1, m->d_next, 8, cudaMemcpyDeviceToHost, c->stream)) ||
+    if (!note(c, "next", cudaMemcpyAsync(c->pinned_u32 + 1, m->d_next, 12, cudaMemcpyDeviceToHost, c->stream)) ||
         !note(c, "forward", cudaStreamSynchronize(c->stream)))
         return -1;
     if (c->pinned_u32[2] && !check_device_error(c, m)) return -1;
@@ -1541,6 +1571,8 @@ int plamo_cuda_forward_greedy(struct plamo_cuda *c, struct model *model, uint64_
     c->info.forwards++;
     publish_counts(m, 1);
     if (next) *next = c->pinned_u32[1];
+    memcpy(&m->last_margin, c->pinned_u32 + 3, 4);
+    if (margin) *margin = m->last_margin;
     return 1;
 }
 
@@ -2368,13 +2400,25 @@ int64_t plamo_cuda_generate_speculative(struct plamo_cuda *c, struct model *targ
             proposed[0] = id;
             unsigned n = 1, processed = 0;
             bool failed = false;
+            // Confidence rule of reference runtime/worker.c:243-286: blocks of
+            // more than 8 stop once 8 are proposed and the smallest top-2
+            // logit margin so far is below 1 (PLAMO_DRAFT_MIN_MARGIN /
+            // PLAMO_DRAFT_MIN_TOKENS override, as there).
+            const float need = c->draft_margin >= 0.0f ? c->draft_margin : (limit > 8 ? 1.0f : 0.0f);
+            const unsigned minimum = c->draft_min_tokens ? c->draft_min_tokens : (limit > 8 ? 8u : 2u);
+            float confidence = INFINITY;
             while (n < limit && proposed[n - 1] != 1 && proposed[n - 1] != 16) {
+                if (need > 0.0f && n >= minimum && confidence < need) break;
                 uint32_t t = 0;
-                if (plamo_cuda_forward_greedy(c, draft, proposed[n - 1], &t) != 1 || t >= draft->vocab) {
+                float margin = 0.0f;
+                if (plamo_cuda_forward_greedy_margin(c, draft, proposed[n - 1], &t, &margin) != 1 ||
+                    t >= draft->vocab) {
                     failed = true;
                     break;
                 }
                 ++processed;
+                if (margin < confidence) confidence = margin;
+                if (need > 0.0f && n >= minimum && confidence < need) break;
                 proposed[n++] = t;
             }
             if (failed || plamo_cuda_verify(c, target, proposed, n, next) != 1) {

@@ -45,6 +45,7 @@ struct GemvParams {
     float *norm_out;              // block 0 writes the normalised input here
     float *y;                     // STORE/ARGMAX: [rows]; SWIGLU: [rows/2]
     float *arg_val;               // ARGMAX: per-block best value
+    float *arg_val2;              // ARGMAX: per-block runner-up value (any other index)
     uint32_t *arg_idx;            // ARGMAX: per-block best index
     uint32_t *arg_nan;            // ARGMAX: per-block NaN flag
     uint32_t *error;              // set to nonzero on an invalid token
@@ -226,6 +227,18 @@ __device__ __forceinline__ bool arg_better(float v, uint32_t i, float bv, uint32
     return v > bv || (v == bv && i < bi);
 }
 
+// Fold candidate (v, i, v2: its own runner-up) into (bv, bi, sv): the best of
+// the two stays best; the runner-up is the largest value of any other index.
+__device__ __forceinline__ void top2_merge(float v, uint32_t i, float v2, float &bv, uint32_t &bi, float &sv) {
+    if (arg_better(v, i, bv, bi)) {
+        sv = fmaxf(fmaxf(sv, v2), bv);
+        bv = v;
+        bi = i;
+    } else {
+        sv = fmaxf(sv, fmaxf(v, v2));
+    }
+}
+
 // Fixed-order reduction of per-slot partials ([unit][slot][pair]), then the
 // epilogue: store, SwiGLU of gate/up pairs, or per-block argmax candidates.
 template <int EPI>
@@ -237,7 +250,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
     constexpr int kPair = EPI == EPI_SWIGLU ? 2 : 1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int warps = (blockDim.x + 31) >> 5;
-    float bv = -__int_as_float(0x7f800000);
+    float bv = -__int_as_float(0x7f800000), sv = bv;
     uint32_t bi = 0xffffffffu;
     bool saw_nan = false;
     const uint32_t ll_tag = EPI == EPI_STORE && p.tp_role == 2 && p.tp.ll ? *p.tp.epoch + 1 : 0;
@@ -259,15 +272,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
             p.y[unit] = t0;
             if (EPI == EPI_ARGMAX) {
                 if (t0 != t0) saw_nan = true;
-                else if (arg_better(t0, static_cast<uint32_t>(unit), bv, bi)) {
-                    bv = t0;
-                    bi = static_cast<uint32_t>(unit);
-                }
+                else top2_merge(t0, static_cast<uint32_t>(unit), -__int_as_float(0x7f800000), bv, bi, sv);
             }
         }
     }
     if (EPI == EPI_STORE && p.tp_role == 2 && !p.tp.ll) tp_signal(p.tp);
     if (EPI == EPI_ARGMAX) {
+        __shared__ float second_val[32];
         if (threadIdx.x == 0) any_nan = 0;
         __syncthreads();
         if (saw_nan) any_nan = 1;
@@ -275,25 +286,21 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const float *
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (arg_better(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
-            }
+            const float os = __shfl_xor_sync(0xffffffffu, sv, o);
+            top2_merge(ov, oi, os, bv, bi, sv);
         }
         if (lane == 0) {
             best_val[warp] = bv;
             best_idx[warp] = bi;
+            second_val[warp] = sv;
         }
         __syncthreads();
         if (threadIdx.x == 0) {
-            for (int w = 1; w < warps; ++w)
-                if (arg_better(best_val[w], best_idx[w], bv, bi)) {
-                    bv = best_val[w];
-                    bi = best_idx[w];
-                }
+            for (int w = 1; w < warps; ++w) top2_merge(best_val[w], best_idx[w], second_val[w], bv, bi, sv);
             p.arg_val[blockIdx.x] = bv;
             p.arg_idx[blockIdx.x] = bi;
             p.arg_nan[blockIdx.x] = any_nan;
+            if (p.arg_val2) p.arg_val2[blockIdx.x] = sv;
         }
     }
 }
@@ -633,50 +640,48 @@ inline size_t gemv_bulk_smem(uint64_t cols, uint64_t rows_per_block, int pair, i
 // Merge per-block argmax candidates: first maximal index, NaN -> UINT32_MAX
 // (reference src/token.s:35-63). Writes the winner to *out and, when given,
 // to the next decode step's token slot.
+// With val2 (the blocks' runner-up values), margin receives best minus the
+// largest value at any other index (the draft proposer's confidence).
 __global__ void argmax_merge_kernel(const float *val, const uint32_t *idx, const uint32_t *nan_flag,
-                                    uint32_t blocks, uint32_t *out, uint32_t *next_token, float *out_val) {
-    __shared__ float sv[32];
-    __shared__ uint32_t si[32];
-    __shared__ uint32_t sn[32];
+                                    uint32_t blocks, uint32_t *out, uint32_t *next_token, float *out_val,
+                                    const float *val2, float *margin) {
+    __shared__ float wv[32], ws[32];
+    __shared__ uint32_t wi[32];
+    __shared__ uint32_t wn[32];
     pdl_wait();
-    float bv = -__int_as_float(0x7f800000);
+    const float ninf = -__int_as_float(0x7f800000);
+    float bv = ninf, sv = ninf;
     uint32_t bi = 0xffffffffu, nan_seen = 0;
     for (uint32_t b = threadIdx.x; b < blocks; b += blockDim.x) {
         nan_seen |= nan_flag[b];
-        if (arg_better(val[b], idx[b], bv, bi)) {
-            bv = val[b];
-            bi = idx[b];
-        }
+        top2_merge(val[b], idx[b], val2 ? val2[b] : ninf, bv, bi, sv);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
         const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const float os = __shfl_xor_sync(0xffffffffu, sv, o);
         nan_seen |= __shfl_xor_sync(0xffffffffu, nan_seen, o);
-        if (arg_better(ov, oi, bv, bi)) {
-            bv = ov;
-            bi = oi;
-        }
+        top2_merge(ov, oi, os, bv, bi, sv);
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (lane == 0) {
-        sv[warp] = bv;
-        si[warp] = bi;
-        sn[warp] = nan_seen;
+        wv[warp] = bv;
+        wi[warp] = bi;
+        ws[warp] = sv;
+        wn[warp] = nan_seen;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
-            nan_seen |= sn[w];
-            if (arg_better(sv[w], si[w], bv, bi)) {
-                bv = sv[w];
-                bi = si[w];
-            }
+            nan_seen |= wn[w];
+            top2_merge(wv[w], wi[w], ws[w], bv, bi, sv);
         }
         const uint32_t result = nan_seen ? 0xffffffffu : bi;
         *out = result;
         if (next_token) *next_token = result;
         if (out_val) *out_val = bv;
+        if (margin) *margin = __fsub_rn(bv, sv);
     }
 }
 

@@ -75,3 +75,34 @@ def test_unrelated_draft_rolls_back_and_matches_greedy(backend, block):
     got, st = speculative(backend, target, draft, ids, 50, block)
     assert got == want
     assert st.verify_batches > 0
+
+
+def test_greedy_margin_is_the_top2_logit_gap(backend):
+    """The draft's confidence (reference runtime/worker.c:268-286): best logit
+    minus the largest logit at any other index, for the step just decoded."""
+    pkg = load_package()
+    prof = small_profile(pkg)
+    a = pkg.HostModel(prof, weights="synthetic")
+    backend.preload_synthetic(a, seed=33)
+    b = pkg.HostModel(prof, weights_of=a)
+    backend.prepare(a)
+    backend.prepare(b)
+    lib = backend.lib
+    ids = np.random.default_rng(4).integers(3, prof.vocab, size=9).astype(np.uint32)
+    nxt = ctypes.c_uint32()
+    for hm in (a, b):
+        assert lib.plamo_cuda_prefill_greedy(backend.ctx, hm.ptr, ids.ctypes.data, len(ids), ctypes.byref(nxt)) == 1
+    token = nxt.value
+    for _ in range(5):
+        assert lib.plamo_cuda_forward(backend.ctx, a.ptr, token) == 1
+        margin = ctypes.c_float()
+        assert lib.plamo_cuda_forward_greedy_margin(backend.ctx, b.ptr, token, ctypes.byref(nxt),
+                                                    ctypes.byref(margin)) == 1
+        logits = a.logits_array()
+        best = int(np.argmax(logits))
+        assert nxt.value == best
+        rest = np.delete(logits, best)
+        assert margin.value == np.float32(logits[best] - rest.max())
+        token = nxt.value
+    lib.plamo_cuda_release_model(backend.ctx, b.ptr)
+    lib.plamo_cuda_release_model(backend.ctx, a.ptr)
