@@ -461,17 +461,33 @@ bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, cons
 // FP32 CUDA-core kernel otherwise. split: BF16 scratch of 3*T*K elements
 // (the hi, mid and lo terms).
 // part/part_floats: scratch for split-K partial tiles (nullptr: no split K).
+// presplit: `split` already holds the BF16 terms of X (written by the kernel
+// that produced X), so no split pass runs. defer: when the projection splits
+// K, leave the partial planes for the consumer to sum (RowFuse.bparts) and
+// describe them here instead of summing into Y; defer->splits = 1 otherwise.
+struct Deferred {
+    uint32_t splits = 1;
+    const float *part = nullptr;
+    uint64_t plane = 0;
+};
+
+// Whether projection_with takes the tensor-core path for this weight.
+bool tc_projection(plamo_cuda *c, const uint16_t *W, uint64_t T, uint64_t R, uint64_t K) {
+    return c->tc_gemm && K % 8 == 0 && K >= kTcK && reinterpret_cast<uintptr_t>(W) % 16 == 0 && T < (1ull << 31) &&
+           R < (1ull << 31) && tensor_maps_available();
+}
+
 bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys, uint64_t T,
                      uint64_t R, uint64_t K, uint16_t *split, uint32_t *error, float *part = nullptr,
-                     uint64_t part_floats = 0) {
+                     uint64_t part_floats = 0, bool presplit = false, Deferred *defer = nullptr) {
+    if (defer) *defer = Deferred{};
     if (!T || !R) return true;
-    const bool tc = c->tc_gemm && split && K % 8 == 0 && K >= kTcK && reinterpret_cast<uintptr_t>(W) % 16 == 0 &&
-                    T < (1ull << 31) && R < (1ull << 31) && tensor_maps_available();
+    const bool tc = split && tc_projection(c, W, T, R, K);
     if (!tc) return gemm(c, X, xs, W, Y, ys, T, R, K);
     uint16_t *hi = split, *mid = split + T * K, *lo = split + 2 * T * K;
     const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((T * K + 255) / 256, 8192));
-    if (!launch(c, split_hilo_kernel, dim3(blocks), dim3(256), 0, X, xs, static_cast<uint32_t>(T),
-                static_cast<uint32_t>(K), hi, mid, lo))
+    if (!presplit && !launch(c, split_hilo_kernel, dim3(blocks), dim3(256), 0, X, xs, static_cast<uint32_t>(T),
+                             static_cast<uint32_t>(K), hi, mid, lo))
         return false;
     const uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
     CUtensorMap mw, mh, mm, ml;
@@ -502,15 +518,34 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
     default: ok = launch_tc<128>(c, mw, mh, mm, ml, p, r32, t32, splits); break;
     }
     if (!ok || splits == 1) return ok;
+    if (defer) {
+        *defer = Deferred{splits, part, T * R};
+        return true;
+    }
     const uint32_t sum_blocks = static_cast<uint32_t>(std::min<uint64_t>((T * R + 255) / 256, 4096));
     return launch(c, splitk_sum_kernel, dim3(sum_blocks), dim3(256), 0, static_cast<const float *>(part), splits, t32,
                   r32, Y, ys);
 }
 
 bool projection(plamo_cuda *c, DModel *m, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys,
-                uint64_t T, uint64_t R, uint64_t K) {
+                uint64_t T, uint64_t R, uint64_t K, bool presplit = false, Deferred *defer = nullptr) {
     return projection_with(c, X, xs, W, Y, ys, T, R, K, T <= m->tmax ? m->p_split : nullptr, m->d_error,
-                           m->p_splitk, kSplitkFloats);
+                           m->p_splitk, kSplitkFloats, presplit, defer);
+}
+
+// The RowFuse of a row kernel whose output feeds projection W next (split
+// terms when that projection runs on the tensor cores) and whose branch input
+// may be the deferred partials of the previous projection.
+RowFuse row_fuse(plamo_cuda *c, DModel *m, const uint16_t *next_w, uint64_t T, uint64_t R, uint64_t K,
+                 const Deferred &in) {
+    RowFuse f{};
+    if (next_w && T <= m->tmax && tc_projection(c, next_w, T, R, K)) f.split = m->p_split;
+    if (in.splits > 1) {
+        f.bparts = in.part;
+        f.bsplits = in.splits;
+        f.bplane = in.plane;
+    }
+    return f;
 }
 
 AttnLayer attn_layer(const DModel *m, uint64_t l) {
@@ -871,39 +906,51 @@ bool record_batch(plamo_cuda *c, plamo_cuda_batch *b, DModel *m) {
     if (!launch(c, embed_rows_kernel, dim3(T), dim3(256), 0, m->emb, static_cast<const uint32_t *>(b->d_tokens), m->V,
                 H, m->p_states, m->d_error))
         return false;
+    // As record_prompt: row kernels write the next projection's BF16 terms and
+    // sum the previous projection's split-K partials.
+    Deferred down_parts;
     for (uint64_t l = 0; l < m->L; ++l) {
         const DLayer &L = m->layers[l];
         bool ok;
+        RowFuse f = row_fuse(c, m, L.qkv_w, T, m->QW, H, down_parts);
         if (l == 0)
             ok = launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
                         static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, L.pre,
-                        1.0f, m->p_norm, H);
+                        1.0f, m->p_norm, H, f);
         else
             ok = launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
                         static_cast<const float *>(m->p_branch), m->layers[l - 1].mpost, kPostMlpOffset, L.pre,
-                        1.0f, m->p_norm, H);
-        if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H)) return false;
+                        1.0f, m->p_norm, H, f);
+        if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H, f.split != nullptr))
+            return false;
         if (!launch(c, decode_attention128_batch_kernel, dim3(static_cast<uint32_t>(m->KH), kDecSplits, b->B),
                     dim3(kDecThreads), decode_attention128_smem(G),
                     static_cast<const DecodeAttnParams *>(b->d_attn + l * b->B)))
             return false;
-        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
+        Deferred o_parts;
+        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW, false, &o_parts)) return false;
+        f = row_fuse(c, m, L.gu, T, 2 * m->I, H, o_parts);
         if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
-                    static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H))
+                    static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H, f))
             return false;
-        if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H)) return false;
+        if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H, f.split != nullptr)) return false;
+        f = row_fuse(c, m, L.down, T, H, m->I, Deferred{});
         if (!launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((m->I * T + 255) / 256, 4096)), dim3(256), 0,
-                    m->p_gu, m->I, T))
+                    m->p_gu, m->I, T, f))
             return false;
-        if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
+        if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I, f.split != nullptr,
+                        &down_parts))
+            return false;
     }
+    const RowFuse fh = row_fuse(c, m, m->head, T, m->V, H, Deferred{});
     if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(512), 0, m->p_states,
                 static_cast<const float *>(m->p_branch), m->layers[m->L - 1].mpost, kPostMlpOffset,
-                static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H) ||
+                static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H,
+                row_fuse(c, m, nullptr, T, 0, 0, down_parts)) ||
         !launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
                 static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, m->norm, 1.0f,
-                m->p_norm, H) ||
-        !projection(c, m, m->p_norm, H, m->head, m->p_logits, m->V, T, m->V, H) ||
+                m->p_norm, H, fh) ||
+        !projection(c, m, m->p_norm, H, m->head, m->p_logits, m->V, T, m->V, H, fh.split != nullptr) ||
         !rows_argmax(c, m, m->p_logits, m->V, static_cast<uint32_t>(T), b->d_tokens, nullptr))
         return false;
     return launch(c, batch_advance_kernel, dim3(1), dim3(256), 0, static_cast<uint64_t *const *>(b->d_counters), m->L,
@@ -995,18 +1042,26 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
     if (!launch(c, embed_rows_kernel, dim3(T), dim3(256), 0, m->emb, static_cast<const uint32_t *>(m->p_ids),
                 m->V, H, m->p_states, m->d_error))
         return false;
+    // The row kernels write the BF16 terms of the next projection's input and
+    // take the previous projection's split-K partials directly (RowFuse);
+    // tensor-parallel branches are all-reduced in place, so nothing is
+    // deferred across an exchange.
+    const bool tp = m->tp.active;
+    Deferred down_parts;
     for (uint64_t l = 0; l < m->L; ++l) {
         const DLayer &L = m->layers[l];
         bool ok;
+        RowFuse f = row_fuse(c, m, L.qkv_w, T, m->QW, H, down_parts);
         if (l == 0)
             ok = launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
                         static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, L.pre,
-                        1.0f, m->p_norm, H);
+                        1.0f, m->p_norm, H, f);
         else
             ok = launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
                         static_cast<const float *>(m->p_branch), m->layers[l - 1].mpost, kPostMlpOffset, L.pre,
-                        1.0f, m->p_norm, H);
-        if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H)) return false;
+                        1.0f, m->p_norm, H, f);
+        if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H, f.split != nullptr))
+            return false;
         AttnLayer al = attn_layer(m, l);
         if (!launch(c, qk_prep_kernel, dim3(m->QH + m->KH, T), dim3(128), 0, m->p_qkv, m->p_q, al, shape))
             return false;
@@ -1024,28 +1079,36 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
                                                         c->stream)))
                 return false;
         }
-        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW)) return false;
-        if (m->tp.active && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l)) return false;
+        Deferred o_parts;
+        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW, false, tp ? nullptr : &o_parts))
+            return false;
+        if (tp && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l)) return false;
+        f = row_fuse(c, m, L.gu, T, 2 * m->I, H, o_parts);
         if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
-                    static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H))
+                    static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H, f))
             return false;
-        if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H)) return false;
+        if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H, f.split != nullptr)) return false;
+        f = row_fuse(c, m, L.down, T, H, m->I, Deferred{});
         if (!launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((m->I * T + 255) / 256, 4096)), dim3(256), 0,
-                    m->p_gu, m->I, T))
+                    m->p_gu, m->I, T, f))
             return false;
-        if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I)) return false;
-        if (m->tp.active && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l + 1)) return false;
+        if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I, f.split != nullptr,
+                        tp ? nullptr : &down_parts))
+            return false;
+        if (tp && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l + 1)) return false;
     }
     if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(512), 0, m->p_states,
                 static_cast<const float *>(m->p_branch), m->layers[m->L - 1].mpost, kPostMlpOffset,
-                static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H))
+                static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H,
+                row_fuse(c, m, nullptr, T, 0, 0, down_parts)))
         return false;
     if (need_all_logits) {
+        const RowFuse f = row_fuse(c, m, m->head, T, m->Vh, H, Deferred{});
         if (!launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, m->p_states,
                     static_cast<const float *>(nullptr), static_cast<const uint16_t *>(nullptr), 0.0f, m->norm,
-                    1.0f, m->p_norm, H))
+                    1.0f, m->p_norm, H, f))
             return false;
-        return projection(c, m, m->p_norm, H, m->head, m->p_logits, m->Vh, T, m->Vh, H);
+        return projection(c, m, m->p_norm, H, m->head, m->p_logits, m->Vh, T, m->Vh, H, f.split != nullptr);
     }
     // Final norm and head for the last prompt token only (reference
     // src/prefill.s:136-158), with the greedy choice on the device.
@@ -1788,7 +1851,7 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
     ok = ok && gemv<PRO_X, EPI_STORE>(c, d);
     ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(1), dim3(512), 0, m->state[1],
                       static_cast<const float *>(m->branch), L.mpost, kPostMlpOffset,
-                      static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), m->H);
+                      static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), m->H, RowFuse{});
     ok = ok && launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended + index, uint64_t{1}, uint64_t{1});
     cudaEventRecord(c->ev1, c->stream);
     ok = ok && note(c, "layer out", cudaMemcpyAsync(state, m->state[1], m->H * 4, cudaMemcpyDeviceToHost,
@@ -1942,14 +2005,14 @@ int plamo_cuda_mlp(struct plamo_cuda *c, const struct mlp *p, float *states, uin
               note(c, "mlp alloc", cudaMalloc(&b, tokens * H * 4));
     ok = ok && note(c, "mlp in", cudaMemcpyAsync(s, states, tokens * H * 4, cudaMemcpyHostToDevice, c->stream));
     ok = ok && launch(c, norm_rows_kernel<ROW_NORM>, dim3(tokens), dim3(512), 0, s, static_cast<const float *>(nullptr),
-                      static_cast<const uint16_t *>(nullptr), 0.0f, pre, 1.0f, n, H);
+                      static_cast<const uint16_t *>(nullptr), 0.0f, pre, 1.0f, n, H, RowFuse{});
     ok = ok && gemm(c, n, H, gu, g, 2 * I, tokens, 2 * I, H);
     ok = ok && launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((I * tokens + 255) / 256, 4096)), dim3(256), 0,
-                      g, I, tokens);
+                      g, I, tokens, RowFuse{});
     ok = ok && gemm(c, g, 2 * I, down, b, H, tokens, H, I);
     ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(tokens), dim3(512), 0, s, static_cast<const float *>(b),
                       post, kPostMlpOffset, static_cast<const uint16_t *>(nullptr), 0.0f,
-                      static_cast<float *>(nullptr), H);
+                      static_cast<float *>(nullptr), H, RowFuse{});
     ok = ok && note(c, "mlp out", cudaMemcpyAsync(states, s, tokens * H * 4, cudaMemcpyDeviceToHost, c->stream)) &&
          note(c, "mlp", cudaStreamSynchronize(c->stream));
     cudaFree(s);

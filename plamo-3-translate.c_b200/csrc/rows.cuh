@@ -23,6 +23,66 @@ __global__ void embed_rows_kernel(const uint16_t *table, const uint32_t *ids, ui
 
 enum RowMode { ROW_NORM = 0, ROW_RESID = 1, ROW_RESID_NORM = 2 };
 
+// FP32 -> BF16 terms hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid)
+// (round to nearest even): the tcgen05 projections' view of an activation.
+__device__ __forceinline__ void split3(float v, uint16_t *h, uint16_t *m, uint16_t *l) {
+    const uint16_t a = plamo_bf16_round(v);
+    const float r1 = __fsub_rn(v, __uint_as_float(static_cast<uint32_t>(a) << 16));
+    const uint16_t b = plamo_bf16_round(r1);
+    const float r2 = __fsub_rn(r1, __uint_as_float(static_cast<uint32_t>(b) << 16));
+    *h = a;
+    *m = b;
+    *l = plamo_bf16_round(r2);
+}
+
+// Work the row kernels take over from their neighbours in the prompt and
+// batch paths (zero-initialised: none):
+//   split  - also write the BF16 terms of the kernel's output for the next
+//            tcgen05 projection ([3][rows][width] planes), so no separate
+//            split pass is needed;
+//   bparts - the branch input arrives as `bsplits` split-K partial planes of
+//            the previous projection ([bsplits][rows][width], plane bplane),
+//            summed here in plane order instead of by a separate pass.
+struct RowFuse {
+    uint16_t *split;
+    const float *bparts;
+    uint32_t bsplits;
+    uint64_t bplane;
+};
+
+__device__ __forceinline__ float4 fuse_branch4(const RowFuse &f, const float *b, uint64_t off) {
+    if (f.bsplits <= 1) return ld4(b + off);
+    float4 s = ld4(f.bparts + off);
+    for (uint32_t z = 1; z < f.bsplits; ++z) {
+        const float4 v = ld4(f.bparts + z * f.bplane + off);
+        s = make_float4(__fadd_rn(s.x, v.x), __fadd_rn(s.y, v.y), __fadd_rn(s.z, v.z), __fadd_rn(s.w, v.w));
+    }
+    return s;
+}
+__device__ __forceinline__ float fuse_branch1(const RowFuse &f, const float *b, uint64_t off) {
+    if (f.bsplits <= 1) return b[off];
+    float s = f.bparts[off];
+    for (uint32_t z = 1; z < f.bsplits; ++z) s = __fadd_rn(s, f.bparts[z * f.bplane + off]);
+    return s;
+}
+__device__ __forceinline__ void fuse_split4(const RowFuse &f, uint64_t plane, uint64_t off, float4 v) {
+    if (!f.split) return;
+    uint16_t h[4], m[4], l[4];
+    split3(v.x, &h[0], &m[0], &l[0]);
+    split3(v.y, &h[1], &m[1], &l[1]);
+    split3(v.z, &h[2], &m[2], &l[2]);
+    split3(v.w, &h[3], &m[3], &l[3]);
+    *reinterpret_cast<uint2 *>(f.split + off) = make_uint2(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16));
+    *reinterpret_cast<uint2 *>(f.split + plane + off) =
+        make_uint2(m[0] | (uint32_t(m[1]) << 16), m[2] | (uint32_t(m[3]) << 16));
+    *reinterpret_cast<uint2 *>(f.split + 2 * plane + off) =
+        make_uint2(l[0] | (uint32_t(l[1]) << 16), l[2] | (uint32_t(l[3]) << 16));
+}
+__device__ __forceinline__ void fuse_split1(const RowFuse &f, uint64_t plane, uint64_t off, float v) {
+    if (!f.split) return;
+    split3(v, f.split + off, f.split + plane + off, f.split + 2 * plane + off);
+}
+
 // One CTA per token row:
 //   ROW_NORM:       out = rmsnorm(states, w2, off2)
 //   ROW_RESID:      states += rmsnorm(branch, w1, off1)
@@ -31,10 +91,12 @@ enum RowMode { ROW_NORM = 0, ROW_RESID = 1, ROW_RESID_NORM = 2 };
 // float4s in registers between the two norms (up to 4 per thread).
 template <int MODE>
 __global__ void norm_rows_kernel(float *states, const float *branch, const uint16_t *w1, float off1,
-                                 const uint16_t *w2, float off2, float *out, uint64_t hidden) {
+                                 const uint16_t *w2, float off2, float *out, uint64_t hidden, RowFuse fuse) {
     __shared__ float red[32];
     pdl_wait();
     float *x = states + static_cast<uint64_t>(blockIdx.x) * hidden;
+    const uint64_t row0 = static_cast<uint64_t>(blockIdx.x) * hidden;
+    const uint64_t plane = static_cast<uint64_t>(gridDim.x) * hidden;
     const uint32_t nt = blockDim.x;
     if (hidden % 4 == 0 && hidden <= 16ull * nt) {
         const uint32_t n4 = static_cast<uint32_t>(hidden / 4);
@@ -45,7 +107,6 @@ __global__ void norm_rows_kernel(float *states, const float *branch, const uint1
             if (i < n4) st[k] = ld4(x + 4 * i);
         }
         if (MODE != ROW_NORM) {
-            const float *b = branch + static_cast<uint64_t>(blockIdx.x) * hidden;
             float4 br[4];
             uint2 wv[4];
             float s = 0.0f;
@@ -53,7 +114,7 @@ __global__ void norm_rows_kernel(float *states, const float *branch, const uint1
             for (int k = 0; k < 4; ++k) {
                 const uint32_t i = threadIdx.x + k * nt;
                 if (i < n4) {
-                    br[k] = ld4(b + 4 * i);
+                    br[k] = fuse_branch4(fuse, branch, row0 + 4 * i);
                     wv[k] = *reinterpret_cast<const uint2 *>(w1 + 4 * i);
                     s += sq4(br[k]);
                 }
@@ -86,19 +147,25 @@ __global__ void norm_rows_kernel(float *states, const float *branch, const uint1
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const uint32_t i = threadIdx.x + k * nt;
-                if (i < n4) *reinterpret_cast<float4 *>(o + 4 * i) = apply4(st[k], inv, norm4(wv[k], off2));
+                if (i < n4) {
+                    const float4 v = apply4(st[k], inv, norm4(wv[k], off2));
+                    *reinterpret_cast<float4 *>(o + 4 * i) = v;
+                    fuse_split4(fuse, plane, row0 + 4 * i, v);
+                }
             }
         }
         pdl_launch_dependents();
         return;
     }
     if (MODE != ROW_NORM) {
-        const float *b = branch + static_cast<uint64_t>(blockIdx.x) * hidden;
         float s = 0.0f;
-        for (uint64_t i = threadIdx.x; i < hidden; i += blockDim.x) s += b[i] * b[i];
+        for (uint64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
+            const float b = fuse_branch1(fuse, branch, row0 + i);
+            s += b * b;
+        }
         const float inv = rms_inverse(block_sum(s, red), hidden);
         for (uint64_t i = threadIdx.x; i < hidden; i += blockDim.x)
-            x[i] = __fadd_rn(x[i], rms_apply(b[i], inv, w1[i], off1));
+            x[i] = __fadd_rn(x[i], rms_apply(fuse_branch1(fuse, branch, row0 + i), inv, w1[i], off1));
         __syncthreads();
     }
     if (MODE != ROW_RESID) {
@@ -106,20 +173,26 @@ __global__ void norm_rows_kernel(float *states, const float *branch, const uint1
         for (uint64_t i = threadIdx.x; i < hidden; i += blockDim.x) s += x[i] * x[i];
         const float inv = rms_inverse(block_sum(s, red), hidden);
         float *o = out + static_cast<uint64_t>(blockIdx.x) * hidden;
-        for (uint64_t i = threadIdx.x; i < hidden; i += blockDim.x) o[i] = rms_apply(x[i], inv, w2[i], off2);
+        for (uint64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
+            o[i] = rms_apply(x[i], inv, w2[i], off2);
+            fuse_split1(fuse, plane, row0 + i, o[i]);
+        }
     }
     pdl_launch_dependents();
 }
 
 // In place: gu[t][i] = swiglu(gu[t][i], gu[t][I + i]) (reference src/batch.s:22-45).
-__global__ void swiglu_rows_kernel(float *gu, uint64_t inter, uint64_t tokens) {
+// fuse.split: also the BF16 terms of the result, [3][tokens][inter].
+__global__ void swiglu_rows_kernel(float *gu, uint64_t inter, uint64_t tokens, RowFuse fuse) {
     pdl_wait();
     const uint64_t total = inter * tokens;
     for (uint64_t k = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; k < total;
          k += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const uint64_t t = k / inter, i = k % inter;
         float *row = gu + t * 2 * inter;
-        row[i] = swiglu(row[i], row[inter + i]);
+        const float v = swiglu(row[i], row[inter + i]);
+        row[i] = v;
+        fuse_split1(fuse, total, k, v);
     }
     pdl_launch_dependents();
 }
