@@ -561,6 +561,9 @@ def run_profile(args):
         ms = timed(1)
     else:
         profile = pkg.PROFILES[args.model]
+        if args.layers:
+            from dataclasses import replace
+            profile = replace(profile, name=f"{profile.name}-{args.layers}layers", layers=args.layers)
         hm = pkg.HostModel(profile, weights="synthetic", full_capacity=8208)
         be.preload_synthetic(hm, seed=4)
         reqs = [hm] + [pkg.HostModel(profile, weights_of=hm, full_capacity=8208)
@@ -604,6 +607,7 @@ def main():
                     help="run one small fixed workload for an ncu capture instead of the benchmark")
     ap.add_argument("--model", default="8b", help="profile of --profile step/batch")
     ap.add_argument("--requests", type=int, default=8, help="requests of --profile batch")
+    ap.add_argument("--layers", type=int, default=0, help="--profile step/batch: keep only this many layers")
     ap.add_argument("--shape", default="", help="rows,cols (gemv) or tokens,rows,cols (gemm)")
     args = ap.parse_args()
     if args.profile:

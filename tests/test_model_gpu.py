@@ -113,3 +113,41 @@ def test_8b_prefix_greedy_tokens_and_logits(backend):
     want, margins = oracle_generate(b, ids, 6)
     got = gpu_generate(backend, a, ids, 6)
     assert got == want, f"margins {margins}"
+
+
+def test_08b_draft_profile_greedy_tokens_match_oracle(backend):
+    """The 0.8B draft profile of config 5 (16 query heads over one KV head, so
+    every grouped-query path runs with G = 16): 30-id prompt, 32 greedy tokens
+    identical to the oracle's."""
+    pkg = load_package()
+    load_oracle().oracle_set_threads(os.cpu_count() or 1)
+    a, b = synthetic_pair(backend, pkg.PROFILES["0.8b"], seed=6, full_capacity=8208)
+    ids = np.random.default_rng(2).integers(3, 100000, size=30).astype(np.uint32)
+    want, margins = oracle_generate(b, ids, 32)
+    got = gpu_generate(backend, a, ids, 32)
+    assert got == want, f"margins {margins}"
+
+
+def test_31b_shaped_layers_match_oracle(backend):
+    """Layers of the 31B profile's exact shape (hidden 5120: rows end inside a
+    chunk of 3 rows of ten 512-column slots; 64 query and 8 KV heads; the
+    tied head) - two of them, one sliding and one full - against the oracle:
+    prefill logits under the whole-model rule, then 6 greedy tokens."""
+    from dataclasses import replace
+    pkg = load_package()
+    load_oracle().oracle_set_threads(os.cpu_count() or 1)
+    prof = replace(pkg.PROFILES["31b"], name="31b-2layers", layers=2, pattern=2)
+    a, b = synthetic_pair(backend, prof, seed=8, full_capacity=1024)
+    ids = np.random.default_rng(1).integers(3, 100000, size=20).astype(np.uint32)
+    assert backend.lib.plamo_cuda_prefill(backend.ctx, a.ptr, ids.ctypes.data, len(ids), 0) == 1
+    ok, _ = oracle_prefill(b, ids)
+    assert ok == 1
+    for name, x, y in (("logits", a.logits_array(), b.logits_array()),
+                       ("state", a.state_array(), b.state_array())):
+        assert np.all(np.isfinite(x)) and np.all(np.isfinite(y)), name
+        assert rel_l2(x, y) <= 1e-4, f"31b-shaped prefill {name}: {rel_l2(x, y):.3g}"
+    a.reset()
+    b.reset()
+    want, margins = oracle_generate(b, ids, 6)
+    got = gpu_generate(backend, a, ids, 6)
+    assert got == want, f"margins {margins}"
