@@ -136,14 +136,15 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
             if (threadIdx.x == 0) tp_wait_flags(p.tp);
             __syncthreads();
         }
+        if (PRO == PRO_RESID_NORM && reduce && p.tp.ll) tp_ll_sum_groups<kPV>(p.tp, threadIdx.x, nt, n4, tag, br);
 #pragma unroll
         for (int k = 0; k < kPV; ++k) {
             const uint32_t i = threadIdx.x + k * nt;
             if (i < n4) {
                 st[k] = ld4(p.state_in + 4 * i);
                 if (PRO == PRO_RESID_NORM) {
-                    br[k] = !reduce ? ld4(p.branch + 4 * i)
-                            : p.tp.ll ? tp_ll_sum4(p.tp, 4 * i, tag) : tp_sum4(p.tp, 4 * i);
+                    if (!reduce) br[k] = ld4(p.branch + 4 * i);
+                    else if (!p.tp.ll) br[k] = tp_sum4(p.tp, 4 * i);
                     w1[k] = *reinterpret_cast<const uint2 *>(p.norm1 + 4 * i);
                 }
             }

@@ -135,22 +135,53 @@ __device__ __forceinline__ bool tp_ll_poll(const TpPoint &t, Load load, Ready re
     }
 }
 
-// Rank-ordered sum of elements i..i+3 of every slot of a low-latency point.
-__device__ __forceinline__ float4 tp_ll_sum4(const TpPoint &t, uint64_t i, uint32_t tag) {
-    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+// Rank-ordered sums of KP groups of 4 elements (group k at element
+// 4 * (i0 + k * step), present when below n4) of a low-latency point: the
+// loads of all groups of one rank are in flight together, so a rank costs
+// one round trip once its values have landed (not one per group).
+template <int KP>
+__device__ __forceinline__ void tp_ll_sum_groups(const TpPoint &t, uint32_t i0, uint32_t step, uint32_t n4,
+                                                 uint32_t tag, float4 (&out)[KP]) {
     uint64_t start = 0;
     for (uint32_t r = 0; r < t.tp; ++r) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint2 *>(t.parts) + r * t.stride + i);
-        uint4 a, b;
-        tp_ll_poll(
-            t, [&] { a = ld_volatile4(src), b = ld_volatile4(src + 1); },
-            [&] { return a.y == tag && a.w == tag && b.y == tag && b.w == tag; }, start);
-        const float4 v = make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(b.x),
-                                     __uint_as_float(b.z));
-        s = r ? make_float4(__fadd_rn(s.x, v.x), __fadd_rn(s.y, v.y), __fadd_rn(s.z, v.z), __fadd_rn(s.w, v.w)) : v;
+        const uint2 *slot = reinterpret_cast<const uint2 *>(t.parts) + r * t.stride;
+        uint4 a[KP], b[KP];
+        uint32_t pending = 0;
+#pragma unroll
+        for (int k = 0; k < KP; ++k)
+            if (i0 + k * step < n4) pending |= 1u << k;
+        const uint32_t present = pending;
+        while (pending) {
+#pragma unroll
+            for (int k = 0; k < KP; ++k)
+                if (pending >> k & 1u) {
+                    const uint4 *src = reinterpret_cast<const uint4 *>(slot + 4ull * (i0 + k * step));
+                    a[k] = ld_volatile4(src);
+                    b[k] = ld_volatile4(src + 1);
+                }
+#pragma unroll
+            for (int k = 0; k < KP; ++k)
+                if ((pending >> k & 1u) && a[k].y == tag && a[k].w == tag && b[k].y == tag && b[k].w == tag)
+                    pending &= ~(1u << k);
+            if (!pending || tp_failed(t.error)) break;
+            if (!start) start = global_ns();
+            else if (global_ns() - start > 2000000000ull) {
+                if (t.error) atomicExch(t.error, 4u);
+                break;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < KP; ++k)
+            if (present >> k & 1u) {
+                const float4 v = make_float4(__uint_as_float(a[k].x), __uint_as_float(a[k].z), __uint_as_float(b[k].x),
+                                             __uint_as_float(b[k].z));
+                out[k] = r ? make_float4(__fadd_rn(out[k].x, v.x), __fadd_rn(out[k].y, v.y), __fadd_rn(out[k].z, v.z),
+                                         __fadd_rn(out[k].w, v.w))
+                           : v;
+            }
     }
-    return s;
 }
+
 __device__ __forceinline__ float tp_ll_sum1(const TpPoint &t, uint64_t i, uint32_t tag) {
     float s = 0.0f;
     uint64_t start = 0;
