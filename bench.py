@@ -31,6 +31,7 @@ import json
 import os
 import subprocess
 import sys
+import threading
 import time
 
 import numpy as np
@@ -83,22 +84,38 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
+        self.first = threading.Event()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        # A short timed region must not end before the first sample: wait for it
+        # (bounded) so every measurement carries at least one clock reading.
+        self.first.wait(timeout=10)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
+            self.first.set()
+        self.first.set()
 
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.proc.wait()
+        self.reader.join(timeout=5)
+        out = "".join(self.lines)
         sms, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.splitlines():
