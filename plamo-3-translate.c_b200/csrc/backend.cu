@@ -371,6 +371,8 @@ int gemv_chunks(const void *w, uint64_t cols) {
 
 template <int PRO, int EPI>
 bool gemv(plamo_cuda *c, GemvParams p, uint32_t *grid_out = nullptr) {
+    if constexpr (PRO == PRO_RESID_NORM)
+        if (p.tp_role == 1) return gemv<PRO_RESID_NORM_TP, EPI>(c, p, grid_out);
     const int pair = EPI == EPI_SWIGLU ? 2 : 1;
     const uint64_t units = p.rows / pair;
     if (c->bulk_gemv && gemv_bulk_shape(p.cols) && reinterpret_cast<uintptr_t>(p.w) % 16 == 0 && units) {
@@ -1235,6 +1237,9 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     set_gemv_smem_limits<PRO_EMBED_NORM, EPI_STORE>(optin);
     set_gemv_smem_limits<PRO_RESID_NORM, EPI_SWIGLU>(optin);
     set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>(optin);
+    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_STORE>(optin);
+    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_SWIGLU>(optin);
+    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_ARGMAX>(optin);
     set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin);
     allow_smem(attention_kernel, optin);
     allow_smem(prompt_attention_kernel, optin);

@@ -25,7 +25,10 @@
 
 namespace plamo {
 
-enum GemvPrologue { PRO_X = 0, PRO_NORM = 1, PRO_RESID_NORM = 2, PRO_EMBED_NORM = 3 };
+// PRO_RESID_NORM_TP: PRO_RESID_NORM whose branch is the rank-ordered sum of a
+// tensor-parallel point's partials (a separate instantiation, so the
+// single-GPU kernels carry no exchange code).
+enum GemvPrologue { PRO_X = 0, PRO_NORM = 1, PRO_RESID_NORM = 2, PRO_EMBED_NORM = 3, PRO_RESID_NORM_TP = 4 };
 enum GemvEpilogue { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ARGMAX = 2 };
 
 struct GemvParams {
@@ -50,7 +53,7 @@ struct GemvParams {
     uint32_t *arg_nan;            // ARGMAX: per-block NaN flag
     uint32_t *error;              // set to nonzero on an invalid token
     // Tensor parallelism: role 1 = the prologue's branch is the rank-ordered
-    // sum of the point's partials (PRO_RESID_NORM); role 2 = the STORE
+    // sum of the point's partials (PRO_RESID_NORM_TP); role 2 = the STORE
     // epilogue pushes its rows into every rank's slot of the point.
     int tp_role;
     TpPoint tp;
@@ -98,6 +101,8 @@ constexpr int kPV = 4;
 
 template <int PRO>
 __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, float *red) {
+    constexpr bool kResid = PRO == PRO_RESID_NORM || PRO == PRO_RESID_NORM_TP;
+    constexpr bool reduce = PRO == PRO_RESID_NORM_TP;
     const uint64_t n = p.cols;
     const bool publish = blockIdx.x == 0;
     const uint32_t nt = blockDim.x;
@@ -130,26 +135,25 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
         const uint32_t n4 = static_cast<uint32_t>(n / 4);
         float4 st[kPV], br[kPV];
         uint2 w1[kPV];
-        const bool reduce = PRO == PRO_RESID_NORM && p.tp_role == 1;
         const uint32_t tag = reduce && p.tp.ll ? *p.tp.epoch + 1 : 0;
         if (reduce && !p.tp.ll) {
             if (threadIdx.x == 0) tp_wait_flags(p.tp);
             __syncthreads();
         }
-        if (PRO == PRO_RESID_NORM && reduce && p.tp.ll) tp_ll_sum_groups<kPV>(p.tp, threadIdx.x, nt, n4, tag, br);
+        if (reduce && p.tp.ll) tp_ll_sum_groups<kPV>(p.tp, threadIdx.x, nt, n4, tag, br);
 #pragma unroll
         for (int k = 0; k < kPV; ++k) {
             const uint32_t i = threadIdx.x + k * nt;
             if (i < n4) {
                 st[k] = ld4(p.state_in + 4 * i);
-                if (PRO == PRO_RESID_NORM) {
+                if (kResid) {
                     if (!reduce) br[k] = ld4(p.branch + 4 * i);
                     else if (!p.tp.ll) br[k] = tp_sum4(p.tp, 4 * i);
                     w1[k] = *reinterpret_cast<const uint2 *>(p.norm1 + 4 * i);
                 }
             }
         }
-        if (PRO == PRO_RESID_NORM) {
+        if (kResid) {
             float s = 0.0f;
 #pragma unroll
             for (int k = 0; k < kPV; ++k)
@@ -189,8 +193,7 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
         return true;
     } else if (PRO == PRO_NORM) {
         for (uint64_t i = threadIdx.x; i < n; i += nt) xs[i] = p.state_in[i];
-    } else {  // PRO_RESID_NORM, any length: state + rmsnorm(branch, norm1, off1)
-        const bool reduce = p.tp_role == 1;
+    } else {  // PRO_RESID_NORM(_TP), any length: state + rmsnorm(branch, norm1, off1)
         const uint32_t tag = reduce && p.tp.ll ? *p.tp.epoch + 1 : 0;
         if (reduce && !p.tp.ll) {
             if (threadIdx.x == 0) tp_wait_flags(p.tp);
