@@ -388,6 +388,13 @@ bool gemv(plamo_cuda *c, GemvParams p, uint32_t *grid_out = nullptr) {
             else if (grid < units) grid = std::min<uint64_t>(units, grid * 2);
             else return false;
         }
+        // The grid is one CTA per SM: two of its CTAs on one SM (possible for
+        // narrow rows and few registers) would give that SM a double share of
+        // the stream while another SM idles, so the request is more than half
+        // an SM's shared memory. A smaller kernel (decode attention) still fits
+        // beside it.
+        if (c->gemv_ctas == 1)
+            smem = std::max<size_t>(smem, static_cast<size_t>(c->smem_per_sm) / 2 - 1024 + 16);
         if (grid_out) *grid_out = static_cast<uint32_t>(grid);
         const dim3 g(static_cast<uint32_t>(grid)), b(kBulkThreads);
         if (p.cols % kSubElems) {
