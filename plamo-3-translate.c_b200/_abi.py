@@ -205,14 +205,14 @@ LOADER_SIGNATURES = {
     "plamo_unmap_file": (None, [POINTER(Mapping)]),
 }
 
-_lib = None
+_libs = {}
 
 
 def load(path=LIB_PATH):
     """Load the backend library and bind every entry point (raises if absent)."""
-    global _lib
-    if _lib is not None:
-        return _lib
+    path = os.path.abspath(path)
+    if path in _libs:
+        return _libs[path]
     if not os.path.exists(path):
         raise OSError(f"{path} is missing: run `make -C plamo-3-translate.c_b200` (or "
                       "__graft_entry__.build()); there is no non-CUDA implementation")
@@ -221,5 +221,5 @@ def load(path=LIB_PATH):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    _lib = lib
+    _libs[path] = lib
     return lib

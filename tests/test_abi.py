@@ -64,3 +64,11 @@ def test_open_reports_missing_device_without_gpu():
         lib.plamo_cuda_close(ctx)
         return
     assert err.value, "open must explain a failure"
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No CPU fallback: without the CUDA library the package refuses to load."""
+    import pytest
+    pkg = load_package()
+    with pytest.raises(OSError, match="no non-CUDA implementation"):
+        pkg._abi.load(str(tmp_path / "libplamo_cuda.so"))
