@@ -115,12 +115,17 @@ class ClockSampler:
             self.proc.kill()
             self.proc.wait()
         self.reader.join(timeout=5)
-        out = "".join(self.lines)
+        return self.summarise(self.lines, self.gpu)
+
+    @staticmethod
+    def summarise(lines, gpu):
+        """Median SM clock, max clock and the throttle reasons seen Active in
+        `nvidia-smi --format=csv,noheader,nounits` lines of FIELDS for one GPU."""
         sms, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.splitlines():
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != self.gpu:
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != gpu:
                 continue
             try:
                 sms.append(float(parts[1]))
