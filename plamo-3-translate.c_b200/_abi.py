@@ -15,6 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libplamo_cuda.so")
 LINEAR_STATIC_FLOATS = 4 << 20  # PLAMO_CUDA_LINEAR_STATIC_FLOATS
 PREFIX_LIMIT = 64  # PLAMO_CUDA_PREFIX_LIMIT
+VERIFY_MAX = 16  # PLAMO_CUDA_VERIFY_MAX
 
 
 class Qkv(ctypes.Structure):

@@ -72,3 +72,14 @@ def test_missing_library_fails_loudly(tmp_path):
     pkg = load_package()
     with pytest.raises(OSError, match="no non-CUDA implementation"):
         pkg._abi.load(str(tmp_path / "libplamo_cuda.so"))
+
+
+def test_python_constants_match_the_header():
+    """The ctypes layer's copies of the header's limits."""
+    text = open(os.path.join(ROOT, "include", "plamo_cuda.h")).read()
+    a = load_package()._abi
+    for name, value in (("PLAMO_CUDA_VERIFY_MAX", a.VERIFY_MAX), ("PLAMO_CUDA_PREFIX_LIMIT", a.PREFIX_LIMIT),
+                        ("PLAMO_CUDA_TP_MAX", a.TP_MAX)):
+        m = re.search(name + r"\s*=\s*(\d+)", text) or re.search(r"#define\s+" + name + r"\s+(\d+)", text)
+        assert m, name
+        assert int(m.group(1)) == value, name

@@ -157,3 +157,30 @@ def run_fixture(kv_backend, a, b, h, capacity):
     assert lib.plamo_cuda_forward(ctx, a.ptr, 2) == 0  # full global cache: declined
     assert a.caches[1].count == capacity
     assert kv_backend.info().graph_launches == launches
+
+
+def test_empty_and_oversized_requests_are_declined(kv_backend):
+    """An empty prompt is declined (reference src/prefill.s:9: count 0 returns 0), as are
+    verification blocks of 0 or more than PLAMO_CUDA_VERIFY_MAX rows and prompts longer
+    than the configured maximum: 0, with the model's state and caches unchanged."""
+    a, _ = decode_fixture_pair(128, 257, 128, 40)
+    try:
+        kv_backend.preload_model(a)
+        kv_backend.prepare(a)
+        lib, ctx = kv_backend.lib, kv_backend.ctx
+        ids = np.array([(j * 7 + 3) % 17 for j in range(4097)], dtype=np.uint32)
+        expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, 0, 0), 0)
+        assert [c.count for c in a.caches] == [0, 0]
+        expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, 3, 0), 1)
+        state, logits = a.state_array().copy(), a.logits_array().copy()
+        counts = [c.count for c in a.caches]
+        limit = load_package()._abi.VERIFY_MAX
+        nxt = np.zeros(limit + 1, dtype=np.uint32)
+        for n in (0, limit + 1):
+            expect(kv_backend, lib.plamo_cuda_verify(ctx, a.ptr, ids.ctypes.data, n, nxt.ctypes.data), 0)
+        expect(kv_backend, lib.plamo_cuda_prefill(ctx, a.ptr, ids.ctypes.data, 4097, 0), 0)
+        assert np.array_equal(a.state_array(), state)
+        assert np.array_equal(a.logits_array(), logits)
+        assert [c.count for c in a.caches] == counts
+    finally:
+        kv_backend.release(a)
