@@ -263,8 +263,10 @@ Rope *get_rope(plamo_cuda *c, const float *freq, uint64_t dim, float scale, uint
     std::vector<float> host(positions * dim);
     build_rope_rows(freq, dim, scale, 0, positions, host.data());
     if (!note(c, "rope alloc", cudaMalloc(&r->dev, host.size() * 4))) return nullptr;
-    if (!note(c, "rope copy", cudaMemcpy(r->dev, host.data(), host.size() * 4, cudaMemcpyHostToDevice)))
+    if (!note(c, "rope copy", cudaMemcpy(r->dev, host.data(), host.size() * 4, cudaMemcpyHostToDevice))) {
+        cudaFree(r->dev);
         return nullptr;
+    }
     c->info.allocated_bytes += host.size() * 4;
     c->ropes.push_back(std::move(r));
     return c->ropes.back().get();
@@ -1228,6 +1230,10 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
         (e = cudaMallocHost(&c->pinned_u32, 64 * 1024 * 4)) != cudaSuccess ||
         (e = cudaMalloc(&c->sink, 4)) != cudaSuccess) {
         if (error && cap) snprintf(error, cap, "cannot create CUDA stream: %s", cudaGetErrorString(e));
+        if (c->pinned_u32) cudaFreeHost(c->pinned_u32);
+        if (c->ev1) cudaEventDestroy(c->ev1);
+        if (c->ev0) cudaEventDestroy(c->ev0);
+        if (c->stream) cudaStreamDestroy(c->stream);
         delete c;
         return nullptr;
     }
