@@ -9,7 +9,7 @@ is missing, because there is no other implementation to fall back to.
 """
 import ctypes
 import os
-from ctypes import POINTER, c_char, c_char_p, c_double, c_int, c_int64, c_uint, c_uint32, c_uint64, c_void_p
+from ctypes import POINTER, c_char, c_char_p, c_double, c_size_t, c_int, c_int64, c_uint, c_uint32, c_uint64, c_void_p
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libplamo_cuda.so")
@@ -206,6 +206,27 @@ LOADER_SIGNATURES = {
     "plamo_unmap_file": (None, [POINTER(Mapping)]),
 }
 
+
+class ModelConfig(ctypes.Structure):
+    """struct plamo_model_config (include/plamo_layout.h)."""
+    _fields_ = [(n, c_uint64) for n in ("hidden", "layers", "query_heads", "kv_heads", "head_dim", "intermediate",
+                                         "vocab", "window", "pattern", "max_position", "tied")] + \
+               [(n, c_double) for n in ("local_theta", "global_theta", "yarn_factor", "yarn_original", "beta_fast",
+                                        "beta_slow")]
+
+
+# include/plamo_layout.h: run-time model descriptor builder
+LAYOUT_SIGNATURES = {
+    "plamo_model_config_profile": (c_int, [c_char_p, POINTER(ModelConfig)]),
+    "plamo_model_layout_create": (c_void_p, [POINTER(ModelConfig), c_uint64, c_char_p, c_size_t]),
+    "plamo_model_layout_schema": (POINTER(WeightSpec), [P]),
+    "plamo_model_layout_finish": (c_int, [P]),
+    "plamo_model_layout_model": (POINTER(Model), [P]),
+    "plamo_model_layout_buffer_bytes": (c_uint64, [P]),
+    "plamo_rope_frequencies": (None, [POINTER(ModelConfig), c_int, POINTER(ctypes.c_float)]),
+    "plamo_model_layout_destroy": (None, [P]),
+}
+
 _libs = {}
 
 
@@ -218,7 +239,8 @@ def load(path=LIB_PATH):
         raise OSError(f"{path} is missing: run `make -C plamo-3-translate.c_b200` (or "
                       "__graft_entry__.build()); there is no non-CUDA implementation")
     lib = ctypes.CDLL(path)
-    for name, (restype, argtypes) in list(SIGNATURES.items()) + list(LOADER_SIGNATURES.items()):
+    for name, (restype, argtypes) in (list(SIGNATURES.items()) + list(LOADER_SIGNATURES.items()) +
+                                      list(LAYOUT_SIGNATURES.items())):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes

@@ -83,3 +83,17 @@ def test_python_constants_match_the_header():
         m = re.search(name + r"\s*=\s*(\d+)", text) or re.search(r"#define\s+" + name + r"\s+(\d+)", text)
         assert m, name
         assert int(m.group(1)) == value, name
+
+
+def test_library_exports_the_model_layout_builder():
+    pkg = load_package()
+    pkg.load()
+    text = open(os.path.join(ROOT, "include", "plamo_layout.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = sorted(set(re.findall(r"\b(plamo_\w+)\s*\(", text)))
+    assert sorted(pkg._abi.LAYOUT_SIGNATURES) == names
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(plamo_\w+)", out))
+    assert not [n for n in names if n not in exported]
+    assert ctypes.sizeof(pkg._abi.ModelConfig) == 136
