@@ -179,3 +179,49 @@ def test_bound_checkpoint_drives_the_oracle_like_the_python_tree(tmp_path):
     finally:
         lay.close()
         lib.plamo_unmap_file(ctypes.byref(mapping))
+
+
+@pytest.mark.gpu
+def test_c_built_model_decodes_like_the_python_tree_on_the_gpu(tmp_path, backend):
+    """The CUDA backend takes a C-built descriptor tree bound to a mapped
+    checkpoint: the same greedy tokens as the Python tree over the same bytes."""
+    import synthetic
+    pkg = load_package()
+    lib = backend.lib
+    prof = pkg.Profile("lay-gpu", 256, 2, 4, 2, 64, 512, vocab=500, window=8, pattern=2, max_position=256)
+    cfg = pkg._abi.ModelConfig(hidden=256, layers=2, query_heads=4, kv_heads=2, head_dim=64, intermediate=512,
+                               vocab=500, window=8, pattern=2, max_position=256, tied=0, local_theta=10000.0,
+                               global_theta=1000000.0, yarn_factor=256.0, yarn_original=4096.0, beta_fast=32.0,
+                               beta_slow=1.0)
+    blob_model = pkg.HostModel(prof)
+    synthetic.fill_model(blob_model, 5)
+    path = tmp_path / "model.safetensors"
+    pkg.write_safetensors(path, {name: blob_model.tensor(name) for name, _ in pkg.schema(prof)})
+    mapping = pkg._abi.Mapping()
+    assert lib.plamo_map_file(str(path).encode(), ctypes.byref(mapping)) == 1
+    lay = Layout(cfg, 256)
+    ids = np.arange(3, 15, dtype=np.uint32)
+    outs = []
+    try:
+        assert lib.plamo_bind_weights(ctypes.byref(mapping), 1, lib.plamo_model_layout_schema(lay.handle)) == 1
+        assert lib.plamo_model_layout_finish(lay.handle) == 1
+        assert lib.plamo_cuda_preload(backend.ctx, mapping.base, mapping.bytes) == 1
+        c_ptr = ctypes.pointer(lay.model)
+        for ptr, release in ((c_ptr, lambda: lib.plamo_cuda_release_weights(backend.ctx, mapping.base,
+                                                                             mapping.bytes)),
+                             (blob_model.ptr, lambda: backend.release(blob_model))):
+            if ptr is blob_model.ptr:
+                backend.preload_model(blob_model)
+            assert lib.plamo_cuda_prepare_model(backend.ctx, ptr) == 1, backend.info().note
+            out = np.zeros(16, dtype=np.uint32)
+            timing = pkg._abi.CudaTiming()
+            n = lib.plamo_cuda_generate(backend.ctx, ptr, ids.ctypes.data, len(ids), 16, out.ctypes.data,
+                                        pkg._abi.TOKEN_CALLBACK(), None, ctypes.byref(timing))
+            assert n > 0, backend.info().note
+            outs.append(list(out[:n]))
+            lib.plamo_cuda_release_model(backend.ctx, ptr)
+            release()
+    finally:
+        lay.close()
+        lib.plamo_unmap_file(ctypes.byref(mapping))
+    assert outs[0] == outs[1]
