@@ -227,6 +227,19 @@ LAYOUT_SIGNATURES = {
     "plamo_model_layout_destroy": (None, [P]),
 }
 
+
+# include/plamo_tokenizer.h: the engine's tokenizer API (the assembly-level
+# pieces are exported too; the reference's own C tests bind those)
+TOKENIZER_SIGNATURES = {
+    "plamo_tokenizer_open": (c_void_p, [c_char_p, c_char_p, c_size_t]),
+    "plamo_tokenizer_close": (None, [P]),
+    "plamo_tokenizer_encode": (c_uint64, [P, c_char_p, c_uint, POINTER(POINTER(c_uint32)), c_char_p, c_size_t]),
+    "plamo_tokenizer_prefix": (c_uint64, [P, c_uint, POINTER(POINTER(c_uint32)), c_char_p, c_size_t]),
+    "plamo_tokenizer_decode": (c_uint64, [P, c_uint32, POINTER(ctypes.c_char_p)]),
+    "plamo_translation_prompt": (c_uint64, [c_char_p, c_char_p, c_char_p, c_char_p, c_uint64]),
+    "plamo_translation_prefix": (c_uint64, [c_char_p, c_char_p, c_uint64]),
+}
+
 _libs = {}
 
 
@@ -240,7 +253,7 @@ def load(path=LIB_PATH):
                       "__graft_entry__.build()); there is no non-CUDA implementation")
     lib = ctypes.CDLL(path)
     for name, (restype, argtypes) in (list(SIGNATURES.items()) + list(LOADER_SIGNATURES.items()) +
-                                      list(LAYOUT_SIGNATURES.items())):
+                                      list(LAYOUT_SIGNATURES.items()) + list(TOKENIZER_SIGNATURES.items())):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes

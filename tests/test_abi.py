@@ -97,3 +97,17 @@ def test_library_exports_the_model_layout_builder():
     exported = set(re.findall(r"\sT\s(plamo_\w+)", out))
     assert not [n for n in names if n not in exported]
     assert ctypes.sizeof(pkg._abi.ModelConfig) == 136
+
+
+def test_library_exports_the_tokenizer():
+    pkg = load_package()
+    pkg.load()
+    text = open(os.path.join(ROOT, "include", "plamo_tokenizer.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = sorted(set(re.findall(r"\b(plamo_\w+)\s*\(", text)))
+    assert len(names) == 23
+    assert set(pkg._abi.TOKENIZER_SIGNATURES) <= set(names)
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(plamo_\w+)", out))
+    assert not [n for n in names if n not in exported]
