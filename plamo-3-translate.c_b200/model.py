@@ -384,6 +384,62 @@ class HostModel:
                 for name, shape in self.schema]
 
 
+class Tokenizer:
+    """PLaMo-3 tokenizer over a tokenizer.jsonl vocabulary (include/plamo_tokenizer.h;
+    reference runtime/tokenizer.h): text -> ids, optionally wrapped in the
+    translation prompt (direction 1: English to Japanese, 2: Japanese to
+    English), and ids -> bytes."""
+
+    FAIL = 2**64 - 1
+
+    def __init__(self, path):
+        self.lib = _abi.load()
+        err = ctypes.create_string_buffer(256)
+        self.handle = self.lib.plamo_tokenizer_open(os.fsencode(path), err, 256)
+        if not self.handle:
+            raise ValueError(err.value.decode() or f"cannot open {path}")
+
+    def encode(self, text, direction=0):
+        ids = ctypes.POINTER(ctypes.c_uint32)()
+        err = ctypes.create_string_buffer(256)
+        data = text.encode() if isinstance(text, str) else bytes(text)
+        n = self.lib.plamo_tokenizer_encode(self.handle, data, direction, ctypes.byref(ids), err, 256)
+        if n == self.FAIL:
+            raise ValueError(err.value.decode())
+        return np.array([ids[i] for i in range(n)], dtype=np.uint32)
+
+    def prefix(self, direction):
+        """The fixed prompt prefix of a source language (0: English, 1: Japanese)."""
+        ids = ctypes.POINTER(ctypes.c_uint32)()
+        err = ctypes.create_string_buffer(256)
+        n = self.lib.plamo_tokenizer_prefix(self.handle, direction, ctypes.byref(ids), err, 256)
+        if n == self.FAIL:
+            raise ValueError(err.value.decode() or "unsupported prefix direction")
+        return np.array([ids[i] for i in range(n)], dtype=np.uint32)
+
+    def decode(self, ids):
+        """Bytes of the pieces (BYTE pieces are raw bytes: decode the result as UTF-8)."""
+        out = b""
+        for i in np.atleast_1d(ids):
+            p = ctypes.c_char_p()
+            n = self.lib.plamo_tokenizer_decode(self.handle, int(i), ctypes.byref(p))
+            if n == self.FAIL:
+                raise ValueError(f"token {int(i)} is outside the vocabulary")
+            out += ctypes.string_at(p, n)
+        return out
+
+    def close(self):
+        if self.handle:
+            self.lib.plamo_tokenizer_close(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
 class Checkpoint:
     """Mapped BF16 safetensors shards bound to a profile's weight schema
     (reference src/model_open.s: map every shard, bind every schema entry with

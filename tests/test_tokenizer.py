@@ -136,3 +136,26 @@ def test_invalid_requests_fail_with_a_reason(tokenizer):
     assert "UTF-8" in encode(tokenizer, b"\xff")[1]
     assert "4096" in encode(tokenizer, "a" * 4097)[1]
     assert encode(tokenizer, "")[0] == []
+
+
+def test_python_tokenizer_class(tokenizer, tmp_path):
+    pkg = load_package()
+    lib, t = tokenizer
+    # the module fixture's vocabulary, reopened through the package class
+    rows = ['["unused", 0, "NORMAL"]'] + [f'["<0x{b:02X}>", 0, "BYTE"]' for b in range(256)]
+    rows += [f'["{p[0]}", {p[1]}, "{p[2] if len(p) > 2 else "NORMAL"}"]' for p in PIECES]
+    rows += ['["x", -1, "NORMAL"]'] * (107520 - len(rows))
+    path = tmp_path / "v.jsonl"
+    path.write_text("\n".join(rows) + "\n", encoding="utf-8")
+    with pkg.Tokenizer(path) as tok:
+        ids = tok.encode("日本語😀")
+        assert ids.tolist() == encode(tokenizer, "日本語😀")[0]
+        assert tok.decode(ids).decode() == "日本語😀"
+        assert tok.encode("日本語", 1).tolist() == encode(tokenizer, "日本語", 1)[0]
+        assert tok.prefix(0).size > 0
+        with pytest.raises(ValueError, match="direction"):
+            tok.encode("a", 3)
+        with pytest.raises(ValueError):
+            tok.decode([107520])
+    with pytest.raises(ValueError, match="missing"):
+        pkg.Tokenizer(tmp_path / "absent.jsonl")
