@@ -189,6 +189,36 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def gemv_cpu_baseline(rows=4096, cols=4096, threads=(1, 8), seconds=0.5):
+    """GEMV benchmark case 1 on the host cores: the oracle's matvec (the
+    reference CPU accumulation order, rows split across threads) on W ~ N(0,
+    0.02) rounded to BF16 and x ~ N(0, 1) from default_rng(0); GB/s of
+    algorithmic bytes (2*rows*cols + 4*cols + 4*rows) per thread count."""
+    lib = oracle_lib()
+    P, U64 = ctypes.c_void_p, ctypes.c_uint64
+    lib.plamo_bf16_matvec.restype, lib.plamo_bf16_matvec.argtypes = None, [P, P, P, U64, U64]
+    rng = np.random.default_rng(0)
+    bits = rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float32).view(np.uint32).astype(np.uint64)
+    w = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16).astype(np.uint16)
+    x = rng.normal(0.0, 1.0, size=cols).astype(np.float32)
+    y = np.zeros(rows, dtype=np.float32)
+    algorithmic = 2 * rows * cols + 4 * cols + 4 * rows
+    out = {}
+    for t in threads:
+        lib.oracle_set_threads(int(t))
+        lib.plamo_bf16_matvec(w.ctypes.data, x.ctypes.data, y.ctypes.data, rows, cols)
+        calls, t0 = 0, time.perf_counter()
+        while True:
+            lib.plamo_bf16_matvec(w.ctypes.data, x.ctypes.data, y.ctypes.data, rows, cols)
+            calls += 1
+            elapsed = time.perf_counter() - t0
+            if elapsed >= seconds:
+                break
+        out[f"threads_{t}"] = algorithmic * calls / elapsed / 1e9
+    lib.oracle_set_threads(1)
+    return {"unit": "GB/s", "shape": f"{rows}x{cols}", "kind": "port", **out}
+
+
 def oracle_decode_rate(pkg, hm, tokens, prompt_tokens, threads):
     """C oracle (restatement of the reference CPU path) decode tok/s on `hm`."""
     lib = oracle_lib()
@@ -354,7 +384,8 @@ def run_ours(args, world, rank, local, dist):
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
                "sample": f"8B-shaped decode, {tokens} tokens after a {prompt}-token prompt "
                          "(same weights; C restatement of the reference CPU path, row-split "
-                         "threads)"}
+                         "threads)",
+               "gemv": gemv_cpu_baseline()}
         del host, blob
 
     if rank == 0:

@@ -45,3 +45,10 @@ def test_roofline_inputs_are_present_and_consistent():
     assert abs((r["dram_read"] + r["dram_write"]) / r["algorithmic"] - r["ratio"]) < 1e-3
     g = t["gemv_gate_up_8b"]
     assert 0.99 < (g["dram_read"] + g["dram_write"]) / g["algorithmic"] < 1.05
+
+
+def test_gemv_cpu_baseline_reports_each_thread_count():
+    b = bench()
+    r = b.gemv_cpu_baseline(rows=64, cols=256, threads=(1, 2), seconds=0.01)
+    assert r["unit"] == "GB/s" and r["shape"] == "64x256" and r["kind"] == "port"
+    assert r["threads_1"] > 0 and r["threads_2"] > 0
