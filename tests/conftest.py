@@ -15,6 +15,9 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG_DIR = os.path.join(ROOT, "plamo-3-translate.c_b200")
 ORACLE_DIR = os.path.join(ROOT, "oracle")
+# Checkout of the reference project whose own tests pin the oracle, the loader and
+# the tokenizer (absent on GPU hosts: those tests skip).
+REF = os.environ.get("PLAMO_REFERENCE", "/root/reference")
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 

@@ -15,9 +15,7 @@ import subprocess
 import numpy as np
 import pytest
 
-from conftest import ORACLE_DIR, load_oracle, load_package
-
-REF = "/root/reference"
+from conftest import REF, ORACLE_DIR, load_oracle, load_package
 
 
 @pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "tests")),

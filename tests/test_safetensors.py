@@ -13,9 +13,7 @@ import subprocess
 import numpy as np
 import pytest
 
-from conftest import load_package
-
-REF = "/root/reference"
+from conftest import REF, load_package
 
 
 @pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "tests")),

@@ -14,9 +14,8 @@ import subprocess
 
 import pytest
 
-from conftest import load_package
+from conftest import REF, load_package
 
-REF = "/root/reference"
 REFERENCE_TESTS = ["utf8", "string", "score", "json", "vocab", "vocab_load", "trie", "unigram", "encode",
                    "boundary", "preprocess", "decode", "tokenizer"]
 
