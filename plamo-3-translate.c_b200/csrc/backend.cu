@@ -10,6 +10,7 @@
 #include "attention.cuh"
 #include "rows.cuh"
 #include "gemm_tc.cuh"
+#include "persist.cuh"
 #include "tp.cuh"
 
 #include <cudaTypedefs.h>
@@ -119,6 +120,11 @@ struct DModel {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
     uint64_t graph_nodes = 0;
+    // persistent decode (one launch per token, single GPU)
+    bool pt_ready = false;
+    PtParams pt{};
+    uint32_t pt_grid = 0;
+    size_t pt_smem = 0;
     std::vector<void *> allocations;
     std::vector<uintptr_t> signature;  // host descriptor identity at prepare time
 };
@@ -151,6 +157,8 @@ struct plamo_cuda {
     unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
     bool tc_gemm;
     bool prompt_attn;  // blocked prompt attention (PLAMO_CUDA_PROMPT_ATTN=0 disables)
+    bool persistent;   // one-launch decode step where the shapes allow (PLAMO_CUDA_PERSISTENT=0 disables)
+    bool cooperative;  // the device supports cooperative launches
     int gemv_ctas;
     uint32_t *sink;
     float *static_scratch;  // device address of g_linear_static_scratch (set on first use)
@@ -968,8 +976,151 @@ bool record_batch(plamo_cuda *c, plamo_cuda_batch *b, DModel *m) {
                   b->B);
 }
 
+// ---- persistent decode step --------------------------------------------------
+// Shapes the one-launch step takes: head dim 128, at most 16 query heads per
+// KV head, every projection's columns a whole number (<= 32) of 512-column
+// slots, a hidden size the prologue holds in registers, and a grid of one
+// co-resident CTA per SM with at least three ring stages.
+bool persistent_plan(plamo_cuda *c, DModel *m, uint32_t *grid, size_t *smem, uint32_t *stages, uint32_t *splits) {
+    if (!c->persistent || !c->cooperative || m->tp.active || m->D != 128 || m->QH % m->KH) return false;
+    const uint64_t G = m->QH / m->KH;
+    if (G > kPtMaxG || m->H % 512 || m->AW % 512 || m->I % 512 || m->H > kPtMaxHidden) return false;
+    if (m->H / 512 > kPtMaxSlots || m->AW / 512 > kPtMaxSlots || m->I / 512 > kPtMaxSlots) return false;
+    if (m->L > 0xffff || m->Vh > 0xffffffffull || m->QW > 0xffffffffull) return false;
+    // Bulk copies and vector loads of every weight need 16-byte alignment
+    // (a mapped checkpoint can place a tensor anywhere).
+    auto aligned = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    if (!aligned(m->emb) || !aligned(m->norm) || !aligned(m->head)) return false;
+    for (const DLayer &L : m->layers)
+        for (const void *w : {static_cast<const void *>(L.qkv_w), static_cast<const void *>(L.o_w),
+                              static_cast<const void *>(L.gu), static_cast<const void *>(L.down),
+                              static_cast<const void *>(L.pre), static_cast<const void *>(L.post),
+                              static_cast<const void *>(L.mpre), static_cast<const void *>(L.mpost),
+                              static_cast<const void *>(L.qn), static_cast<const void *>(L.kn)})
+            if (!aligned(w)) return false;
+    const uint32_t g = static_cast<uint32_t>(c->sm_count);
+    const uint32_t S = static_cast<uint32_t>(std::max<uint64_t>(
+        1, std::min<uint64_t>({g / m->KH, kPtMaxSplits, 384 / G})));
+    // Largest per-CTA partial block of any projection: rows x slots x pair.
+    uint64_t part = 0;
+    const uint64_t shapes[5][3] = {{m->QW, m->H, 1}, {m->H, m->AW, 1}, {m->I, m->H, 2}, {m->H, m->I, 1},
+                                   {m->Vh, m->H, 1}};
+    for (const auto &sh : shapes) part = std::max<uint64_t>(part, (sh[0] + g - 1) / g * (sh[1] / 512) * sh[2]);
+    const uint64_t work =
+        std::max<uint64_t>(((m->H + 3) & ~3ull) + part, pt_attention_floats(static_cast<uint32_t>(G), S)) * 4;
+    cudaFuncAttributes attr{};
+    if (cudaFuncGetAttributes(&attr, decode_token_kernel) != cudaSuccess) return false;
+    const int64_t room = static_cast<int64_t>(c->smem_optin) - static_cast<int64_t>(attr.sharedSizeBytes) -
+                         static_cast<int64_t>(work);
+    const int64_t st = std::min<int64_t>(kPtMaxStages, room / kPtStageBytes);
+    if (st < 3) return false;
+    const size_t bytes = static_cast<size_t>(st) * kPtStageBytes + work;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_token_kernel, kPtThreads, bytes) !=
+            cudaSuccess ||
+        per_sm < 1)
+        return false;
+    *grid = g;
+    *smem = bytes;
+    *stages = static_cast<uint32_t>(st);
+    *splits = S;
+    return true;
+}
+
+bool persistent_init(plamo_cuda *c, DModel *m) {
+    uint32_t grid = 0, stages = 0, S = 0;
+    size_t smem = 0;
+    if (!persistent_plan(c, m, &grid, &smem, &stages, &S)) return false;
+    std::vector<PtLayer> layers(m->L);
+    for (uint64_t l = 0; l < m->L; ++l) {
+        const DLayer &L = m->layers[l];
+        layers[l] = PtLayer{L.qkv_w, L.o_w, L.gu, L.down, L.pre, L.post, L.mpre, L.mpost, attn_layer(m, l)};
+    }
+    const uint64_t G = m->QH / m->KH;
+    auto *d_layers = static_cast<PtLayer *>(dalloc(c, m, m->L * sizeof(PtLayer)));
+    auto *apart = static_cast<float *>(dalloc(c, m, m->KH * S * G * (128 + 2) * 4));
+    auto *arrive = static_cast<uint32_t *>(dalloc(c, m, std::max<uint64_t>(m->KH, 4) * 4));
+    auto *counters = static_cast<unsigned long long *>(dalloc(c, m, 16));
+    if (!d_layers || !apart || !arrive || !counters) return false;
+    if (!note(c, "persistent layers", cudaMemcpyAsync(d_layers, layers.data(), m->L * sizeof(PtLayer),
+                                                      cudaMemcpyHostToDevice, c->stream)) ||
+        !note(c, "persistent counters", cudaMemsetAsync(arrive, 0, std::max<uint64_t>(m->KH, 4) * 4, c->stream)) ||
+        !note(c, "persistent counters", cudaMemsetAsync(counters, 0, 16, c->stream)) ||
+        !note(c, "persistent init", cudaStreamSynchronize(c->stream)))
+        return false;
+    PtParams &p = m->pt;
+    p.layers = d_layers;
+    p.L = static_cast<uint32_t>(m->L);
+    p.H = static_cast<uint32_t>(m->H);
+    p.QH = static_cast<uint32_t>(m->QH);
+    p.KH = static_cast<uint32_t>(m->KH);
+    p.AW = static_cast<uint32_t>(m->AW);
+    p.I = static_cast<uint32_t>(m->I);
+    p.QW = static_cast<uint32_t>(m->QW);
+    p.head_rows = static_cast<uint32_t>(m->Vh);
+    p.vocab = m->V;
+    p.emb = m->emb;
+    p.norm = m->norm;
+    p.head = m->head;
+    p.token = m->d_token;
+    p.next = m->d_next;
+    p.state[0] = m->state[0];
+    p.state[1] = m->state[1];
+    p.normalized = m->normalized;
+    p.logits = m->logits;
+    p.qkv = m->qkv;
+    p.attn = m->attn;
+    p.branch = m->branch;
+    p.mid = m->mid;
+    p.apart = apart;
+    p.head_arrive = arrive;
+    p.bar = counters;
+    p.gen = counters + 1;
+    p.arg_val = m->arg_val;
+    p.arg_val2 = m->arg_val2;
+    p.arg_idx = m->arg_idx;
+    p.arg_nan = m->arg_nan;
+    p.appended = m->d_appended;
+    p.S = S;
+    p.stages = stages;
+    m->pt_grid = grid;
+    m->pt_smem = smem;
+    // The step leaves its final state where the graph's does: the layers flip
+    // the ping-pong 2L - 1 times after layer 0 wrote state[0], the head once
+    // more, so the head writes state[0].
+    m->final_state = m->state[0];
+    m->pt_ready = true;
+    return true;
+}
+
+// Counters back to zero after a failed step (a CTA that stopped early left
+// arrivals behind); the next launch starts from generation 0.
+bool persistent_reset(plamo_cuda *c, DModel *m) {
+    return note(c, "persistent reset",
+                cudaMemsetAsync(m->pt.head_arrive, 0, std::max<uint64_t>(m->KH, 4) * 4, c->stream)) &&
+           note(c, "persistent reset", cudaMemsetAsync(m->pt.bar, 0, 16, c->stream)) &&
+           note(c, "persistent reset", cudaStreamSynchronize(c->stream));
+}
+
+bool launch_persistent(plamo_cuda *c, DModel *m) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(m->pt_grid);
+    cfg.blockDim = dim3(kPtThreads);
+    cfg.dynamicSmemBytes = m->pt_smem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (!note(c, "persistent decode", cudaLaunchKernelEx(&cfg, decode_token_kernel, m->pt))) return false;
+    c->info.launches++;
+    return true;
+}
+
 bool ensure_graph(plamo_cuda *c, DModel *m) {
-    if (m->graph_exec) return true;
+    if (m->graph_exec || m->pt_ready) return true;
+    if (persistent_init(c, m)) return true;
     if (!note(c, "capture", cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal)))
         return false;
     const uint64_t before = c->info.launches;
@@ -987,6 +1138,11 @@ bool ensure_graph(plamo_cuda *c, DModel *m) {
 }
 
 bool launch_decode(plamo_cuda *c, DModel *m) {
+    if (m->pt_ready) {
+        if (!launch_persistent(c, m)) return false;
+        c->info.graph_launches++;
+        return true;
+    }
     if (!note(c, "graph launch", cudaGraphLaunch(m->graph_exec, c->stream))) return false;
     c->info.graph_launches++;
     c->info.launches += m->graph_nodes;
@@ -998,10 +1154,12 @@ bool check_device_error(plamo_cuda *c, DModel *m) {
     if (!note(c, "error flag", cudaMemcpy(&err, m->d_error, 4, cudaMemcpyDeviceToHost))) return false;
     if (err) {
         cudaMemset(m->d_error, 0, 4);
+        if (m->pt_ready) persistent_reset(c, m);
         c->info.errors++;
         snprintf(c->info.note, sizeof c->info.note, "%s",
                  err == 1   ? "device rejected a token id"
                  : err == 4 ? "a tensor-parallel peer did not arrive within 2 s"
+                 : err == 5 ? "a decode grid barrier did not complete within 2 s"
                             : "a weight stream stalled for 2 s");
         return false;
     }
@@ -1205,6 +1363,11 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_gemm = !tc || strcmp(tc, "0");
     const char *pa = getenv("PLAMO_CUDA_PROMPT_ATTN");
     c->prompt_attn = !pa || strcmp(pa, "0");
+    const char *pt = getenv("PLAMO_CUDA_PERSISTENT");
+    c->persistent = !pt || strcmp(pt, "0");
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, cfg.device);
+    c->cooperative = coop != 0;
     // Draft confidence settings, parsed as reference runtime/worker.c:199-208
     // (invalid values fall back to the default rule).
     c->draft_margin = -1.0f;
@@ -1264,6 +1427,7 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     allow_smem(decode_attention_kernel<128>, optin);
     allow_smem(decode_attention128_batch_kernel, optin);
     allow_smem(decode_attention_kernel<0>, optin);
+    allow_smem(decode_token_kernel, optin);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         if (error && cap) snprintf(error, cap, "cannot configure kernels: %s", cudaGetErrorString(e));
         plamo_cuda_close(c);
@@ -1975,12 +2139,15 @@ int plamo_cuda_linear_static(struct plamo_cuda *c, const struct plamo_matmul *mm
     if (!mm->rows || !mm->tokens) return 1;
     cudaSetDevice(c->device);
     const uint64_t T = mm->tokens, K = mm->columns, R = mm->rows;
-    if (T * K + T * R > kStaticLinearFloats || T * K / T != K || T * R / T != R) {
+    // Each product is bounded before the sum is formed (T >= 1 here), so no
+    // intermediate can wrap: K, R <= limit / T keeps T*K and T*R <= limit.
+    if (K > kStaticLinearFloats / T || R > kStaticLinearFloats / T || T * K > kStaticLinearFloats - T * R) {
         c->info.declines++;
         snprintf(c->info.note, sizeof c->info.note,
-                 "linear_static: %llu input + %llu output floats exceed the static staging of %llu floats",
-                 static_cast<unsigned long long>(T * K), static_cast<unsigned long long>(T * R),
-                 static_cast<unsigned long long>(kStaticLinearFloats));
+                 "linear_static: %llu tokens x (%llu input + %llu output) floats exceed the static staging of %llu "
+                 "floats",
+                 static_cast<unsigned long long>(T), static_cast<unsigned long long>(K),
+                 static_cast<unsigned long long>(R), static_cast<unsigned long long>(kStaticLinearFloats));
         return 0;
     }
     const uint16_t *w = resolve(c, mm->weights, R * K * 2, false);

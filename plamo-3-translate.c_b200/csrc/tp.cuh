@@ -14,10 +14,14 @@
 // so every rank computes the same bits.
 //
 // Decode points use a low-latency form instead of flags: every partial value
-// travels with its epoch tag as one 8-byte store {value, epoch + 1}, which
-// reaches the peer as a unit, so the consumer polls the values themselves and
-// proceeds the moment the last one lands - no fence, ticket or flag round
-// trip on the producer side (the protocol NCCL calls LL).
+// travels with its epoch tag in one aligned 64-bit word (value bits in the low
+// half, epoch + 1 in the high half), written with one scalar 64-bit relaxed
+// system-scope store and read with loads whose elements are 64-bit words
+// (scalar, or a v2.u64 vector, which the PTX memory model treats as two
+// 64-bit element accesses). An aligned 64-bit access is single-copy atomic,
+// so a reader that sees the new tag also sees the value stored with it; the
+// consumer polls the values themselves and proceeds the moment the last one
+// lands - no fence, ticket or flag round trip on the producer side.
 //
 // Epochs: a device counter, advanced once at the end of every tensor-parallel
 // operation (decode step, prompt, verification) on every rank; a flag holds
@@ -96,27 +100,29 @@ __device__ __forceinline__ void tp_signal(const TpPoint &t) {
     }
 }
 
-__device__ __forceinline__ uint4 ld_volatile4(const void *p) {
-    uint4 v;
-    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p)
-                 : "memory");
+// Tagged words of the low-latency points: {value bits, tag} as one 64-bit
+// word. Two consecutive words per load (16-byte aligned); each element is
+// a 64-bit access of its own.
+__device__ __forceinline__ ulonglong2 ld_tagged2(const void *p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ uint2 ld_volatile2(const void *p) {
-    uint2 v;
-    asm volatile("ld.volatile.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_tagged1(const void *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void st_volatile2(void *p, uint32_t a, uint32_t b) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+__device__ __forceinline__ void st_tagged(void *p, float value, uint32_t tag) {
+    const uint64_t word = static_cast<uint64_t>(__float_as_uint(value)) | (static_cast<uint64_t>(tag) << 32);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(word) : "memory");
 }
+__device__ __forceinline__ uint32_t tag_of(uint64_t word) { return static_cast<uint32_t>(word >> 32); }
+__device__ __forceinline__ float value_of(uint64_t word) { return __uint_as_float(static_cast<uint32_t>(word)); }
 
 // Low-latency point: this rank's value of element `unit` to every rank.
 __device__ __forceinline__ void tp_ll_store(const TpPoint &t, uint64_t unit, float v, uint32_t tag) {
-    for (uint32_t r = 0; r < t.tp; ++r)
-        st_volatile2(reinterpret_cast<uint2 *>(t.peer_parts[r]) + unit, __float_as_uint(v), tag);
+    for (uint32_t r = 0; r < t.tp; ++r) st_tagged(reinterpret_cast<uint64_t *>(t.peer_parts[r]) + unit, v, tag);
 }
 
 // Wait (bounded) until `ok(...)` holds for the polled words; false on timeout
@@ -144,8 +150,8 @@ __device__ __forceinline__ void tp_ll_sum_groups(const TpPoint &t, uint32_t i0, 
                                                  uint32_t tag, float4 (&out)[KP]) {
     uint64_t start = 0;
     for (uint32_t r = 0; r < t.tp; ++r) {
-        const uint2 *slot = reinterpret_cast<const uint2 *>(t.parts) + r * t.stride;
-        uint4 a[KP], b[KP];
+        const uint64_t *slot = reinterpret_cast<const uint64_t *>(t.parts) + r * t.stride;
+        ulonglong2 a[KP], b[KP];
         uint32_t pending = 0;
 #pragma unroll
         for (int k = 0; k < KP; ++k)
@@ -155,13 +161,14 @@ __device__ __forceinline__ void tp_ll_sum_groups(const TpPoint &t, uint32_t i0, 
 #pragma unroll
             for (int k = 0; k < KP; ++k)
                 if (pending >> k & 1u) {
-                    const uint4 *src = reinterpret_cast<const uint4 *>(slot + 4ull * (i0 + k * step));
-                    a[k] = ld_volatile4(src);
-                    b[k] = ld_volatile4(src + 1);
+                    const uint64_t *src = slot + 4ull * (i0 + k * step);
+                    a[k] = ld_tagged2(src);
+                    b[k] = ld_tagged2(src + 2);
                 }
 #pragma unroll
             for (int k = 0; k < KP; ++k)
-                if ((pending >> k & 1u) && a[k].y == tag && a[k].w == tag && b[k].y == tag && b[k].w == tag)
+                if ((pending >> k & 1u) && tag_of(a[k].x) == tag && tag_of(a[k].y) == tag &&
+                    tag_of(b[k].x) == tag && tag_of(b[k].y) == tag)
                     pending &= ~(1u << k);
             if (!pending || tp_failed(t.error)) break;
             if (!start) start = global_ns();
@@ -173,8 +180,7 @@ __device__ __forceinline__ void tp_ll_sum_groups(const TpPoint &t, uint32_t i0, 
 #pragma unroll
         for (int k = 0; k < KP; ++k)
             if (present >> k & 1u) {
-                const float4 v = make_float4(__uint_as_float(a[k].x), __uint_as_float(a[k].z), __uint_as_float(b[k].x),
-                                             __uint_as_float(b[k].z));
+                const float4 v = make_float4(value_of(a[k].x), value_of(a[k].y), value_of(b[k].x), value_of(b[k].y));
                 out[k] = r ? make_float4(__fadd_rn(out[k].x, v.x), __fadd_rn(out[k].y, v.y), __fadd_rn(out[k].z, v.z),
                                          __fadd_rn(out[k].w, v.w))
                            : v;
@@ -186,10 +192,10 @@ __device__ __forceinline__ float tp_ll_sum1(const TpPoint &t, uint64_t i, uint32
     float s = 0.0f;
     uint64_t start = 0;
     for (uint32_t r = 0; r < t.tp; ++r) {
-        const uint2 *src = reinterpret_cast<const uint2 *>(t.parts) + r * t.stride + i;
-        uint2 a;
-        tp_ll_poll(t, [&] { a = ld_volatile2(src); }, [&] { return a.y == tag; }, start);
-        s = r ? __fadd_rn(s, __uint_as_float(a.x)) : __uint_as_float(a.x);
+        const uint64_t *src = reinterpret_cast<const uint64_t *>(t.parts) + r * t.stride + i;
+        uint64_t a = 0;
+        tp_ll_poll(t, [&] { a = ld_tagged1(src); }, [&] { return tag_of(a) == tag; }, start);
+        s = r ? __fadd_rn(s, value_of(a)) : value_of(a);
     }
     return s;
 }

@@ -16,8 +16,9 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG_DIR = os.path.join(ROOT, "plamo-3-translate.c_b200")
 ORACLE_DIR = os.path.join(ROOT, "oracle")
 # Checkout of the reference project whose own tests pin the oracle, the loader and
-# the tokenizer (absent on GPU hosts: those tests skip).
-REF = os.environ.get("PLAMO_REFERENCE", "/root/reference")
+# the tokenizer: $PLAMO_REFERENCE, else a "reference" directory beside this
+# repository (absent on GPU hosts: those tests skip).
+REF = os.environ.get("PLAMO_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 
@@ -60,6 +61,7 @@ def load_oracle():
         "plamo_rope_table": (None, [P, U64, U64, P, P, ctypes.c_float]),
         "oracle_set_threads": (None, [ctypes.c_int]),
         "plamo_cache_rope": (None, [P, ctypes.c_float]),
+        "oracle_synthetic_bf16": (None, [P, U64, U64, ctypes.c_float, ctypes.c_float, ctypes.c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -22,7 +22,21 @@ the pin travels without the reference checkout:
                   global capacity 40, vocab 17): prefill of 6 ids, then 4
                   forward steps; state and logits after each call.
 
-Usage: python tests/golden/make_golden.py (rewrites the three .npz files).
+  model_8b.npz    (--large) BASELINE config 4 at its full size: profile 8b
+                  with the seeded synthetic weights of seed 4 (the benchmark's
+                  model), a 455-id prompt (default_rng(1) over [3, 100000)),
+                  the state and logits after the prefill, then 64 greedy
+                  tokens with the top-2 logit margin of every step.
+  tp_31b_cut.npz  (--large) a two-layer cut of profile 31b (one sliding and
+                  one full layer, tied head, seed 8): prefill of 20 ids
+                  (default_rng(1) over [3, 100000)), then 32 greedy tokens and
+                  their margins - the token check of the tensor-parallel
+                  benchmark at every rank count.
+
+Usage: python tests/golden/make_golden.py [--large]
+(rewrites the three small .npz files; --large writes the two whole-model
+fixtures instead, which streams 16 GB of weights per oracle token on the host
+and takes several minutes with every host core).
 """
 import hashlib
 import os
@@ -150,7 +164,52 @@ def make_decode_fixture():
             "logits": np.stack(logits)}
 
 
+LARGE_8B = dict(profile="8b", seed=4, prompt=455, tokens=64, prompt_seed=1, full_capacity=8208)
+LARGE_31B_CUT = dict(profile="31b", seed=8, prompt=20, tokens=32, prompt_seed=1, full_capacity=1024, layers=2,
+                     pattern=2)
+
+
+def large_host_model(spec):
+    """Host model of a profile with the device generator's synthetic weights
+    (seed * 1000003 + tensor slot, the restatement in the oracle)."""
+    from dataclasses import replace
+    pkg = load_package()
+    prof = pkg.PROFILES[spec["profile"]]
+    if "layers" in spec:
+        prof = replace(prof, name=f"{prof.name}-{spec['layers']}layers", layers=spec["layers"],
+                       pattern=spec["pattern"])
+    o = load_oracle()
+    hm = pkg.HostModel(prof, weights=np.empty(pkg.HostModel(prof, weights="synthetic").blob_bytes // 2,
+                                              dtype=np.uint16), full_capacity=spec["full_capacity"])
+    threads = os.cpu_count() or 1
+    for k, (addr, count, name) in enumerate(hm.tensor_ranges()):
+        mean, std = pkg.synthetic_parameters(name)
+        o.oracle_synthetic_bf16(addr, count, spec["seed"] * 1000003 + k, mean, std, threads)
+    return hm
+
+
+def make_large(spec):
+    o = load_oracle()
+    o.oracle_set_threads(os.cpu_count() or 1)
+    hm = large_host_model(spec)
+    ids = np.random.default_rng(spec["prompt_seed"]).integers(3, 100000, size=spec["prompt"]).astype(np.uint32)
+    oracle_prefill(hm, ids)
+    fields = {"ids": ids, "prefill_logits": hm.logits_array().copy(), "prefill_state": hm.state_array().copy(),
+              "profile": np.array(hm.profile.name), "seed": np.array(spec["seed"]),
+              "embed_sha256": np.array(sha256(hm.tensor("model.embed_tokens.weight")))}
+    tokens, margins = oracle_greedy(hm, spec["tokens"])
+    fields["tokens"] = tokens
+    fields["margins"] = margins
+    return fields
+
+
 def main():
+    if "--large" in sys.argv[1:]:
+        for name, spec in (("tp_31b_cut", LARGE_31B_CUT), ("model_8b", LARGE_8B)):
+            path = os.path.join(HERE, f"{name}.npz")
+            np.savez_compressed(path, **make_large(spec))
+            print(f"wrote {path} ({os.path.getsize(path)} bytes)", flush=True)
+        return
     load_oracle().oracle_set_threads(1)
     for name, make in (("gemv", make_gemv), ("model_small", make_small), ("decode_fixture", make_decode_fixture)):
         path = os.path.join(HERE, f"{name}.npz")

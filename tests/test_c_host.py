@@ -9,9 +9,11 @@ declines with a message and the program stops there, so the host half runs
 on any machine.
 """
 import os
+import re
 import subprocess
 
 import numpy as np
+import pytest
 
 from conftest import ROOT, load_package
 
@@ -81,7 +83,8 @@ int main(int argc, char **argv) {
 """
 
 
-def test_c_host_program_builds_and_runs_the_host_path(tmp_path):
+def build_host_program(tmp_path):
+    """(executable, vocabulary file, checkpoint) of the C host program."""
     pkg = load_package()
     pkg.load()
     libdir = os.path.dirname(pkg.LIB_PATH)
@@ -107,8 +110,23 @@ def test_c_host_program_builds_and_runs_the_host_path(tmp_path):
         tensors[name] = (x.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
     ckpt = tmp_path / "model.safetensors"
     pkg.write_safetensors(ckpt, tensors)
+    return exe, vocab, ckpt
 
+
+def test_c_host_program_builds_and_runs_the_host_path(tmp_path):
+    exe, vocab, ckpt = build_host_program(tmp_path)
     r = subprocess.run([str(exe), str(vocab), str(ckpt)], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "model of 2 layers bound" in r.stdout
     assert "no CUDA device: declined with a reason" in r.stdout or "generated" in r.stdout
+
+
+@pytest.mark.gpu
+def test_c_host_program_generates_on_the_gpu(tmp_path):
+    """The same program on a GPU host: the backend opens, preloads the mapped
+    checkpoint, prepares the run-time descriptors and generates up to 8
+    tokens (fewer when a stop id comes first)."""
+    exe, vocab, ckpt = build_host_program(tmp_path)
+    r = subprocess.run([str(exe), str(vocab), str(ckpt)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert re.search(r"generated [0-8] tokens", r.stdout), r.stdout

@@ -83,3 +83,58 @@ def test_decode_fixture_matches_golden(backend):
             assert_close(a.logits_array(), g["logits"][i], f"step {i} logits")
     finally:
         backend.release(a)
+
+
+def large_model(backend, spec):
+    from dataclasses import replace
+    pkg = load_package()
+    prof = pkg.PROFILES[spec["profile"]]
+    if "layers" in spec:
+        prof = replace(prof, name=f"{prof.name}-{spec['layers']}layers", layers=spec["layers"],
+                       pattern=spec["pattern"])
+    hm = pkg.HostModel(prof, weights="synthetic", full_capacity=spec["full_capacity"])
+    backend.preload_synthetic(hm, spec["seed"])
+    backend.prepare(hm)
+    return hm
+
+
+def first_flip(got, want, margins):
+    for i, (a, b) in enumerate(zip(got, want)):
+        if a != b:
+            return f"first difference at token {i}: {a} vs {b}, oracle top-2 margin there {margins[i]:.4g}"
+    return f"lengths {len(got)} vs {len(want)}"
+
+
+@pytest.mark.parametrize("name,spec", [("model_8b", golden.LARGE_8B), ("tp_31b_cut", golden.LARGE_31B_CUT)])
+def test_large_model_matches_golden(backend, name, spec):
+    """BASELINE config 4 at its full size (8B profile, the benchmark's weights,
+    455-id prompt, 64 greedy tokens) and the 31B-shaped two-layer cut: the
+    prefill logits and state within the whole-model rule, the greedy tokens
+    identical to the oracle's (a flip is reported with its oracle margin)."""
+    pkg = load_package()
+    g = fixture(name)
+    hm = large_model(backend, spec)
+    try:
+        emb = np.empty(hm.profile.vocab * hm.profile.hidden, dtype=np.uint16)
+        key = hm.tensor_ranges()[0][0]
+        expect(backend, backend.lib.plamo_cuda_read_weights(backend.ctx, key, emb.ctypes.data, emb.nbytes))
+        assert golden.sha256(emb) == str(g["embed_sha256"]), "device weights differ from the fixture's"
+        del emb
+        ids = np.ascontiguousarray(g["ids"], dtype=np.uint32)
+        expect(backend, backend.lib.plamo_cuda_prefill(backend.ctx, hm.ptr, ids.ctypes.data, len(ids), 0))
+        for what, got, want in (("logits", hm.logits_array(), g["prefill_logits"]),
+                                ("state", hm.state_array(), g["prefill_state"])):
+            assert np.all(np.isfinite(got)), what
+            assert rel_l2(got, want) <= 1e-4, f"{name} prefill {what}: {rel_l2(got, want):.3g}"
+        hm.reset()
+        n_want = len(g["tokens"])
+        out = np.zeros(n_want, dtype=np.uint32)
+        timing = pkg._abi.CudaTiming()
+        n = backend.lib.plamo_cuda_generate(backend.ctx, hm.ptr, ids.ctypes.data, len(ids), n_want,
+                                            out.ctypes.data, pkg._abi.TOKEN_CALLBACK(), None, ctypes.byref(timing))
+        assert n >= 0, backend.info().note
+        got, want = out[:n].tolist(), g["tokens"].tolist()
+        print(f"{name}: {n} tokens, smallest oracle top-2 margin {float(np.min(g['margins'])):.4g}")
+        assert got == want, first_flip(got, want, g["margins"])
+    finally:
+        backend.release(hm)

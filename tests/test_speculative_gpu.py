@@ -106,3 +106,25 @@ def test_greedy_margin_is_the_top2_logit_gap(backend):
         token = nxt.value
     lib.plamo_cuda_release_model(backend.ctx, b.ptr)
     lib.plamo_cuda_release_model(backend.ctx, a.ptr)
+
+
+def test_config5_form_matches_the_oracle_greedy_tokens(backend):
+    """The speculative loop of BASELINE config 5 on one GPU: a 0.8B-shaped
+    draft proposing 4 tokens per verification for a larger target (the 2B
+    profile here, whose oracle run fits the host), 64 tokens after an 81-id
+    prompt - identical to the oracle's greedy tokens, not only to the GPU's
+    own greedy path."""
+    import os
+    from conftest import load_oracle
+    from test_model_gpu import oracle_generate, synthetic_pair
+    pkg = load_package()
+    load_oracle().oracle_set_threads(os.cpu_count() or 1)
+    target, host = synthetic_pair(backend, pkg.PROFILES["2b"], seed=3, full_capacity=8208)
+    draft = pkg.HostModel(pkg.PROFILES["0.8b"], weights="synthetic", full_capacity=8208)
+    backend.preload_synthetic(draft, seed=6)
+    backend.prepare(draft)
+    ids = np.random.default_rng(1).integers(3, 100000, size=81).astype(np.uint32)
+    want, margins = oracle_generate(host, ids, 64)
+    got, st = speculative(backend, target, draft, ids, 64, 4)
+    assert got == want, f"margins {margins}"
+    assert st.verify_batches > 0

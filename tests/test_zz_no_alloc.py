@@ -18,7 +18,7 @@ import numpy as np
 import pytest
 
 import synthetic
-from conftest import expect, load_package, rel_l2
+from conftest import expect, load_oracle, load_package, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -45,6 +45,11 @@ def test_static_linear_matches_allocating_linear_twice(backend):
             a, b = got[t * ys:t * ys + rows], want[t * ys:t * ys + rows]
             assert rel_l2(a, b) <= 1e-5, f"call {call} token {t}"
             assert np.all(got[t * ys + rows:(t + 1) * ys] == -7.0), "wrote outside the output rows"
+            # And the reference's CPU matvec order (the oracle) on the same row.
+            ref = np.zeros(rows, dtype=np.float32)
+            xt = np.ascontiguousarray(x[t * xs:t * xs + cols])
+            load_oracle().plamo_bf16_matvec(w.ctypes.data, xt.ctypes.data, ref.ctypes.data, rows, cols)
+            assert rel_l2(a, ref) <= 1e-5, f"call {call} token {t} against the oracle"
 
 
 def test_static_linear_declines_requests_beyond_its_array(backend):
@@ -57,6 +62,19 @@ def test_static_linear_declines_requests_beyond_its_array(backend):
     x = np.zeros(tokens * cols, dtype=np.float32)
     y = np.full(tokens * rows, 5.0, dtype=np.float32)
     mm = pkg._abi.Matmul(w.ctypes.data, x.ctypes.data, y.ctypes.data, rows, cols, tokens, cols, rows)
+    assert backend.lib.plamo_cuda_linear_static(backend.ctx, ctypes.byref(mm)) == 0
+    assert b"static staging" in backend.info().note
+    assert np.all(y == 5.0)
+
+
+def test_static_linear_declines_sizes_whose_sum_would_wrap(backend):
+    """tokens x columns and tokens x rows each fit in 64 bits, but their sum
+    wraps to zero: declined by the size check, before any address is used."""
+    pkg = load_package()
+    x = np.zeros(4, dtype=np.float32)
+    y = np.full(4, 5.0, dtype=np.float32)
+    w = np.zeros(4, dtype=np.uint16)
+    mm = pkg._abi.Matmul(w.ctypes.data, x.ctypes.data, y.ctypes.data, 1 << 31, 1 << 31, 1 << 32, 1 << 31, 1 << 31)
     assert backend.lib.plamo_cuda_linear_static(backend.ctx, ctypes.byref(mm)) == 0
     assert b"static staging" in backend.info().note
     assert np.all(y == 5.0)
