@@ -15,6 +15,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <new>
 #include <vector>
 
@@ -577,144 +578,227 @@ uint64_t plamo_translation_prefix(const char *source, char *out, uint64_t capaci
 }  // extern "C"
 
 // ---- the engine's tokenizer (reference runtime/tokenizer.h) -------------------
+//
+// One object per opened vocabulary. It keeps the file's bytes mapped read-only
+// (a decoded token is a slice of its row), the trie and the byte-piece ids
+// built from them, an index of row starts, and every buffer a request needs,
+// sized once at open so that encoding and decoding allocate nothing.
 namespace {
 
-constexpr uint64_t kTrieNodes = 1000000;     // capacity of the vocabulary trie
-constexpr uint64_t kMaxScalars = 4096;       // input scalars per request
-constexpr uint64_t kTempCapacity = 16384;    // after special-token markers
-constexpr uint64_t kMarkedCapacity = 49152;  // after repeat-run markers
+// Capacities of one request (the reference engine's limits).
+constexpr uint64_t kTrieNodes = 1000000;
+constexpr uint64_t kMaxScalars = 4096;       // Unicode scalars of the text
+constexpr uint64_t kTempCapacity = 16384;    // after special-token marking
+constexpr uint64_t kMarkedCapacity = 49152;  // after repeated-run marking
 constexpr uint64_t kMaxIds = 16384;
-constexpr uint64_t kCandidates = 4097;       // trie matches per position + the fallback
-constexpr size_t kTextBytes = 16384;         // prompts and decoded pieces
+constexpr uint64_t kCandidates = 4097;       // trie matches at one position, plus the fallback
+constexpr size_t kTextBytes = 16384;         // a wrapped prompt, a decoded piece
+
+enum class TokStatus { Ok, NoMemory, Unreadable, BadRows, BadLineBreaks, BadArguments, BadDirection,
+                       PromptTooLong, BadText, MarkingOverflow, SegmentOverflow };
+
+const char *status_text(TokStatus s) {
+    switch (s) {
+    case TokStatus::NoMemory: return "tokenizer: out of memory";
+    case TokStatus::Unreadable: return "tokenizer: vocabulary file missing or unreadable";
+    case TokStatus::BadRows: return "tokenizer: vocabulary file is not 107520 well-formed rows";
+    case TokStatus::BadLineBreaks: return "tokenizer: vocabulary line breaks do not match its rows";
+    case TokStatus::BadArguments: return "tokenizer: null tokenizer, text or output";
+    case TokStatus::BadDirection: return "tokenizer: translation direction must be 0, 1 or 2";
+    case TokStatus::PromptTooLong: return "tokenizer: text too long for the translation template";
+    case TokStatus::BadText: return "tokenizer: text is not UTF-8 or longer than 4096 characters";
+    case TokStatus::MarkingOverflow: return "tokenizer: text too long after marking special runs";
+    case TokStatus::SegmentOverflow: return "tokenizer: segmentation ran out of room";
+    default: return "";
+    }
+}
+
+void put_status(TokStatus s, char *error, size_t cap) {
+    if (s != TokStatus::Ok && error && cap) snprintf(error, cap, "%s", status_text(s));
+}
+
+// A whole file mapped read-only; unmapped with the object.
+class MappedFile {
+  public:
+    MappedFile() = default;
+    MappedFile(const MappedFile &) = delete;
+    MappedFile &operator=(const MappedFile &) = delete;
+    ~MappedFile() {
+        if (data_) munmap(const_cast<char *>(data_), size_);
+    }
+    bool map(const char *path) {
+        if (!path) return false;
+        const int fd = open(path, O_RDONLY | O_CLOEXEC);
+        if (fd < 0) return false;
+        struct stat st;
+        void *m = MAP_FAILED;
+        if (fstat(fd, &st) == 0 && st.st_size > 0)
+            m = mmap(nullptr, static_cast<size_t>(st.st_size), PROT_READ, MAP_PRIVATE, fd, 0);
+        close(fd);
+        if (m == MAP_FAILED) return false;
+        data_ = static_cast<const char *>(m);
+        size_ = static_cast<size_t>(st.st_size);
+        return true;
+    }
+    const char *begin() const { return data_; }
+    const char *end() const { return data_ + size_; }
+
+  private:
+    const char *data_ = nullptr;
+    size_t size_ = 0;
+};
 
 }  // namespace
 
 struct plamo_tokenizer {
-    const char *vocab = nullptr;
-    size_t vocab_bytes = 0;
+    MappedFile file;
     std::vector<plamo_trie_node> nodes;
-    std::vector<uint32_t> roots;
+    std::vector<uint32_t> first_scalar;  // direct index of the trie's first level
     plamo_trie trie{};
     uint32_t byte_ids[256] = {};
-    std::vector<const char *> rows;  // row starts, plus the end
-    // Per-request workspace, reused.
-    std::vector<uint32_t> scratch, input, temp, marked, ids;
+    std::vector<const char *> row_start;  // PLAMO_VOCAB_ROWS starts, then the end of the last row
+    // Request buffers.
+    std::vector<uint32_t> scalars, text, special, marked, ids;
     std::vector<uint8_t> flags;
     std::vector<int64_t> costs;
     std::vector<plamo_unigram_path> paths;
     std::vector<plamo_candidate> candidates;
-    std::vector<char> prompt, decoded;
+    std::vector<char> wrapped, piece;
 
-    ~plamo_tokenizer() {
-        if (vocab) munmap(const_cast<char *>(vocab), vocab_bytes);
-    }
+    TokStatus load(const char *path);
+    TokStatus index_rows();
+    TokStatus scalars_of(const char *utf8, uint64_t *count);
+    TokStatus encode(const char *utf8, unsigned direction, uint64_t *count);
 };
+
+TokStatus plamo_tokenizer::load(const char *path) {
+    if (!file.map(path)) return TokStatus::Unreadable;
+    try {
+        nodes.assign(kTrieNodes, plamo_trie_node{});
+        first_scalar.assign(kScalarLimit, 0);
+        scalars.resize(kMaxScalars);
+        text.resize(kMaxScalars);
+        special.resize(kTempCapacity);
+        marked.resize(kMarkedCapacity);
+        ids.resize(kMaxIds);
+        flags.resize(kTempCapacity + 1);
+        costs.resize(kMarkedCapacity + 1);
+        paths.resize(kMarkedCapacity);
+        candidates.resize(kCandidates);
+        wrapped.resize(kTextBytes);
+        piece.resize(kTextBytes);
+        row_start.reserve(PLAMO_VOCAB_ROWS + 2);
+    } catch (const std::bad_alloc &) {
+        return TokStatus::NoMemory;
+    }
+    trie = plamo_trie{nodes.data(), kTrieNodes, 1, first_scalar.data()};
+    if (plamo_vocab_load(file.begin(), file.end(), &trie, scalars.data(), kMaxScalars, byte_ids) != PLAMO_VOCAB_ROWS)
+        return TokStatus::BadRows;
+    return index_rows();
+}
+
+// Row i spans [row_start[i], row_start[i + 1]); a final row may lack its
+// line break.
+TokStatus plamo_tokenizer::index_rows() {
+    const char *p = file.begin(), *end = file.end();
+    row_start.push_back(p);
+    while (p < end && row_start.size() <= PLAMO_VOCAB_ROWS) {
+        const void *nl = memchr(p, '\n', static_cast<size_t>(end - p));
+        if (!nl) break;
+        p = static_cast<const char *>(nl) + 1;
+        row_start.push_back(p);
+    }
+    if (row_start.back() != end) row_start.push_back(end);
+    return row_start.size() == PLAMO_VOCAB_ROWS + 1 ? TokStatus::Ok : TokStatus::BadLineBreaks;
+}
+
+TokStatus plamo_tokenizer::scalars_of(const char *utf8, uint64_t *count) {
+    const char *end = utf8 + strlen(utf8);
+    uint64_t n = 0;
+    for (const char *p = utf8; p < end; ++n) {
+        plamo_scalar sc;
+        if (n == kMaxScalars || !plamo_utf8_next(p, end, &sc)) return TokStatus::BadText;
+        text[n] = static_cast<uint32_t>(sc.cp);
+        p = sc.next;
+    }
+    *count = n;
+    return TokStatus::Ok;
+}
+
+// Direction 1 wraps the text for English -> Japanese, 2 for Japanese ->
+// English, 0 encodes it as given; then scalars, special/repeat marking and
+// the Unigram segmentation.
+TokStatus plamo_tokenizer::encode(const char *utf8, unsigned direction, uint64_t *count) {
+    if (direction > 2) return TokStatus::BadDirection;
+    const char *source = utf8;
+    if (direction != 0) {
+        const char *from = direction == 1 ? "en" : "ja", *to = direction == 1 ? "ja" : "en";
+        if (plamo_translation_prompt(utf8, from, to, wrapped.data(), wrapped.size()) == kFail)
+            return TokStatus::PromptTooLong;
+        source = wrapped.data();
+    }
+    uint64_t n = 0;
+    if (const TokStatus st = scalars_of(source, &n); st != TokStatus::Ok) return st;
+    const plamo_preprocess_args marking{text.data(),    n,        special.data(), kTempCapacity,
+                                        marked.data(), kMarkedCapacity, flags.data()};
+    const uint64_t width = plamo_preprocess(&marking);
+    if (width == kFail) return TokStatus::MarkingOverflow;
+    const plamo_encoder seg{&trie,        marked.data(),     width,       byte_ids, costs.data(),
+                            paths.data(), candidates.data(), kCandidates, ids.data(), kMaxIds};
+    const uint64_t produced = plamo_encode_marked(&seg);
+    if (produced == kFail) return TokStatus::SegmentOverflow;
+    *count = produced;
+    return TokStatus::Ok;
+}
 
 extern "C" {
 
 struct plamo_tokenizer *plamo_tokenizer_open(const char *path, char *error, size_t cap) {
-    auto fail = [&](plamo_tokenizer *t, const char *why) -> plamo_tokenizer * {
-        if (error && cap) snprintf(error, cap, "%s", why);
-        delete t;
+    std::unique_ptr<plamo_tokenizer> t(new (std::nothrow) plamo_tokenizer());
+    const TokStatus st = t ? t->load(path) : TokStatus::NoMemory;
+    if (st != TokStatus::Ok) {
+        put_status(st, error, cap);
         return nullptr;
-    };
-    auto *t = new (std::nothrow) plamo_tokenizer();
-    if (!t) return fail(nullptr, "cannot allocate tokenizer state");
-    const int fd = path ? open(path, O_RDONLY | O_CLOEXEC) : -1;
-    struct stat st;
-    if (fd < 0 || fstat(fd, &st) != 0 || st.st_size <= 0) {
-        if (fd >= 0) close(fd);
-        return fail(t, "tokenizer is missing");
     }
-    void *map = mmap(nullptr, static_cast<size_t>(st.st_size), PROT_READ, MAP_PRIVATE, fd, 0);
-    close(fd);
-    if (map == MAP_FAILED) return fail(t, "cannot map tokenizer");
-    t->vocab = static_cast<const char *>(map);
-    t->vocab_bytes = static_cast<size_t>(st.st_size);
-    try {
-        t->nodes.assign(kTrieNodes, plamo_trie_node{});
-        t->roots.assign(kScalarLimit, 0);
-        t->scratch.resize(kMaxScalars);
-        t->input.resize(kMaxScalars);
-        t->temp.resize(kTempCapacity);
-        t->marked.resize(kMarkedCapacity);
-        t->ids.resize(kMaxIds);
-        t->flags.resize(kTempCapacity + 1);
-        t->costs.resize(kMarkedCapacity + 1);
-        t->paths.resize(kMarkedCapacity);
-        t->candidates.resize(kCandidates);
-        t->prompt.resize(kTextBytes);
-        t->decoded.resize(kTextBytes);
-        t->rows.reserve(PLAMO_VOCAB_ROWS + 1);
-    } catch (const std::bad_alloc &) {
-        return fail(t, "cannot allocate vocabulary trie");
-    }
-    t->trie = plamo_trie{t->nodes.data(), kTrieNodes, 1, t->roots.data()};
-    const char *end = t->vocab + t->vocab_bytes;
-    if (plamo_vocab_load(t->vocab, end, &t->trie, t->scratch.data(), kMaxScalars, t->byte_ids) != PLAMO_VOCAB_ROWS)
-        return fail(t, "vocabulary must contain 107520 valid rows");
-    // Row starts, so decoding a token does not rescan the file.
-    t->rows.push_back(t->vocab);
-    for (const char *p = t->vocab; p < end && t->rows.size() <= PLAMO_VOCAB_ROWS; ++p)
-        if (*p == '\n') t->rows.push_back(p + 1);
-    if (t->rows.size() == PLAMO_VOCAB_ROWS && end[-1] != '\n') t->rows.push_back(end);
-    if (t->rows.size() != PLAMO_VOCAB_ROWS + 1) return fail(t, "invalid vocabulary row boundaries");
-    return t;
+    return t.release();
 }
 
 void plamo_tokenizer_close(struct plamo_tokenizer *t) { delete t; }
 
 uint64_t plamo_tokenizer_encode(struct plamo_tokenizer *t, const char *text, unsigned direction,
                                 const uint32_t **ids, char *error, size_t cap) {
-    auto fail = [&](const char *why) {
-        if (error && cap) snprintf(error, cap, "%s", why);
-        return kFail;
-    };
-    if (!t || !text || !ids) return fail("invalid arguments");
-    if (direction > 2) return fail("unsupported translation direction");
-    const char *input = text;
-    if (direction) {
-        const bool to_japanese = direction == 1;
-        if (plamo_translation_prompt(text, to_japanese ? "en" : "ja", to_japanese ? "ja" : "en", t->prompt.data(),
-                                     t->prompt.size()) == kFail)
-            return fail("translation prompt exceeds the byte capacity");
-        input = t->prompt.data();
-    }
-    const char *end = input + strlen(input);
     uint64_t n = 0;
-    for (const char *p = input; p < end;) {
-        plamo_scalar s;
-        if (n == kMaxScalars || !plamo_utf8_next(p, end, &s))
-            return fail("prompt exceeds 4096 Unicode scalars or is not valid UTF-8");
-        t->input[n++] = static_cast<uint32_t>(s.cp);
-        p = s.next;
+    const TokStatus st = (!t || !text || !ids) ? TokStatus::BadArguments : t->encode(text, direction, &n);
+    if (st != TokStatus::Ok) {
+        put_status(st, error, cap);
+        return kFail;
     }
-    const plamo_preprocess_args pre{t->input.data(), n,      t->temp.data(), kTempCapacity, t->marked.data(),
-                                    kMarkedCapacity, t->flags.data()};
-    const uint64_t marked = plamo_preprocess(&pre);
-    if (marked == kFail) return fail("tokenizer preprocessing failed");
-    const plamo_encoder enc{&t->trie,       t->marked.data(),     marked, t->byte_ids, t->costs.data(),
-                            t->paths.data(), t->candidates.data(), kCandidates, t->ids.data(), kMaxIds};
-    const uint64_t count = plamo_encode_marked(&enc);
-    if (count == kFail) return fail("tokenizer encoding failed");
     *ids = t->ids.data();
-    return count;
+    return n;
 }
 
 uint64_t plamo_tokenizer_prefix(struct plamo_tokenizer *t, unsigned direction, const uint32_t **ids, char *error,
                                 size_t cap) {
-    if (!t || direction > 1 ||
-        plamo_translation_prefix(direction ? "ja" : "en", t->prompt.data(), t->prompt.size()) == kFail)
+    // The template's fixed head up to the source language (0: English source,
+    // 1: Japanese source), encoded as plain text.
+    if (!t || !ids || direction > 1) return kFail;
+    if (plamo_translation_prefix(direction == 0 ? "en" : "ja", t->wrapped.data(), t->wrapped.size()) == kFail)
         return kFail;
-    // Encoding raw text (direction 0) leaves the prompt buffer alone.
-    return plamo_tokenizer_encode(t, t->prompt.data(), 0, ids, error, cap);
+    uint64_t n = 0;
+    const TokStatus st = t->encode(t->wrapped.data(), 0, &n);
+    if (st != TokStatus::Ok) {
+        put_status(st, error, cap);
+        return kFail;
+    }
+    *ids = t->ids.data();
+    return n;
 }
 
 uint64_t plamo_tokenizer_decode(struct plamo_tokenizer *t, uint32_t id, const char **bytes) {
     if (!t || id >= PLAMO_VOCAB_ROWS) return kFail;
-    const uint64_t n = plamo_decode_token(t->rows[id], t->rows[id + 1], 0, t->decoded.data(), t->decoded.size(),
-                                          t->scratch.data(), t->scratch.size());
-    if (n != kFail && bytes) *bytes = t->decoded.data();
+    const uint64_t n = plamo_decode_token(t->row_start[id], t->row_start[id + 1], 0, t->piece.data(), t->piece.size(),
+                                          t->scalars.data(), t->scalars.size());
+    if (n != kFail && bytes) *bytes = t->piece.data();
     return n;
 }
 

@@ -131,7 +131,7 @@ def test_translation_directions_wrap_the_prompt_template(tokenizer):
 
 
 def test_invalid_requests_fail_with_a_reason(tokenizer):
-    assert encode(tokenizer, "a", 3)[1] == "unsupported translation direction"
+    assert encode(tokenizer, "a", 3)[1] == "tokenizer: translation direction must be 0, 1 or 2"
     assert "UTF-8" in encode(tokenizer, b"\xff")[1]
     assert "4096" in encode(tokenizer, "a" * 4097)[1]
     assert encode(tokenizer, "")[0] == []
