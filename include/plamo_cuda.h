@@ -106,6 +106,10 @@ int plamo_cuda_mlp(struct plamo_cuda *, const struct mlp *, float *states, uint6
    reference's rotation cache holds them), state, normalized and logits of
    `model` into its host arrays, and set the host counters. */
 int plamo_cuda_sync_host(struct plamo_cuda *, struct model *);
+/* Copy only state, normalized and logits of the last step into the host
+   descriptors of `model` (what plamo_cuda_forward leaves there; the greedy
+   entry points leave them on the device). */
+int plamo_cuda_read_outputs(struct plamo_cuda *, struct model *);
 /* Free the device state prepared for `model` (KV, workspace, graph). */
 int plamo_cuda_release_model(struct plamo_cuda *, struct model *);
 /* Unregister and free every preloaded range inside [src, src+bytes) (weights
@@ -249,6 +253,23 @@ double plamo_cuda_time_gemm(struct plamo_cuda *, const float *x, const uint16_t 
 /* Kernels launched by the library since open (counts every launch and every
    kernel node of a launched graph). */
 uint64_t plamo_cuda_kernel_launches(const struct plamo_cuda *);
+/* How a decode step of `model` runs, preparing it if needed: "persistent" (one
+   launch per token: every projection, attention and the greedy choice in one
+   kernel with one CTA per SM) or "graph: <reason>" (one CUDA graph of
+   per-projection kernels, with the reason the one-launch step does not
+   apply). NULL when the model is not prepared. Valid until the next call. */
+const char *plamo_cuda_decode_path(struct plamo_cuda *, struct model *);
+/* One persistent decode step of `token` (as plamo_cuda_forward_greedy, the
+   step is committed) that also records device timestamps (ns, %globaltimer)
+   of CTA 0 into stamps: [0] kernel start; [1 + b] when its consumer warps
+   passed grid barrier b, b < B = 5 * layers + 1 (per layer: after qkv, after
+   attention, after o_proj, after gate_up, after down_proj; last: after the
+   head); [1 + B + p] when its producer warp issued the first weight chunk of
+   projection p, p < 4 * layers + 1 (qkv, o_proj, gate_up, down_proj per
+   layer, then the head). Returns the number of stamps, or -1 when the model
+   does not decode with the persistent step or capacity is too small. */
+double plamo_cuda_decode_trace(struct plamo_cuda *, struct model *, uint64_t token, uint64_t *stamps,
+                               uint64_t capacity);
 
 /* Synthetic BF16 weights generated on the device: value(i) =
    mean + std * z(seed, i), z = (sum of 12 hash bytes - 1530) / 256, rounded to

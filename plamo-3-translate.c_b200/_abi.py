@@ -159,6 +159,9 @@ SIGNATURES = {
     "plamo_cuda_time_decode": (c_double, [P, M, c_uint64]),
     "plamo_cuda_time_gemv": (c_double, [P, P, P, P, c_uint64, c_uint64, c_uint64]),
     "plamo_cuda_kernel_launches": (c_uint64, [P]),
+    "plamo_cuda_decode_path": (c_char_p, [P, M]),
+    "plamo_cuda_read_outputs": (c_int, [P, M]),
+    "plamo_cuda_decode_trace": (c_double, [P, M, c_uint64, P, c_uint64]),
     "plamo_cuda_preload_synthetic": (c_int, [P, P, c_uint64, c_uint64, ctypes.c_float,
                                              ctypes.c_float]),
     "plamo_cuda_fill_synthetic_bf16": (c_int, [P, P, c_uint64, c_uint64, ctypes.c_float,
