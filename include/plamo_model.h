@@ -21,6 +21,13 @@
 extern "C" {
 #endif
 
+/* The records are the reference's, under the reference's own include guards
+   (runtime/model.h: PLAMO_RUNTIME_MODEL_H, runtime/parallel.h:
+   PLAMO_PARALLEL_H): a translation unit that includes the reference's
+   headers first and this one after (an adapter such as
+   integration/metal_cuda.c) sees each record once. This header does not
+   define those guards itself. */
+#ifndef PLAMO_RUNTIME_MODEL_H
 /* Fused Q|K|V projection followed by per-head RMSNorm(+1) of Q and K.
    out = [(qh + 2*kh) * dim], Q heads, then K heads, then V heads. */
 struct qkv {
@@ -87,13 +94,6 @@ struct model {
     const uint16_t *head;
     float *logits;
 };
-/* Y[token, row] = W[row, :] . X[token, :], strides in FP32 elements. */
-struct plamo_matmul {
-    const uint16_t *weights;
-    const float *input;
-    float *output;
-    uint64_t rows, columns, tokens, input_stride, output_stride;
-};
 /* Checkpoint mapping and weight schema records (reference runtime/model.h:65-74). */
 struct plamo_mapping {
     void *base;
@@ -105,6 +105,16 @@ struct plamo_weight_spec {
     const uint64_t *shape;
     void **slot;
 };
+#endif
+#ifndef PLAMO_PARALLEL_H
+/* Y[token, row] = W[row, :] . X[token, :], strides in FP32 elements. */
+struct plamo_matmul {
+    const uint16_t *weights;
+    const float *input;
+    float *output;
+    uint64_t rows, columns, tokens, input_stride, output_stride;
+};
+#endif
 
 #ifdef __cplusplus
 #define PLAMO_STATIC_ASSERT static_assert
