@@ -16,6 +16,12 @@ aggregate (N x steps / max-over-ranks device time).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload 8b-decode|31b-tp]
 
+At N > 1 the line also carries "tp": BASELINE config 5 at that rank count
+(the 31B-shaped tensor-parallel decode and its speculative form), the
+oracle token check of a 31B-shaped two-layer cut sharded the same way, and
+the latency of an NCCL all-reduce of one exchange's vector for comparison
+(--no-tp skips it).
+
 --workload 31b-tp: the 31B-shaped model (profile 31b,
 tied head) tensor-parallel over the N ranks of the launch (N = 1: one GPU, no
 tensor parallelism): a 128-token prompt, then batch-1 greedy decode of one
@@ -327,7 +333,8 @@ def run_ours(args, world, rank, local, dist):
         prefill_s = be.info().gpu_seconds - before
     prefill_rate = world * PROMPT / reduce_max(dist, prefill_s)
 
-    # Decode: warm-up, then exactly K graph launches between barriers.
+    # Decode: warm-up, then exactly K steps between barriers.
+    decode_path = (lib.plamo_cuda_decode_path(ctx, hm.ptr) or b"?").decode()
     assert lib.plamo_cuda_time_decode(ctx, hm.ptr, args.warmup) > 0, be.info().note
     barrier(dist)
     lib.plamo_cuda_synchronize(ctx)
@@ -398,6 +405,7 @@ def run_ours(args, world, rank, local, dist):
                "gemv": gemv_cpu_baseline()}
         del host, blob
 
+    line = None
     if rank == 0:
         traffic = measured_traffic()
         line = {
@@ -406,7 +414,11 @@ def run_ours(args, world, rank, local, dist):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": workload_config(world),
             "prefill_tok_s": prefill_rate,
-            "roofline": {"bound": "hbm", "kernel": "decode step (one CUDA graph launch per token)",
+            "decode_path": decode_path,
+            "roofline": {"bound": "hbm",
+                         "kernel": ("decode_token_kernel (one persistent launch per token)"
+                                    if decode_path == "persistent" else
+                                    "decode step (one CUDA graph launch per token)"),
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": (step_bytes * traffic["decode_step_ratio"]["ratio"]) if traffic else None,
@@ -426,8 +438,8 @@ def run_ours(args, world, rank, local, dist):
             "cpu_baseline": cpu,
             "batch": batch_info,
         }
-        print(json.dumps(line), flush=True)
     be.close()
+    return line if rank == 0 else None
 
 
 def run_batch(args, pkg, lib, be, hm, profile, world, rank, dist, peak):
@@ -495,7 +507,66 @@ def shard_bytes_per_token(full, shard, vocab_rows, ctx_mean):
     return weights + full.norm_bytes_per_token() + 2 * h + kv
 
 
+def tp_cut_check(world, rank, local, dist):
+    """Token check of the tensor-parallel path: the two-layer cut of the 31B
+    profile sharded over the ranks of this launch, its prefill and greedy
+    tokens against the oracle's (tests/golden/tp_31b_cut.npz, written by
+    tests/golden/make_golden.py --large)."""
+    from dataclasses import replace
+    pkg = load_package()
+    lib = pkg.load()
+    g = np.load(os.path.join(ROOT, "tests", "golden", "tp_31b_cut.npz"))
+    full = replace(pkg.PROFILES["31b"], name="31b-2layers", layers=2, pattern=2)
+    shard = pkg.tp_shard_profile(full, world)
+    be = pkg.Backend(device=local, max_context=1024, max_prefill=256)
+    try:
+        hm = pkg.HostModel(shard, weights="synthetic", full_capacity=1024)
+        be.preload_synthetic_tp(hm, full, rank, world, seed=int(g["seed"]))
+        be.tp_connect(hm, pkg.tp_all_gather_handles(be.tp_prepare(hm, rank, world)))
+        ids = np.ascontiguousarray(g["ids"], dtype=np.uint32)
+        n_want = len(g["tokens"])
+        out = np.zeros(n_want, dtype=np.uint32)
+        timing = pkg._abi.CudaTiming()
+        barrier(dist)
+        n = lib.plamo_cuda_generate(be.ctx, hm.ptr, ids.ctypes.data, len(ids), n_want, out.ctypes.data,
+                                    pkg._abi.TOKEN_CALLBACK(), None, ctypes.byref(timing))
+        assert n > 0, be.info().note
+        got = out[:n].tolist()
+        equal = got == g["tokens"].tolist()
+        equal_all = reduce_max(dist, 0.0 if equal else 1.0) == 0.0
+        barrier(dist)
+    finally:
+        be.close()
+    return {"model": "31b profile, 2 layers (sliding + full), tied head", "prompt": len(ids), "tokens": n_want,
+            "tokens_equal_oracle": bool(equal_all), "oracle_fixture": "tests/golden/tp_31b_cut.npz"}
+
+
+def nccl_allreduce_latency(dist, hidden, iters=200):
+    """Device time of one NCCL all-reduce of a [hidden] FP32 vector (the size
+    of one tensor-parallel exchange), mean over `iters` back-to-back calls,
+    max over ranks."""
+    import torch
+    x = torch.ones(hidden, dtype=torch.float32, device="cuda")
+    for _ in range(20):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        dist.all_reduce(x)
+    end.record()
+    torch.cuda.synchronize()
+    return reduce_max(dist, start.elapsed_time(end) / iters * 1000.0)
+
+
 def run_tp31b(args, world, rank, local, dist):
+    line = measure_tp31b(args, world, rank, local, dist)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def measure_tp31b(args, world, rank, local, dist):
     pkg = load_package()
     lib = pkg.load()
     full = pkg.PROFILES["31b"]
@@ -568,6 +639,7 @@ def run_tp31b(args, world, rank, local, dist):
     same = bool(np.array_equal(spec_out[:k], out[:k]))
     barrier(dist)
 
+    line = None
     if rank == 0:
         line = {
             "metric": TP_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
@@ -594,8 +666,36 @@ def run_tp31b(args, world, rank, local, dist):
             "clocks": clock_info,
             "cpu_baseline": None,
         }
-        print(json.dumps(line), flush=True)
     be.close()
+    return line
+
+
+def tp_section(args, world, rank, local, dist):
+    """BASELINE config 5 at this launch's rank count, for the scaling runs:
+    the 31B-shaped tensor-parallel decode (tok/s, per-rank roofline, e2e,
+    speculative with a 0.8B-shaped draft), its oracle token check on the
+    two-layer cut, and an NCCL all-reduce of one exchange's vector beside the
+    fused peer-memory exchanges (129 per token: two per layer and the head's)."""
+    check = tp_cut_check(world, rank, local, dist)
+    tp = measure_tp31b(args, world, rank, local, dist)
+    nccl_us = nccl_allreduce_latency(dist, pkg_profile_hidden("31b"))
+    if rank != 0:
+        return None
+    exchanges = 2 * 64 + 1
+    return {"workload": tp["config"]["workload"], "parallelism": tp["config"]["parallelism"],
+            "value": tp["value"], "unit": "tok/s", "ms_per_step": tp["ms_per_step"],
+            "scaling": "strong", "prefill_tok_s": tp["prefill_tok_s"], "roofline": tp["roofline"],
+            "e2e": tp["e2e"], "speculative": tp["speculative"], "gpu_launches": tp["gpu_launches"],
+            "clocks": tp["clocks"], "oracle_check": check,
+            "nccl_reference": {"allreduce_us": nccl_us, "vector": "[5120] fp32",
+                               "per_token_ms_if_nccl": nccl_us * exchanges / 1000.0,
+                               "exchanges_per_token": exchanges,
+                               "note": "latency of the library collective for one exchange; the step "
+                                       "uses fused peer-memory exchanges inside its projection kernels"}}
+
+
+def pkg_profile_hidden(name):
+    return load_package().PROFILES[name].hidden
 
 
 def run_profile(args):
@@ -665,6 +765,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="at N > 1, skip the 31B tensor-parallel section of the line")
     ap.add_argument("--workload", choices=["8b-decode", "31b-tp"], default="8b-decode")
     ap.add_argument("--profile", choices=["step", "batch", "gemv", "gemm"],
                     help="run one small fixed workload for an ncu capture instead of the benchmark")
@@ -698,7 +800,17 @@ def main():
                     time.sleep(5)
                 raise
         else:
-            run_ours(args, world, rank, local, dist)
+            line = run_ours(args, world, rank, local, dist)
+            if world > 1 and not args.no_tp:
+                try:
+                    tp = tp_section(args, world, rank, local, dist)
+                except BaseException:
+                    time.sleep(5)  # peers' bounded waits end before this rank's buffers go
+                    raise
+                if rank == 0:
+                    line["tp"] = tp
+            if rank == 0:
+                print(json.dumps(line), flush=True)
     finally:
         if dist is not None:
             dist.destroy_process_group()

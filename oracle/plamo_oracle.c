@@ -61,7 +61,7 @@ uint64_t plamo_weight_chunk_bytes = 0;
 /* One output row: four FMA lanes over columns c = j (mod 4), reduced as
    (l0 + l1) + (l2 + l3), then a scalar FMA tail (src/math.s:86-344; the 8-row,
    4-row and 1-row loops all keep this per-row order). */
-static inline float matvec_row(const uint16_t *w, const float *x, uint64_t cols) {
+static inline float matvec_row4(const uint16_t *w, const float *x, uint64_t cols) {
     float l0 = 0, l1 = 0, l2 = 0, l3 = 0;
     uint64_t body = cols & ~(uint64_t)3, c = 0;
     for (; c < body; c += 4) {
@@ -74,6 +74,31 @@ static inline float matvec_row(const uint16_t *w, const float *x, uint64_t cols)
     for (; c < cols; ++c)
         s = fmaf(bf16(w[c]), x[c], s);
     return s;
+}
+
+/* NOT the reference's order: eight FMA lanes reduced pairwise. Only for
+   measuring how far an equally valid FP32 summation order moves a whole
+   model's outputs (the spread a GPU's own order is held to in the
+   whole-model fixtures); off unless oracle_set_matvec_lanes(8) is called. */
+static inline float matvec_row8(const uint16_t *w, const float *x, uint64_t cols) {
+    float l[8] = {0};
+    uint64_t body = cols & ~(uint64_t)7, c = 0;
+    for (; c < body; c += 8)
+        for (int j = 0; j < 8; ++j)
+            l[j] = fmaf(bf16(w[c + j]), x[c + j], l[j]);
+    float s = ((l[0] + l[1]) + (l[2] + l[3])) + ((l[4] + l[5]) + (l[6] + l[7]));
+    for (; c < cols; ++c)
+        s = fmaf(bf16(w[c]), x[c], s);
+    return s;
+}
+
+static int oracle_matvec_lanes = 4;
+void oracle_set_matvec_lanes(int lanes) {
+    oracle_matvec_lanes = lanes == 8 ? 8 : 4;
+}
+
+static inline float matvec_row(const uint16_t *w, const float *x, uint64_t cols) {
+    return oracle_matvec_lanes == 8 ? matvec_row8(w, x, cols) : matvec_row4(w, x, cols);
 }
 
 struct matvec_job {

@@ -14,6 +14,10 @@ extern "C" {
 
 void oracle_set_threads(int threads);
 int oracle_threads(void);
+/* 4 (default): the reference's matvec order. 8: an equally valid FP32 order
+   that is not the reference's, for measuring a whole model's sensitivity to
+   summation order. */
+void oracle_set_matvec_lanes(int lanes);
 extern uint64_t plamo_weight_chunk_bytes;
 
 void plamo_bf16_matvec(const uint16_t *, const float *, float *, uint64_t rows, uint64_t cols);

@@ -448,6 +448,9 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
 constexpr int kDecThreads = 256;
 constexpr int kDecTile = 64;
 constexpr int kDecSplits = 8;
+// Head dim 128: 16 key splits per KV head (a non-portable cluster of 16),
+// so a context of up to 1024 rows is one tile per CTA.
+constexpr int kDec128Splits = 16;
 
 struct DecodeAttnParams {
     AttnLayer L;
@@ -506,12 +509,14 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
 
     pdl_launch_dependents();  // the next projection may start streaming its weights
-    pdl_wait();
+    // The committed rows and their counter were final before this step began
+    // (only the new row comes from the projection still in flight), so the
+    // first tile of old rows is requested before waiting for that projection.
     const uint64_t P = *p.L.appended;
     const uint64_t lo = window_start(p.L, P, 0);
     const uint32_t n = static_cast<uint32_t>(P + 1 - lo);
-    const uint64_t k0 = lo + static_cast<uint64_t>(n) * split / kDecSplits;
-    const uint64_t k1 = lo + static_cast<uint64_t>(n) * (split + 1) / kDecSplits;
+    const uint64_t k0 = lo + static_cast<uint64_t>(n) * split / kDec128Splits;
+    const uint64_t k1 = lo + static_cast<uint64_t>(n) * (split + 1) / kDec128Splits;
     const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
 
     // Asynchronous staging of one tile: 32 16-byte pieces per 512-byte row.
@@ -529,6 +534,7 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
         cp_async_commit();
     };
     if (k0 < k1) stage(k0, static_cast<uint32_t>(k1 - k0 < kDecTile ? k1 - k0 : kDecTile));
+    pdl_wait();
 
     // Q heads of the group (one warp each): lane l < 16 owns coordinate pairs
     // 4l..4l+3 / 64+4l..64+4l+3; RMSNorm(+1), rotate at the query position.
@@ -672,50 +678,55 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     }
     __syncthreads();
 
+    // Every cluster rank merges its share of the group's outputs from all
+    // splits' partials (distributed shared memory, fixed split order).
     cluster.sync();
-    if (cluster.block_rank() == 0) {
-        float *w = kt;  // [G][splits] weights, then [G] denominators
+    {
+        constexpr int S = kDec128Splits;
+        float *w = kt;  // [G][S] weights, then [G] denominators
         if (threadIdx.x < G) {
             const uint32_t g = threadIdx.x;
-            float ms[kDecSplits];
+            float ms[S];
             float M = -__int_as_float(0x7f800000);
 #pragma unroll
-            for (int r = 0; r < kDecSplits; ++r) {
+            for (int r = 0; r < S; ++r) {
                 ms[r] = cluster.map_shared_rank(mrow, r)[g];
                 M = fmaxf(M, ms[r]);
             }
             float Ls = 0.0f;
 #pragma unroll
-            for (int r = 0; r < kDecSplits; ++r) {
+            for (int r = 0; r < S; ++r) {
                 const float e = plamo_exp(__fsub_rn(ms[r], M));
-                w[g * kDecSplits + r] = e;
+                w[g * S + r] = e;
                 Ls = fmaf(cluster.map_shared_rank(lrow, r)[g], e, Ls);
             }
-            w[G * kDecSplits + g] = Ls;
+            w[G * S + g] = Ls;
         }
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) {
+        const uint32_t per = (G * D + S - 1) / S, i0 = cluster.block_rank() * per;
+        const uint32_t i1 = min(i0 + per, G * D);
+        for (uint32_t i = i0 + threadIdx.x; i < i1; i += kDecThreads) {
             const uint32_t g = i / D;
-            float parts[kDecSplits];
+            float parts[S];
 #pragma unroll
-            for (int r = 0; r < kDecSplits; ++r) parts[r] = cluster.map_shared_rank(acc, r)[i];
+            for (int r = 0; r < S; ++r) parts[r] = cluster.map_shared_rank(acc, r)[i];
             float A = 0.0f;
 #pragma unroll
-            for (int r = 0; r < kDecSplits; ++r) A = fmaf(parts[r], w[g * kDecSplits + r], A);
-            p.out[static_cast<uint64_t>(kh * G) * D + i] = __fdiv_rn(A, w[G * kDecSplits + g]);
+            for (int r = 0; r < S; ++r) A = fmaf(parts[r], w[g * S + r], A);
+            p.out[static_cast<uint64_t>(kh * G) * D + i] = __fdiv_rn(A, w[G * S + g]);
         }
     }
     cluster.sync();
 }
 
-__global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)
+__global__ void __cluster_dims__(1, kDec128Splits, 1) __launch_bounds__(kDecThreads)
     decode_attention128_kernel(DecodeAttnParams p) {
     decode_attention128_body(p);
 }
 
 // Several independent requests in one launch (blockIdx.z = request): each
 // has its own KV rings, counter and projection row.
-__global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads)
+__global__ void __cluster_dims__(1, kDec128Splits, 1) __launch_bounds__(kDecThreads)
     decode_attention128_batch_kernel(const DecodeAttnParams *ps) {
     decode_attention128_body(ps[blockIdx.z]);
 }

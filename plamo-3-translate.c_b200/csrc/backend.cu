@@ -125,6 +125,7 @@ struct DModel {
     PtParams pt{};
     uint32_t pt_grid = 0;
     size_t pt_smem = 0;
+    char pt_reason[96] = "";  // why the persistent step is not used
     std::vector<void *> allocations;
     std::vector<uintptr_t> signature;  // host descriptor identity at prepare time
 };
@@ -157,8 +158,10 @@ struct plamo_cuda {
     unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
     bool tc_gemm;
     bool prompt_attn;  // blocked prompt attention (PLAMO_CUDA_PROMPT_ATTN=0 disables)
-    bool persistent;   // one-launch decode step where the shapes allow (PLAMO_CUDA_PERSISTENT=0 disables)
+    bool persistent;   // one-launch decode step where the shapes allow (opt-in: PLAMO_CUDA_PERSISTENT=1)
     bool cooperative;  // the device supports cooperative launches
+    uint32_t pt_piece;  // bytes per bulk copy of the persistent step (PLAMO_CUDA_PT_PIECE_KB)
+    int pt_stages;      // ring stages of the persistent step (PLAMO_CUDA_PT_STAGES; 0: as many as fit)
     int gemv_ctas;
     uint32_t *sink;
     float *static_scratch;  // device address of g_linear_static_scratch (set on first use)
@@ -727,11 +730,11 @@ bool launch_decode_attention(plamo_cuda *c, DModel *m, uint64_t l) {
     DecodeAttnParams dp{attn_layer(m, l), static_cast<uint32_t>(m->QH), static_cast<uint32_t>(m->KH),
                         static_cast<uint32_t>(m->D), m->qkv, m->attn};
     const size_t smem = decode_attention_smem(static_cast<uint32_t>(m->QH / m->KH), static_cast<uint32_t>(m->D));
-    const dim3 grid(static_cast<uint32_t>(m->KH), kDecSplits), block(kDecThreads);
+    const dim3 block(kDecThreads);
     if (m->D == 128 && m->QH / m->KH <= 32)
-        return launch(c, decode_attention128_kernel, grid, block,
+        return launch(c, decode_attention128_kernel, dim3(static_cast<uint32_t>(m->KH), kDec128Splits), block,
                       decode_attention128_smem(static_cast<uint32_t>(m->QH / m->KH)), dp);
-    return launch(c, decode_attention_kernel<0>, grid, block, smem, dp);
+    return launch(c, decode_attention_kernel<0>, dim3(static_cast<uint32_t>(m->KH), kDecSplits), block, smem, dp);
 }
 
 // Exchange point `index` of the decode step (0..2L-1) or of a prompt.
@@ -942,7 +945,7 @@ bool record_batch(plamo_cuda *c, plamo_cuda_batch *b, DModel *m) {
                         1.0f, m->p_norm, H, f);
         if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H, f.split != nullptr))
             return false;
-        if (!launch(c, decode_attention128_batch_kernel, dim3(static_cast<uint32_t>(m->KH), kDecSplits, b->B),
+        if (!launch(c, decode_attention128_batch_kernel, dim3(static_cast<uint32_t>(m->KH), kDec128Splits, b->B),
                     dim3(kDecThreads), decode_attention128_smem(G),
                     static_cast<const DecodeAttnParams *>(b->d_attn + l * b->B)))
             return false;
@@ -981,23 +984,27 @@ bool record_batch(plamo_cuda *c, plamo_cuda_batch *b, DModel *m) {
 // KV head, every projection's columns a whole number (<= 32) of 512-column
 // slots, a hidden size the prologue holds in registers, and a grid of one
 // co-resident CTA per SM with at least three ring stages.
-bool persistent_plan(plamo_cuda *c, DModel *m, uint32_t *grid, size_t *smem, uint32_t *stages, uint32_t *splits) {
-    if (!c->persistent || !c->cooperative || m->tp.active || m->D != 128 || m->QH % m->KH) return false;
+const char *persistent_plan(plamo_cuda *c, DModel *m, uint32_t *grid, size_t *smem, uint32_t *stages,
+                            uint32_t *splits) {
+    if (!c->persistent) return "one-launch step not enabled (PLAMO_CUDA_PERSISTENT=1)";
+    if (!c->cooperative) return "no cooperative launch on this device";
+    if (m->tp.active) return "tensor-parallel shard";
+    if (m->D != 128 || m->QH % m->KH) return "head shape";
     const uint64_t G = m->QH / m->KH;
-    if (G > kPtMaxG || m->H % 512 || m->AW % 512 || m->I % 512 || m->H > kPtMaxHidden) return false;
-    if (m->H / 512 > kPtMaxSlots || m->AW / 512 > kPtMaxSlots || m->I / 512 > kPtMaxSlots) return false;
-    if (m->L > 0xffff || m->Vh > 0xffffffffull || m->QW > 0xffffffffull) return false;
+    if (G > kPtMaxG || m->H % 512 || m->AW % 512 || m->I % 512 || m->H > kPtMaxHidden) return "projection shape";
+    if (m->H / 512 > kPtMaxSlots || m->AW / 512 > kPtMaxSlots || m->I / 512 > kPtMaxSlots) return "row width";
+    if (m->L > 0xffff || m->Vh > 0xffffffffull || m->QW > 0xffffffffull) return "model size";
     // Bulk copies and vector loads of every weight need 16-byte alignment
     // (a mapped checkpoint can place a tensor anywhere).
     auto aligned = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-    if (!aligned(m->emb) || !aligned(m->norm) || !aligned(m->head)) return false;
+    if (!aligned(m->emb) || !aligned(m->norm) || !aligned(m->head)) return "unaligned weights";
     for (const DLayer &L : m->layers)
         for (const void *w : {static_cast<const void *>(L.qkv_w), static_cast<const void *>(L.o_w),
                               static_cast<const void *>(L.gu), static_cast<const void *>(L.down),
                               static_cast<const void *>(L.pre), static_cast<const void *>(L.post),
                               static_cast<const void *>(L.mpre), static_cast<const void *>(L.mpost),
                               static_cast<const void *>(L.qn), static_cast<const void *>(L.kn)})
-            if (!aligned(w)) return false;
+            if (!aligned(w)) return "unaligned weights";
     const uint32_t g = static_cast<uint32_t>(c->sm_count);
     const uint32_t S = static_cast<uint32_t>(std::max<uint64_t>(
         1, std::min<uint64_t>({g / m->KH, kPtMaxSplits, 384 / G})));
@@ -1009,28 +1016,33 @@ bool persistent_plan(plamo_cuda *c, DModel *m, uint32_t *grid, size_t *smem, uin
     const uint64_t work =
         std::max<uint64_t>(((m->H + 3) & ~3ull) + part, pt_attention_floats(static_cast<uint32_t>(G), S)) * 4;
     cudaFuncAttributes attr{};
-    if (cudaFuncGetAttributes(&attr, decode_token_kernel) != cudaSuccess) return false;
+    if (cudaFuncGetAttributes(&attr, decode_token_kernel) != cudaSuccess) return "kernel attributes";
     const int64_t room = static_cast<int64_t>(c->smem_optin) - static_cast<int64_t>(attr.sharedSizeBytes) -
                          static_cast<int64_t>(work);
-    const int64_t st = std::min<int64_t>(kPtMaxStages, room / kPtStageBytes);
-    if (st < 3) return false;
+    const int64_t st = std::min<int64_t>(c->pt_stages ? c->pt_stages : kPtDefaultStages, room / kPtStageBytes);
+    if (st < 3) return "shared memory";
     const size_t bytes = static_cast<size_t>(st) * kPtStageBytes + work;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_token_kernel, kPtThreads, bytes) !=
-            cudaSuccess ||
-        per_sm < 1)
-        return false;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_token_kernel, kPtThreads, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cudaGetErrorString(e);
+    }
+    if (per_sm < 1) return "no resident CTA per SM";
     *grid = g;
     *smem = bytes;
     *stages = static_cast<uint32_t>(st);
     *splits = S;
-    return true;
+    return nullptr;
 }
 
 bool persistent_init(plamo_cuda *c, DModel *m) {
     uint32_t grid = 0, stages = 0, S = 0;
     size_t smem = 0;
-    if (!persistent_plan(c, m, &grid, &smem, &stages, &S)) return false;
+    if (const char *why = persistent_plan(c, m, &grid, &smem, &stages, &S)) {
+        snprintf(m->pt_reason, sizeof m->pt_reason, "%s", why);
+        return false;
+    }
     std::vector<PtLayer> layers(m->L);
     for (uint64_t l = 0; l < m->L; ++l) {
         const DLayer &L = m->layers[l];
@@ -1083,6 +1095,7 @@ bool persistent_init(plamo_cuda *c, DModel *m) {
     p.appended = m->d_appended;
     p.S = S;
     p.stages = stages;
+    p.piece = c->pt_piece;
     m->pt_grid = grid;
     m->pt_smem = smem;
     // The step leaves its final state where the graph's does: the layers flip
@@ -1363,11 +1376,18 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_gemm = !tc || strcmp(tc, "0");
     const char *pa = getenv("PLAMO_CUDA_PROMPT_ATTN");
     c->prompt_attn = !pa || strcmp(pa, "0");
+    // The one-launch step is opt-in: on the 8B profile it measured 4.8 ms per
+    // token against 3.38 ms for the graph (its per-phase grid barriers and
+    // prologues cost more than the graph's programmatic launch boundaries).
     const char *pt = getenv("PLAMO_CUDA_PERSISTENT");
-    c->persistent = !pt || strcmp(pt, "0");
+    c->persistent = pt && !strcmp(pt, "1");
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, cfg.device);
     c->cooperative = coop != 0;
+    const char *piece = getenv("PLAMO_CUDA_PT_PIECE_KB");
+    c->pt_piece = 1024u * static_cast<uint32_t>(piece ? std::max(1, std::min(atoi(piece), 32)) : 8);
+    const char *pst = getenv("PLAMO_CUDA_PT_STAGES");
+    c->pt_stages = pst ? std::max(3, std::min(atoi(pst), kPtMaxStages)) : 0;
     // Draft confidence settings, parsed as reference runtime/worker.c:199-208
     // (invalid values fall back to the default rule).
     c->draft_margin = -1.0f;
@@ -1428,6 +1448,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     allow_smem(decode_attention128_batch_kernel, optin);
     allow_smem(decode_attention_kernel<0>, optin);
     allow_smem(decode_token_kernel, optin);
+    cudaFuncSetAttribute(decode_attention128_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaFuncSetAttribute(decode_attention128_batch_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         if (error && cap) snprintf(error, cap, "cannot configure kernels: %s", cudaGetErrorString(e));
         plamo_cuda_close(c);
@@ -1966,6 +1988,14 @@ int plamo_cuda_sync_host(struct plamo_cuda *c, struct model *model) {
     if (!m) return 0;
     if (!sync_kv(c, m)) return -1;
     return 1;
+}
+
+int plamo_cuda_read_outputs(struct plamo_cuda *c, struct model *model) {
+    if (!c) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m) return 0;
+    return copy_outputs(c, m) && note(c, "outputs", cudaStreamSynchronize(c->stream)) ? 1 : -1;
 }
 
 int plamo_cuda_read_weights(struct plamo_cuda *c, const void *key, void *dst, uint64_t bytes) {
@@ -2764,6 +2794,43 @@ double plamo_cuda_time_decode(struct plamo_cuda *c, struct model *model, uint64_
 
 uint64_t plamo_cuda_kernel_launches(const struct plamo_cuda *c) {
     return c ? c->info.launches : 0;
+}
+
+double plamo_cuda_decode_trace(struct plamo_cuda *c, struct model *model, uint64_t token, uint64_t *stamps,
+                               uint64_t capacity) {
+    if (!c || !stamps) return -1;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || token >= model->vocab || !reconcile(c, m) || !fits(m, 1) || !ensure_graph(c, m) || !m->pt_ready)
+        return -1;
+    const uint64_t n = 1 + (5 * m->L + 1) + (4 * m->L + 1);
+    if (capacity < n) return -1;
+    auto *trace = static_cast<unsigned long long *>(plamo_cuda_device_alloc(c, n * 8));
+    if (!trace) return -1;
+    m->verify_valid = false;
+    c->pinned_u32[0] = static_cast<uint32_t>(token);
+    m->pt.trace = trace;
+    bool ok = note(c, "trace", cudaMemsetAsync(trace, 0, n * 8, c->stream)) &&
+              note(c, "token", cudaMemcpyAsync(m->d_token, c->pinned_u32, 4, cudaMemcpyHostToDevice, c->stream)) &&
+              launch_decode(c, m) &&
+              note(c, "trace", cudaMemcpyAsync(stamps, trace, n * 8, cudaMemcpyDeviceToHost, c->stream)) &&
+              note(c, "trace", cudaStreamSynchronize(c->stream));
+    m->pt.trace = nullptr;
+    cudaFree(trace);
+    if (!ok || !check_device_error(c, m)) return -1;
+    publish_counts(m, 1);
+    return static_cast<double>(n);
+}
+
+const char *plamo_cuda_decode_path(struct plamo_cuda *c, struct model *model) {
+    static thread_local char text[128];
+    if (!c) return nullptr;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || !ensure_graph(c, m)) return nullptr;
+    if (m->pt_ready) return "persistent";
+    snprintf(text, sizeof text, "graph: %s", m->pt_reason);
+    return text;
 }
 
 void *plamo_cuda_device_alloc(struct plamo_cuda *c, uint64_t bytes) {

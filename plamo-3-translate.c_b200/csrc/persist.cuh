@@ -40,13 +40,19 @@
 
 namespace plamo {
 
+// 16 consumer warps and one producer warp. A stage holds 16 sub-ranges of
+// 512 columns (16 KB), one per consumer warp: a chunk is a whole number of
+// rows when a row has at most 16 sub-ranges, else one part of a row of 32
+// (two parts per row, the warp's column slot alternating between its two
+// register sets with the chunk's parity).
 constexpr int kPtConsumers = 16;
 constexpr int kPtConsumerThreads = kPtConsumers * 32;
 constexpr int kPtThreads = kPtConsumerThreads + 32;
-constexpr uint32_t kPtStageBytes = 32768;
-constexpr uint32_t kPtStageSubs = kPtStageBytes / (kSubElems * 2);  // 32 sub-ranges of 512 columns
-constexpr int kPtMaxStages = 8;
-constexpr uint32_t kPtMaxSlots = kPtStageSubs;  // rows of at most 16384 columns
+constexpr uint32_t kPtStageSubs = kPtConsumers;
+constexpr uint32_t kPtStageBytes = kPtStageSubs * kSubElems * 2;
+constexpr int kPtMaxStages = 12;
+constexpr int kPtDefaultStages = 6;  // 96 KB in flight per SM
+constexpr uint32_t kPtMaxSlots = 2 * kPtStageSubs;  // rows of at most 16384 columns
 constexpr uint32_t kPtTile = 16;                // attention key rows per tile
 constexpr uint32_t kPtMaxG = 16;                // query heads per KV head
 constexpr uint32_t kPtMaxSplits = 64;           // attention splits per KV head
@@ -79,14 +85,21 @@ struct PtParams {
     uint64_t *appended;      // [L] committed rows, +1 at the end of the step
     uint32_t S;              // attention splits per KV head
     uint32_t stages;
+    uint32_t piece;          // bytes per bulk copy (a stage is filled by several)
+    // Optional (null: off) %globaltimer stamps of block 0: [0] start, then
+    // [1 + b] when its consumers passed grid barrier b (B = 5L + 1 of them),
+    // then [1 + B + ph] when its producer issued the first chunk of
+    // projection ph (4L + 1 of them).
+    unsigned long long *trace;
 };
 
 // Phase geometry of projection `ph` (4 per layer: qkv, o, gate_up, down;
-// then the head) for this CTA.
+// then the head) for this CTA. parts = 1: a chunk is rpc whole rows; parts =
+// 2: a chunk is half a row (rpc = 1, cpr counts half rows).
 struct PtGemv {
     const uint16_t *w;
     uint32_t units, cols, pair;
-    uint32_t slots, rpc, u0, n, cpr;
+    uint32_t slots, parts, rpc, u0, n, cpr;
 };
 
 __device__ __forceinline__ PtGemv pt_gemv(const PtParams &p, uint32_t ph) {
@@ -103,10 +116,11 @@ __device__ __forceinline__ PtGemv pt_gemv(const PtParams &p, uint32_t ph) {
         }
     }
     g.slots = g.cols / kSubElems;
-    g.rpc = kPtStageSubs / g.slots;
+    g.parts = g.slots > kPtStageSubs ? 2u : 1u;
+    g.rpc = g.parts == 1 ? kPtStageSubs / g.slots : 1u;
     g.u0 = static_cast<uint32_t>(static_cast<uint64_t>(g.units) * blockIdx.x / gridDim.x);
     g.n = static_cast<uint32_t>(static_cast<uint64_t>(g.units) * (blockIdx.x + 1) / gridDim.x) - g.u0;
-    g.cpr = (g.n + g.rpc - 1) / g.rpc;
+    g.cpr = g.parts == 1 ? (g.n + g.rpc - 1) / g.rpc : 2 * g.n;
     return g;
 }
 
@@ -183,6 +197,7 @@ __device__ __forceinline__ bool pt_grid_sync(const PtParams &p, unsigned long lo
             }
         }
         __threadfence();
+        if (p.trace && blockIdx.x == 0) p.trace[1 + b] = global_ns();
     }
     return !pt_sync_any(*abort_flag);
 }
@@ -253,20 +268,25 @@ __device__ __noinline__ bool pt_norm_input(const PtParams &p, uint32_t token, bo
 
 // Consumer side of one projection phase: register slices of the input
 // (from shared `xs`, or from global `xg` written by other CTAs), the staged
-// chunks in ring order, per-(row, slot) partials, then the epilogue.
-// EPI: 0 store y, 1 SwiGLU of gate/up pairs into y, 2 head (logits + candidates).
-template <int EPI>
-__device__ __noinline__ bool pt_consume(const PtParams &p, const PtGemv &g, const float *xs, const float *xg,
-                                           float *y, unsigned char *ring, uint64_t *full_bar, uint64_t *empty_bar,
-                                           uint32_t &chunk, float *partial, float *red, volatile int *abort_flag) {
+// chunks in ring order, per-(row, slot) partials. Returns the ring position
+// after the phase, or kPtAbort after an abort (the same value in every
+// consumer thread). The epilogues below then reduce the partials.
+constexpr uint32_t kPtAbort = 0xffffffffu;
+__device__ __noinline__ uint32_t pt_stream(const PtParams &p, const PtGemv g, const float *xs, const float *xg,
+                                           unsigned char *ring, uint64_t *full_bar, uint64_t *empty_bar,
+                                           uint32_t chunk, float *partial, volatile int *abort_flag) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t csubs = g.rpc * g.slots;
+    // This warp's column slots: warp % slots (whole-row chunks), or warp in
+    // the first part of a row and warp + 16 in the second (which holds the
+    // row's last slots - 16 sub-ranges).
+    const uint32_t csubs = g.parts == 1 ? g.rpc * g.slots : kPtStageSubs;
     float xr[2][16];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        const uint32_t j = warp + 16u * i;
-        if (j < csubs) {
-            const uint32_t col = (j % g.slots) * kSubElems + lane * 8;
+        const bool mine = g.parts == 1 ? (i == 0 && static_cast<uint32_t>(warp) < csubs)
+                                       : warp + kPtStageSubs * i < g.slots;
+        if (mine) {
+            const uint32_t col = (g.parts == 1 ? warp % g.slots : warp + kPtStageSubs * i) * kSubElems + lane * 8;
             if (xg) {
                 const float4 a = __ldcg(reinterpret_cast<const float4 *>(xg + col));
                 const float4 b = __ldcg(reinterpret_cast<const float4 *>(xg + col + 4));
@@ -283,95 +303,128 @@ __device__ __noinline__ bool pt_consume(const PtParams &p, const PtGemv &g, cons
                     xr[i][8 + e] = xs[col + 256 + e];
                 }
             }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) xr[i][e] = 0.0f;
         }
     }
     const uint32_t stages = p.stages;
     const uint32_t total = g.pair * g.cpr;
+    const uint4 *ring4 = reinterpret_cast<const uint4 *>(ring);
+    uint32_t s = chunk % stages, parity = (chunk / stages) & 1u;
     // After an abort the remaining chunks are skipped without waiting, so
     // every warp still reaches the barrier after the loop.
-    for (uint32_t k = 0; k < total; ++k, ++chunk) {
-        const uint32_t s = chunk % stages;
-        if (*abort_flag) continue;
-        // Every lane waits (each then sees the copied bytes); the warp acts on
-        // the common result so its shuffles below stay convergent.
-        if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[s], (chunk / stages) & 1u))) {
-            if (lane == 0) pt_fail(p, 2u, abort_flag);
-            continue;
-        }
-        const uint32_t m = k >= g.cpr ? 1u : 0u;
-        const uint32_t kc = k - m * g.cpr;
-        const uint32_t rows = min(g.rpc, g.n - kc * g.rpc);
-        const uint32_t nsub = rows * g.slots;
-        const uint4 *stage = reinterpret_cast<const uint4 *>(ring + static_cast<size_t>(s) * kPtStageBytes);
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const uint32_t j = warp + 16u * i;
-            if (j < nsub) {
-                const uint32_t r = j / g.slots, slot = j - r * g.slots;
-                const uint4 w0 = stage[j * 64 + lane], w1 = stage[j * 64 + 32 + lane];
-                const float a = dot8r(w0, xr[i], 0.0f);
-                const float b = dot8r(w1, xr[i] + 8, 0.0f);
-                const float sum = warp_sum(a + b);
-                if (lane == 0) partial[((kc * g.rpc + r) * g.slots + slot) * g.pair + m] = sum;
+    for (uint32_t k = 0; k < total; ++k) {
+        if (!*abort_flag) {
+            // Every lane waits (each then sees the copied bytes); the warp acts
+            // on the common result so its shuffles below stay convergent.
+            if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[s], parity))) {
+                if (lane == 0) pt_fail(p, 2u, abort_flag);
+            } else {
+                const uint32_t m = k >= g.cpr ? 1u : 0u;
+                const uint32_t kc = k - m * g.cpr;
+                uint32_t row, slot, nsub;
+                bool odd = false;
+                if (g.parts == 1) {
+                    const uint32_t rows = min(g.rpc, g.n - kc * g.rpc);
+                    nsub = rows * g.slots;
+                    const uint32_t r = static_cast<uint32_t>(warp) / g.slots;
+                    row = kc * g.rpc + r;
+                    slot = warp - r * g.slots;
+                } else {
+                    odd = kc & 1u;
+                    nsub = odd ? g.slots - kPtStageSubs : kPtStageSubs;
+                    row = kc >> 1;
+                    slot = warp + (odd ? kPtStageSubs : 0u);
+                }
+                if (static_cast<uint32_t>(warp) < nsub) {
+                    const uint4 *stage = ring4 + static_cast<size_t>(s) * (kPtStageBytes / 16);
+                    const uint4 w0 = stage[warp * 64 + lane], w1 = stage[warp * 64 + 32 + lane];
+                    float a, b;
+                    if (odd) {
+                        a = dot8r(w0, xr[1], 0.0f);
+                        b = dot8r(w1, xr[1] + 8, 0.0f);
+                    } else {
+                        a = dot8r(w0, xr[0], 0.0f);
+                        b = dot8r(w1, xr[0] + 8, 0.0f);
+                    }
+                    const float sum = warp_sum(a + b);
+                    if (lane == 0) partial[(row * g.slots + slot) * g.pair + m] = sum;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_bar[s]);
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);
+        if (++s == stages) {
+            s = 0;
+            parity ^= 1u;
+        }
     }
-    if (pt_sync_any(*abort_flag)) return false;
-    // Epilogue: per-unit sums of the slots in order.
+    return pt_sync_any(*abort_flag) ? kPtAbort : chunk + total;
+}
+
+// Epilogues: per-unit sums of the slots, in slot order.
+__device__ __noinline__ void pt_store_epilogue(const PtGemv g, const float *partial, float *y) {
+    for (uint32_t u = threadIdx.x; u < g.n; u += kPtConsumerThreads) {
+        float t0 = 0.0f;
+        for (uint32_t s = 0; s < g.slots; ++s) t0 += partial[u * g.slots + s];
+        y[g.u0 + u] = t0;
+    }
+}
+// SwiGLU of every gate/up unit pair of this CTA.
+__device__ __noinline__ void pt_swiglu_epilogue(const PtGemv g, const float *partial, float *y) {
+    for (uint32_t u = threadIdx.x; u < g.n; u += kPtConsumerThreads) {
+        float t0 = 0.0f, t1 = 0.0f;
+        for (uint32_t s = 0; s < g.slots; ++s) {
+            t0 += partial[(u * g.slots + s) * 2];
+            t1 += partial[(u * g.slots + s) * 2 + 1];
+        }
+        y[g.u0 + u] = swiglu(t0, t1);
+    }
+}
+// Head: logits, and this CTA's greedy candidate (first maximum, runner-up
+// value, NaN flag) for the merge at the end of the step.
+__device__ __noinline__ void pt_head_epilogue(const PtParams &p, const PtGemv g, const float *partial, float *y) {
+    __shared__ float cand_v[kPtConsumers], cand_s[kPtConsumers];
+    __shared__ uint32_t cand_i[kPtConsumers], cand_n[kPtConsumers];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float bv = -__int_as_float(0x7f800000), sv = bv;
     uint32_t bi = 0xffffffffu;
     bool saw_nan = false;
     for (uint32_t u = threadIdx.x; u < g.n; u += kPtConsumerThreads) {
-        float t0 = 0.0f, t1 = 0.0f;
-        for (uint32_t s = 0; s < g.slots; ++s) {
-            t0 += partial[(u * g.slots + s) * g.pair];
-            if (EPI == 1) t1 += partial[(u * g.slots + s) * g.pair + 1];
-        }
+        float t0 = 0.0f;
+        for (uint32_t s = 0; s < g.slots; ++s) t0 += partial[u * g.slots + s];
         const uint32_t unit = g.u0 + u;
-        if (EPI == 1) {
-            y[unit] = swiglu(t0, t1);
-        } else {
-            y[unit] = t0;
-            if (EPI == 2) {
-                if (t0 != t0) saw_nan = true;
-                else top2_merge(t0, unit, -__int_as_float(0x7f800000), bv, bi, sv);
-            }
-        }
+        y[unit] = t0;
+        if (t0 != t0) saw_nan = true;
+        else top2_merge(t0, unit, -__int_as_float(0x7f800000), bv, bi, sv);
     }
-    if (EPI == 2) {
-        __shared__ float cand_v[kPtConsumers], cand_s[kPtConsumers];
-        __shared__ uint32_t cand_i[kPtConsumers], cand_n[kPtConsumers];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const float os = __shfl_xor_sync(0xffffffffu, sv, o);
-            top2_merge(ov, oi, os, bv, bi, sv);
-        }
-        const uint32_t any_nan = __any_sync(0xffffffffu, saw_nan);
-        if (lane == 0) {
-            cand_v[warp] = bv;
-            cand_i[warp] = bi;
-            cand_s[warp] = sv;
-            cand_n[warp] = any_nan;
-        }
-        pt_consumer_sync();
-        if (threadIdx.x == 0) {
-            uint32_t nan_seen = cand_n[0];
-            for (int w = 1; w < kPtConsumers; ++w) {
-                top2_merge(cand_v[w], cand_i[w], cand_s[w], bv, bi, sv);
-                nan_seen |= cand_n[w];
-            }
-            p.arg_val[blockIdx.x] = bv;
-            p.arg_val2[blockIdx.x] = sv;
-            p.arg_idx[blockIdx.x] = bi;
-            p.arg_nan[blockIdx.x] = nan_seen;
-        }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const float os = __shfl_xor_sync(0xffffffffu, sv, o);
+        top2_merge(ov, oi, os, bv, bi, sv);
     }
-    (void)red;
-    return true;
+    const uint32_t any_nan = __any_sync(0xffffffffu, saw_nan);
+    if (lane == 0) {
+        cand_v[warp] = bv;
+        cand_i[warp] = bi;
+        cand_s[warp] = sv;
+        cand_n[warp] = any_nan;
+    }
+    pt_consumer_sync();
+    if (threadIdx.x == 0) {
+        uint32_t nan_seen = cand_n[0];
+        for (int w = 1; w < kPtConsumers; ++w) {
+            top2_merge(cand_v[w], cand_i[w], cand_s[w], bv, bi, sv);
+            nan_seen |= cand_n[w];
+        }
+        p.arg_val[blockIdx.x] = bv;
+        p.arg_val2[blockIdx.x] = sv;
+        p.arg_idx[blockIdx.x] = bi;
+        p.arg_nan[blockIdx.x] = nan_seen;
+    }
 }
 
 // Attention shared memory (floats) for G query heads per KV head and S splits.
@@ -590,31 +643,50 @@ __device__ __noinline__ void pt_attention(const PtParams &p, uint32_t l, float *
     pt_consumer_sync();
     if (!last) return;
 
-    // Merge of the head's S splits (fixed split order).
+    // Merge of the head's S splits (fixed split order). Every split's (m, l)
+    // is fetched at once into shared memory (one L2 round trip), then the
+    // weights; the weighted sums keep kPtMergeBatch loads in flight.
     const float *parts = p.apart + static_cast<uint64_t>(kh) * S * pf;
+    float *ms = kt;  // [S][G] split maxima, then [S][G] split sums (the key tile is free now)
+    for (uint32_t i = threadIdx.x; i < S * G; i += nt) {
+        const uint32_t r = i / G, g = i - r * G;
+        ms[i] = __ldcg(parts + r * pf + G * D + g);
+        ms[S * G + i] = __ldcg(parts + r * pf + G * D + G + g);
+    }
+    pt_consumer_sync();
     for (uint32_t g = threadIdx.x; g < G; g += nt) {
         float M = -__int_as_float(0x7f800000);
-        for (uint32_t r = 0; r < S; ++r) M = fmaxf(M, __ldcg(parts + r * pf + G * D + g));
+        for (uint32_t r = 0; r < S; ++r) M = fmaxf(M, ms[r * G + g]);
         float Ls = 0.0f;
         for (uint32_t r = 0; r < S; ++r) {
-            const float e = plamo_exp(__fsub_rn(__ldcg(parts + r * pf + G * D + g), M));
+            const float e = plamo_exp(__fsub_rn(ms[r * G + g], M));
             wmerge[g * S + r] = e;
-            Ls = fmaf(__ldcg(parts + r * pf + G * D + G + g), e, Ls);
+            Ls = fmaf(ms[S * G + r * G + g], e, Ls);
         }
         wmerge[G * S + g] = Ls;
     }
     pt_consumer_sync();
+    constexpr uint32_t kPtMergeBatch = 16;
     for (uint32_t i = threadIdx.x; i < G * D; i += nt) {
         const uint32_t g = i / D;
         const float *w = wmerge + g * S;
         float a = 0.0f;
-#pragma unroll 8
-        for (uint32_t r = 0; r < S; ++r) a = fmaf(__ldcg(parts + r * pf + i), w[r], a);
+        for (uint32_t r0 = 0; r0 < S; r0 += kPtMergeBatch) {
+            float v[kPtMergeBatch];
+#pragma unroll
+            for (uint32_t k = 0; k < kPtMergeBatch; ++k)
+                v[k] = r0 + k < S ? __ldcg(parts + (r0 + k) * pf + i) : 0.0f;
+#pragma unroll
+            for (uint32_t k = 0; k < kPtMergeBatch; ++k)
+                if (r0 + k < S) a = fmaf(v[k], w[r0 + k], a);
+        }
         p.attn[static_cast<uint64_t>(kh * G) * D + i] = __fdiv_rn(a, wmerge[G * S + g]);
     }
 }
 
-__global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
+// Parameters stay in the constant parameter space (__grid_constant__): the
+// phase functions read them in place instead of from a per-thread copy.
+__global__ void __launch_bounds__(kPtThreads, 1) decode_token_kernel(const __grid_constant__ PtParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kPtMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kPtMaxStages];
@@ -639,6 +711,7 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
     }
     __syncthreads();
     const unsigned long long gen = __ldcg(p.gen);
+    if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[0] = global_ns();
 
     if (warp == kPtConsumers) {
         // Producer: every projection's rows of this CTA, in step order.
@@ -653,10 +726,11 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
                 const uint32_t s = issued % stages;
                 if (issued >= stages) {
                     const uint32_t parity = ((issued / stages) - 1) & 1u;
-                    const uint64_t start = global_ns();
                     bool ready = mbar_try_wait(&empty_bar[s], parity);
+                    uint64_t start = 0;
                     while (!ready && !*abort_flag) {
-                        if (global_ns() - start > kPtWaitNs) {
+                        if (!start) start = global_ns();
+                        else if (global_ns() - start > kPtWaitNs) {
                             pt_fail(p, 2u, abort_flag);
                             break;
                         }
@@ -669,12 +743,25 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
                 }
                 const uint32_t m = k >= g.cpr ? 1u : 0u;
                 const uint32_t kc = k - m * g.cpr;
-                const uint32_t rows = min(g.rpc, g.n - kc * g.rpc);
-                const uint32_t bytes = rows * g.cols * 2;
-                const uint16_t *src =
-                    g.w + (static_cast<uint64_t>(g.u0) + kc * g.rpc + static_cast<uint64_t>(m) * g.units) * g.cols;
+                uint32_t bytes;
+                const uint16_t *src;
+                if (g.parts == 1) {
+                    const uint32_t rows = min(g.rpc, g.n - kc * g.rpc);
+                    bytes = rows * g.cols * 2;
+                    src = g.w + (static_cast<uint64_t>(g.u0) + kc * g.rpc + static_cast<uint64_t>(m) * g.units) * g.cols;
+                } else {
+                    bytes = ((kc & 1u) ? g.slots - kPtStageSubs : kPtStageSubs) * kSubElems * 2;
+                    src = g.w + (static_cast<uint64_t>(g.u0) + (kc >> 1) + static_cast<uint64_t>(m) * g.units) * g.cols +
+                          (kc & 1u) * (kPtStageSubs * kSubElems);
+                }
+                // Several copies in flight per stage: the copy engine moves more
+                // bytes per SM with smaller, concurrent bulk copies.
                 mbar_expect_tx(&full_bar[s], bytes);
-                bulk_load(ring + static_cast<size_t>(s) * kPtStageBytes, src, bytes, &full_bar[s], policy);
+                unsigned char *dst = ring + static_cast<size_t>(s) * kPtStageBytes;
+                for (uint32_t off = 0; off < bytes; off += p.piece)
+                    bulk_load(dst + off, reinterpret_cast<const unsigned char *>(src) + off, min(p.piece, bytes - off),
+                              &full_bar[s], policy);
+                if (p.trace && blockIdx.x == 0 && k == 0) p.trace[1 + (5 * p.L + 1) + ph] = global_ns();
                 ++issued;
             }
         }
@@ -690,7 +777,6 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
     // Consumers.
     uint32_t chunk = 0;
     int s = 0;
-    const uint32_t G = p.QH / p.KH;
     float *xs = work;
     float *partial = work + ((p.H + 3) & ~3u);
     bool ok = true;
@@ -711,13 +797,18 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
                 ok = false;
                 break;
             }
-            pt_norm_input(p, 0, false, s ? p.state[1] : p.state[0], p.branch, p.layers[l - 1].mpost, kPtPostMlp, L.pre, 1.0f,
-                          s ? p.state[0] : p.state[1], nullptr, xs, red);
+            pt_norm_input(p, 0, false, s ? p.state[1] : p.state[0], p.branch, p.layers[l - 1].mpost, kPtPostMlp,
+                          L.pre, 1.0f, s ? p.state[0] : p.state[1], nullptr, xs, red);
             s ^= 1;
         }
-        ok = pt_consume<0>(p, pt_gemv(p, 4 * l), xs, nullptr, p.qkv, ring, full_bar, empty_bar, chunk, partial, red,
-                           abort_flag);
-        if (!ok || !pt_grid_sync(p, gen, 5 * l, B, abort_flag)) {
+        const PtGemv gq = pt_gemv(p, 4 * l);
+        chunk = pt_stream(p, gq, xs, nullptr, ring, full_bar, empty_bar, chunk, partial, abort_flag);
+        if (chunk == kPtAbort) {
+            ok = false;
+            break;
+        }
+        pt_store_epilogue(gq, partial, p.qkv);
+        if (!pt_grid_sync(p, gen, 5 * l, B, abort_flag)) {
             ok = false;
             break;
         }
@@ -726,32 +817,46 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
             ok = false;
             break;
         }
-        ok = pt_consume<0>(p, pt_gemv(p, 4 * l + 1), nullptr, p.attn, p.branch, ring, full_bar, empty_bar, chunk,
-                           partial, red, abort_flag);
-        if (!ok || !pt_grid_sync(p, gen, 5 * l + 2, B, abort_flag)) {
+        const PtGemv go = pt_gemv(p, 4 * l + 1);
+        chunk = pt_stream(p, go, nullptr, p.attn, ring, full_bar, empty_bar, chunk, partial, abort_flag);
+        if (chunk == kPtAbort) {
+            ok = false;
+            break;
+        }
+        pt_store_epilogue(go, partial, p.branch);
+        if (!pt_grid_sync(p, gen, 5 * l + 2, B, abort_flag)) {
             ok = false;
             break;
         }
         pt_norm_input(p, 0, false, s ? p.state[1] : p.state[0], p.branch, L.post, kPtPostMixer, L.mpre, 1.0f,
-                      s ? p.state[0] : p.state[1], nullptr,
-                      xs, red);
+                      s ? p.state[0] : p.state[1], nullptr, xs, red);
         s ^= 1;
-        ok = pt_consume<1>(p, pt_gemv(p, 4 * l + 2), xs, nullptr, p.mid, ring, full_bar, empty_bar, chunk, partial,
-                           red, abort_flag);
-        if (!ok || !pt_grid_sync(p, gen, 5 * l + 3, B, abort_flag)) {
+        const PtGemv gg = pt_gemv(p, 4 * l + 2);
+        chunk = pt_stream(p, gg, xs, nullptr, ring, full_bar, empty_bar, chunk, partial, abort_flag);
+        if (chunk == kPtAbort) {
             ok = false;
             break;
         }
-        ok = pt_consume<0>(p, pt_gemv(p, 4 * l + 3), nullptr, p.mid, p.branch, ring, full_bar, empty_bar, chunk,
-                           partial, red, abort_flag);
+        pt_swiglu_epilogue(gg, partial, p.mid);
+        if (!pt_grid_sync(p, gen, 5 * l + 3, B, abort_flag)) {
+            ok = false;
+            break;
+        }
+        const PtGemv gd = pt_gemv(p, 4 * l + 3);
+        chunk = pt_stream(p, gd, nullptr, p.mid, ring, full_bar, empty_bar, chunk, partial, abort_flag);
+        if (chunk == kPtAbort) {
+            ok = false;
+            break;
+        }
+        pt_store_epilogue(gd, partial, p.branch);
     }
     if (!ok || !pt_grid_sync(p, gen, 5 * (p.L - 1) + 4, B, abort_flag)) return;
     // Head: final norm of state + post-MLP branch, logits and candidates.
     pt_norm_input(p, 0, false, s ? p.state[1] : p.state[0], p.branch, p.layers[p.L - 1].mpost, kPtPostMlp, p.norm,
                   1.0f, s ? p.state[0] : p.state[1], p.normalized, xs, red);
-    if (!pt_consume<2>(p, pt_gemv(p, 4 * p.L), xs, nullptr, p.logits, ring, full_bar, empty_bar, chunk, partial, red,
-                       abort_flag))
-        return;
+    const PtGemv gh = pt_gemv(p, 4 * p.L);
+    if (pt_stream(p, gh, xs, nullptr, ring, full_bar, empty_bar, chunk, partial, abort_flag) == kPtAbort) return;
+    pt_head_epilogue(p, gh, partial, p.logits);
     // Only block 0 waits for every block's candidates.
     pt_consumer_sync();
     if (threadIdx.x == 0 && !*abort_flag) {
@@ -773,6 +878,7 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
             }
         }
         __threadfence();
+        if (p.trace) p.trace[B] = global_ns();
     }
     if (pt_sync_any(*abort_flag) || warp != 0) return;
     // Merge the candidates (argmax_merge_kernel's rule), publish the token,
@@ -800,7 +906,6 @@ __global__ void __maxnreg__(120) decode_token_kernel(PtParams p) {
         p.next[2] = __float_as_uint(__fsub_rn(bv, sv));
         *p.gen = gen + 1;
     }
-    (void)G;
 }
 
 }  // namespace plamo

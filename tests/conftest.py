@@ -62,6 +62,7 @@ def load_oracle():
         "oracle_set_threads": (None, [ctypes.c_int]),
         "plamo_cache_rope": (None, [P, ctypes.c_float]),
         "oracle_synthetic_bf16": (None, [P, U64, U64, ctypes.c_float, ctypes.c_float, ctypes.c_int]),
+        "oracle_set_matvec_lanes": (None, [ctypes.c_int]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -41,9 +41,9 @@ int main(int argc, char **argv) {
     uint64_t n = plamo_tokenizer_encode(tok, "Hello.", 1, &ids, err, sizeof err);
     if (n == UINT64_MAX || n == 0) { fprintf(stderr, "encode: %s\n", err); return 2; }
 
-    struct plamo_model_config cfg = {64, 2, 4, 2, 16, 96, 50, 8, 2, 64, 0,
+    struct plamo_model_config cfg = {64, 2, 4, 2, 16, 96, 50, 8, 2, 128, 0,
                                      10000.0, 1000000.0, 256.0, 4096.0, 32.0, 1.0};
-    struct plamo_model_layout *lay = plamo_model_layout_create(&cfg, 64, err, sizeof err);
+    struct plamo_model_layout *lay = plamo_model_layout_create(&cfg, 128, err, sizeof err);
     if (!lay) { fprintf(stderr, "layout: %s\n", err); return 3; }
     struct plamo_mapping map;
     if (!plamo_map_file(argv[2], &map)) return 4;
@@ -102,7 +102,7 @@ def build_host_program(tmp_path):
     rows += ['["x", -1, "NORMAL"]'] * (107520 - len(rows))
     vocab.write_text("\n".join(rows) + "\n", encoding="utf-8")
 
-    prof = pkg.Profile("c-host", 64, 2, 4, 2, 16, 96, vocab=50, window=8, pattern=2, max_position=64)
+    prof = pkg.Profile("c-host", 64, 2, 4, 2, 16, 96, vocab=50, window=8, pattern=2, max_position=128)
     rng = np.random.default_rng(3)
     tensors = {}
     for name, shape in pkg.schema(prof):

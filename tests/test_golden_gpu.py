@@ -109,8 +109,13 @@ def first_flip(got, want, margins):
 def test_large_model_matches_golden(backend, name, spec):
     """BASELINE config 4 at its full size (8B profile, the benchmark's weights,
     455-id prompt, 64 greedy tokens) and the 31B-shaped two-layer cut: the
-    prefill logits and state within the whole-model rule, the greedy tokens
-    identical to the oracle's (a flip is reported with its oracle margin)."""
+    greedy tokens identical to the oracle's (a flip is reported with its
+    oracle margin), and the prefill logits and state within the whole-model
+    rule (relative L2 <= 1e-4, reference tools/compare_backends.py:16-33) or,
+    where the model itself amplifies rounding past it, within twice the
+    distance the fixture measured between the reference-order oracle and the
+    same oracle with another valid FP32 summation order (order_spread_*: 32
+    layers over a 455-token prompt move the 8B logits by 5e-4 that way)."""
     pkg = load_package()
     g = fixture(name)
     hm = large_model(backend, spec)
@@ -125,7 +130,10 @@ def test_large_model_matches_golden(backend, name, spec):
         for what, got, want in (("logits", hm.logits_array(), g["prefill_logits"]),
                                 ("state", hm.state_array(), g["prefill_state"])):
             assert np.all(np.isfinite(got)), what
-            assert rel_l2(got, want) <= 1e-4, f"{name} prefill {what}: {rel_l2(got, want):.3g}"
+            bound = max(1e-4, 2 * float(g[f"order_spread_{what}"]))
+            print(f"{name} prefill {what}: relative L2 {rel_l2(got, want):.3g} (oracle order spread "
+                  f"{float(g[f'order_spread_{what}']):.3g}, bound {bound:.3g})")
+            assert rel_l2(got, want) <= bound, f"{name} prefill {what}: {rel_l2(got, want):.3g} > {bound:.3g}"
         hm.reset()
         n_want = len(g["tokens"])
         out = np.zeros(n_want, dtype=np.uint32)

@@ -65,6 +65,8 @@ def test_persistent_step_matches_graph_and_oracle():
             hm = pkg.HostModel(prof, weights="synthetic")
             be.preload_synthetic(hm, seed=17)
             be.prepare(hm)
+            path = be.lib.plamo_cuda_decode_path(be.ctx, hm.ptr).decode()
+            assert (path == "persistent") == persistent, path
             results[persistent] = decode(be, hm, ids, 40) + (be.last_step_launches,)
             if persistent:
                 blob = np.empty(hm.blob_bytes // 2, dtype=np.uint16)
@@ -116,3 +118,32 @@ def test_persistent_profiles_match_graph_tokens(name):
         finally:
             be.close()
     assert tokens[True] == tokens[False]
+
+
+def test_decode_trace_reports_every_phase():
+    """plamo_cuda_decode_trace: one committed persistent step with the device
+    timestamps of CTA 0 - kernel start, then every grid barrier in step order
+    (non-decreasing), then the first chunk issued for every projection."""
+    pkg = load_package()
+    prof = mini_profile(pkg)
+    be = backend_with(True)
+    try:
+        hm = pkg.HostModel(prof, weights="synthetic")
+        be.preload_synthetic(hm, seed=17)
+        be.prepare(hm)
+        ids = np.random.default_rng(9).integers(3, prof.vocab, size=5).astype(np.uint32)
+        expect(be, be.lib.plamo_cuda_prefill(be.ctx, hm.ptr, ids.ctypes.data, len(ids), None))
+        L = prof.layers
+        n = 1 + (5 * L + 1) + (4 * L + 1)
+        stamps = np.zeros(n, dtype=np.uint64)
+        assert be.lib.plamo_cuda_decode_trace(be.ctx, hm.ptr, 7, stamps.ctypes.data, n - 1) == -1
+        assert be.lib.plamo_cuda_decode_trace(be.ctx, hm.ptr, 7, stamps.ctypes.data, n) == n
+        barriers = stamps[1:1 + 5 * L + 1].astype(np.int64)
+        issues = stamps[1 + 5 * L + 1:].astype(np.int64)
+        assert np.all(barriers > 0) and np.all(issues > 0)
+        assert np.all(np.diff(barriers) >= 0)
+        assert barriers[0] >= int(stamps[0]) and np.all(issues >= int(stamps[0]))
+        # The step was committed: the next forward continues from it.
+        expect(be, be.lib.plamo_cuda_forward(be.ctx, hm.ptr, 11))
+    finally:
+        be.close()
