@@ -481,7 +481,10 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
     const bool producer = warp == kBulkConsumers;
     const uint64_t policy = evict_first_policy();
     const uint64_t half_rows = p.rows / 2;
-    const uint16_t *range_base[2] = {p.w + u0 * cols, p.w + (u0 + half_rows) * cols};
+    // The CTA's rows (gate rows, then the matching up rows of a pair);
+    // selected, not indexed, so no local-memory array is formed.
+    const uint16_t *const range_gate = p.w + u0 * cols;
+    const uint16_t *const range_up = p.w + (u0 + half_rows) * cols;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -504,8 +507,9 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
         const uint32_t bytes = PART ? (left < csubs ? left : csubs) / slots * cols32 * 2
                                     : (left < csubs ? left : csubs) * kSubElems * 2;
         mbar_expect_tx(&full_bar[s], bytes);
-        const uint16_t *src = PART ? range_base[m] + static_cast<uint64_t>(kc) * rpc * cols
-                                   : range_base[m] + static_cast<uint64_t>(kc) * csubs * kSubElems;
+        const uint16_t *base = m ? range_up : range_gate;
+        const uint16_t *src = PART ? base + static_cast<uint64_t>(kc) * rpc * cols
+                                   : base + static_cast<uint64_t>(kc) * csubs * kSubElems;
         bulk_load(ring + static_cast<size_t>(s) * chunk_bytes, src, bytes, &full_bar[s], policy);
     };
     const uint32_t primed = total < static_cast<uint32_t>(stages) ? total : static_cast<uint32_t>(stages);

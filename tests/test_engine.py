@@ -97,8 +97,11 @@ int main(int argc, char **argv) {
 
 def write_vocab(path):
     rows = ['["unused", 0, "NORMAL"]'] + [f'["<0x{b:02X}>", 0, "BYTE"]' for b in range(256)]
-    rows += ['["Hello", -1.0, "NORMAL"]', '["<|plamo:op|>", 0, "CONTROL"]', '["<|plamo:msg|>", 0, "CONTROL"]',
-             '["translation", -2.0, "NORMAL"]']
+    # The template's special and word pieces, as the real vocabulary has them,
+    # so the fixed prefix is a dozen ids (the device snapshot holds at most 64).
+    rows += ['["Hello", -1.0, "NORMAL"]']
+    rows += [f'["<|plamo:{t}|>", 0, "CONTROL"]' for t in ("bos", "tag", "msg", "key", "val", "op")]
+    rows += [f'["{w}", -2.0, "NORMAL"]' for w in ("dataset", "translation", "input", "output", "lang", "en", "ja")]
     rows += [f'["w{i}", -3, "NORMAL"]' for i in range(107520 - len(rows))]
     path.write_text("\n".join(rows) + "\n", encoding="utf-8")
 
