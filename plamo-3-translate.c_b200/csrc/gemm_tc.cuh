@@ -4,9 +4,13 @@
 // activations. X is split once into BF16 terms hi = bf16(x), mid = bf16(x - hi),
 // lo = bf16(x - hi - mid), and every K step issues one tcgen05.mma per term into
 // the same FP32 accumulator in tensor memory. Products of BF16 pairs are exact
-// in FP32, so three terms carry x to about 24 significant bits, FP32 class (two
-// terms, 16 bits, left deviations beyond the reference's own GPU acceptance
-// bound on small fixtures). Replaces the reference's FP32 batched matvec
+// in FP32, so three terms carry x to about 24 significant bits, FP32 class.
+// Two terms (16 bits) were measured against three on B200: projections stay
+// within 1e-5 relative L2 (2.5e-6 against 6.5e-7) and the 455-token 8B prefill
+// is 13 % faster (gate_up 311 against 370 us), but the whole model drifts -
+// prefill logits 1.7e-3 from the oracle, 3.3 times the spread of two valid FP32
+// summation orders - and its 64 greedy tokens no longer match the oracle's,
+// so three terms stay (kTcTerms). Replaces the reference's FP32 batched matvec
 // (src/matmul*.s, runtime/kernels.metal:299-365).
 //
 // The tensor cores truncate while they accumulate, so error grows with the
@@ -50,7 +54,8 @@ template <int N>
 __host__ __device__ constexpr int tc_acc_count() {
     return N <= 16 ? 16 : N <= 32 ? 8 : N <= 64 ? 4 : 2;
 }
-constexpr int kTcTerms = 3;  // BF16 terms of each FP32 activation
+constexpr int kTcTerms = 3;  // BF16 terms of each FP32 activation (2 or 3: loads and MMAs follow it)
+static_assert(kTcTerms == 2 || kTcTerms == 3, "two or three BF16 terms");
 
 struct TcGemmParams {
     float *y;  // [T][ys]
@@ -205,7 +210,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_2d(st, &map_w, kx, static_cast<int>(row0), &full_bar[s]);
             tma_load_2d(st + kTcM * 128, &map_hi, kx, static_cast<int>(tok0), &full_bar[s]);
             tma_load_2d(st + kTcM * 128 + N * 128, &map_mid, kx, static_cast<int>(tok0), &full_bar[s]);
-            tma_load_2d(st + kTcM * 128 + 2 * N * 128, &map_lo, kx, static_cast<int>(tok0), &full_bar[s]);
+            if constexpr (kTcTerms == 3)
+                tma_load_2d(st + kTcM * 128 + 2 * N * 128, &map_lo, kx, static_cast<int>(tok0), &full_bar[s]);
             issued = kb + 1;
             if (++s == static_cast<uint32_t>(stages)) {
                 s = 0;
@@ -241,7 +247,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint64_t da = smem_desc_sw128(sa + 32 * k);
                 tc_mma(acc, da, smem_desc_sw128(bh + 32 * k), idesc, k ? 1u : 0u);
                 tc_mma(acc, da, smem_desc_sw128(bm + 32 * k), idesc, 1u);
-                tc_mma(acc, da, smem_desc_sw128(bl + 32 * k), idesc, 1u);
+                if constexpr (kTcTerms == 3) tc_mma(acc, da, smem_desc_sw128(bl + 32 * k), idesc, 1u);
             }
             tc_commit(&empty_bar[s]);   // the stage is free once these MMAs have read it
             tc_commit(&acc_full[a]);    // and the block's partial is ready
