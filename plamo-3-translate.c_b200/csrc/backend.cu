@@ -165,6 +165,8 @@ struct plamo_cuda {
     int gemv_ctas;
     uint32_t *sink;
     float *static_scratch;  // device address of g_linear_static_scratch (set on first use)
+    char *staging = nullptr;   // grow-only device staging of linear / mlp (host buffers in and out)
+    uint64_t staging_bytes = 0;
 };
 
 // A template-prefix snapshot (reference runtime/prompt_cache.c:5-13 keeps the
@@ -1467,6 +1469,7 @@ void plamo_cuda_close(struct plamo_cuda *c) {
     for (Range &r : c->ranges) cudaFree(r.dev);
     cudaFreeHost(c->pinned_u32);
     cudaFree(c->sink);
+    cudaFree(c->staging);
     cudaEventDestroy(c->ev0);
     cudaEventDestroy(c->ev1);
     cudaStreamDestroy(c->stream);
@@ -2136,6 +2139,58 @@ void plamo_cuda_reset_request(struct plamo_cuda *c, struct model *model) {
     }
 }
 
+}  // extern "C"
+
+namespace {
+
+// Device staging of the host-buffer entry points (linear, mlp): one
+// allocation per context, grown to the largest request seen and kept until
+// close, carved into 256-byte aligned pieces. The last 256 bytes hold the
+// projections' error flag.
+struct Staging {
+    char *base;
+    uint64_t used;
+    template <typename T>
+    T *take(uint64_t count) {
+        T *p = reinterpret_cast<T *>(base + used);
+        used += (std::max<uint64_t>(count, 1) * sizeof(T) + 255) & ~255ull;
+        return p;
+    }
+};
+bool staging(plamo_cuda *c, uint64_t bytes, Staging *out) {
+    bytes += 256;
+    if (bytes > c->staging_bytes) {
+        if (!note(c, "staging", cudaStreamSynchronize(c->stream))) return false;
+        cudaFree(c->staging);
+        c->staging = nullptr;
+        c->staging_bytes = 0;
+        if (!note(c, "staging alloc", cudaMalloc(&c->staging, bytes))) return false;
+        c->staging_bytes = bytes;
+        if (!note(c, "staging flag", cudaMemsetAsync(c->staging + bytes - 256, 0, 4, c->stream))) return false;
+    }
+    *out = Staging{c->staging, 0};
+    return true;
+}
+uint32_t *staging_error(plamo_cuda *c) {
+    return reinterpret_cast<uint32_t *>(c->staging + c->staging_bytes - 256);
+}
+uint64_t pad256(uint64_t bytes) { return (std::max<uint64_t>(bytes, 1) + 255) & ~255ull; }
+
+// Read back and clear the projections' error flag after a synchronised call.
+bool staging_ok(plamo_cuda *c) {
+    uint32_t err = 0;
+    if (!note(c, "staging flag", cudaMemcpy(&err, staging_error(c), 4, cudaMemcpyDeviceToHost))) return false;
+    if (!err) return true;
+    cudaMemset(staging_error(c), 0, 4);
+    c->info.errors++;
+    snprintf(c->info.note, sizeof c->info.note, "a tensor-core projection stalled for 2 s");
+    return false;
+}
+
+}  // namespace
+
+extern "C" {
+
 int plamo_cuda_linear(struct plamo_cuda *c, const struct plamo_matmul *mm) {
     if (!c || !mm) return 0;
     if (!mm->rows || !mm->tokens) return 1;
@@ -2145,22 +2200,18 @@ int plamo_cuda_linear(struct plamo_cuda *c, const struct plamo_matmul *mm) {
         c->info.declines++;
         return 0;
     }
-    float *x = nullptr, *y = nullptr;
     const uint64_t T = mm->tokens, K = mm->columns, R = mm->rows;
-    if (!note(c, "linear alloc", cudaMalloc(&x, std::max<uint64_t>(T * K, 1) * 4)) ||
-        !note(c, "linear alloc", cudaMalloc(&y, T * R * 4))) {
-        cudaFree(x);
-        return -1;
-    }
+    Staging st{};
+    if (!staging(c, pad256(T * K * 4) + pad256(T * R * 4) + pad256(3 * T * K * 2), &st)) return -1;
+    float *x = st.take<float>(T * K), *y = st.take<float>(T * R);
+    uint16_t *split = st.take<uint16_t>(3 * T * K);
     bool ok = !K || note(c, "linear in", cudaMemcpy2DAsync(x, K * 4, mm->input, mm->input_stride * 4, K * 4, T,
                                                           cudaMemcpyHostToDevice, c->stream));
     if (ok && !K) ok = note(c, "linear zero", cudaMemsetAsync(y, 0, T * R * 4, c->stream));
-    else if (ok) ok = gemm(c, x, K, w, y, R, T, R, K);
+    else if (ok) ok = projection_with(c, x, K, w, y, R, T, R, K, split, staging_error(c));
     ok = ok && note(c, "linear out", cudaMemcpy2DAsync(mm->output, mm->output_stride * 4, y, R * 4, R * 4, T,
                                                        cudaMemcpyDeviceToHost, c->stream)) &&
-         note(c, "linear", cudaStreamSynchronize(c->stream));
-    cudaFree(x);
-    cudaFree(y);
+         note(c, "linear", cudaStreamSynchronize(c->stream)) && staging_ok(c);
     return ok ? 1 : -1;
 }
 
@@ -2214,26 +2265,25 @@ int plamo_cuda_mlp(struct plamo_cuda *c, const struct mlp *p, float *states, uin
         c->info.declines++;
         return 0;
     }
-    float *s = nullptr, *n = nullptr, *g = nullptr, *b = nullptr;
-    bool ok = note(c, "mlp alloc", cudaMalloc(&s, tokens * H * 4)) && note(c, "mlp alloc", cudaMalloc(&n, tokens * H * 4)) &&
-              note(c, "mlp alloc", cudaMalloc(&g, tokens * 2 * I * 4)) &&
-              note(c, "mlp alloc", cudaMalloc(&b, tokens * H * 4));
-    ok = ok && note(c, "mlp in", cudaMemcpyAsync(s, states, tokens * H * 4, cudaMemcpyHostToDevice, c->stream));
-    ok = ok && launch(c, norm_rows_kernel<ROW_NORM>, dim3(tokens), dim3(512), 0, s, static_cast<const float *>(nullptr),
+    const uint64_t T = tokens, KM = std::max<uint64_t>(H, I);
+    Staging st{};
+    if (!staging(c, 3 * pad256(T * H * 4) + pad256(T * 2 * I * 4) + pad256(3 * T * KM * 2), &st)) return -1;
+    float *s = st.take<float>(T * H), *n = st.take<float>(T * H), *g = st.take<float>(T * 2 * I),
+          *b = st.take<float>(T * H);
+    uint16_t *split = st.take<uint16_t>(3 * T * KM);
+    uint32_t *err = staging_error(c);
+    bool ok = note(c, "mlp in", cudaMemcpyAsync(s, states, T * H * 4, cudaMemcpyHostToDevice, c->stream));
+    ok = ok && launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, s, static_cast<const float *>(nullptr),
                       static_cast<const uint16_t *>(nullptr), 0.0f, pre, 1.0f, n, H, RowFuse{});
-    ok = ok && gemm(c, n, H, gu, g, 2 * I, tokens, 2 * I, H);
-    ok = ok && launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((I * tokens + 255) / 256, 4096)), dim3(256), 0,
-                      g, I, tokens, RowFuse{});
-    ok = ok && gemm(c, g, 2 * I, down, b, H, tokens, H, I);
-    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(tokens), dim3(512), 0, s, static_cast<const float *>(b),
-                      post, kPostMlpOffset, static_cast<const uint16_t *>(nullptr), 0.0f,
-                      static_cast<float *>(nullptr), H, RowFuse{});
-    ok = ok && note(c, "mlp out", cudaMemcpyAsync(states, s, tokens * H * 4, cudaMemcpyDeviceToHost, c->stream)) &&
-         note(c, "mlp", cudaStreamSynchronize(c->stream));
-    cudaFree(s);
-    cudaFree(n);
-    cudaFree(g);
-    cudaFree(b);
+    ok = ok && projection_with(c, n, H, gu, g, 2 * I, T, 2 * I, H, split, err);
+    ok = ok && launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((I * T + 255) / 256, 4096)), dim3(256), 0, g, I,
+                      T, RowFuse{});
+    ok = ok && projection_with(c, g, 2 * I, down, b, H, T, H, I, split, err);
+    ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(512), 0, s, static_cast<const float *>(b), post,
+                      kPostMlpOffset, static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H,
+                      RowFuse{});
+    ok = ok && note(c, "mlp out", cudaMemcpyAsync(states, s, T * H * 4, cudaMemcpyDeviceToHost, c->stream)) &&
+         note(c, "mlp", cudaStreamSynchronize(c->stream)) && staging_ok(c);
     return ok ? 1 : -1;
 }
 

@@ -46,7 +46,7 @@ int main(int argc, char **argv) {
     if (argc != 4) return 90;
     const int tokenizer_only = !strcmp(argv[3], "tokenizer");
     const char *weights[1] = {argv[2]};
-    struct plamo_model_config cfg = {128, 2, 4, 2, 32, 192, 107520, 8, 2, 512, 0,
+    struct plamo_model_config cfg = {128, 2, 4, 2, 32, 192, 107520, 64, 2, 512, 0,
                                      10000.0, 1000000.0, 256.0, 4096.0, 32.0, 1.0};
     struct plamo_engine_files files = {argv[1], weights, 1, NULL, &cfg, 512, 0};
     struct plamo_engine_info info;
@@ -107,7 +107,9 @@ def write_vocab(path):
 
 
 def engine_profile(pkg):
-    return pkg.Profile("engine", 128, 2, 4, 2, 32, 192, vocab=107520, window=8, pattern=2, max_position=512)
+    # The sliding window holds the whole template prefix (the reference's
+    # snapshot rule: every layer keeps exactly the prefix's rows).
+    return pkg.Profile("engine", 128, 2, 4, 2, 32, 192, vocab=107520, window=64, pattern=2, max_position=512)
 
 
 def write_checkpoint(pkg, path):
