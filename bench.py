@@ -388,6 +388,7 @@ def run_ours(args, world, rank, local, dist):
     e2e_value = world / e2e_s
 
     batch_info = run_batch(args, pkg, lib, be, hm, profile, world, rank, dist, peak)
+    config1 = gemv_configs(lib, ctx, peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -437,9 +438,65 @@ def run_ours(args, world, rank, local, dist):
             "clocks": clock_info,
             "cpu_baseline": cpu,
             "batch": batch_info,
+            "config1_gemv": config1,
         }
     be.close()
+    if rank == 0 and world == 1:
+        line["config3_2b_decode"] = decode_2b(args, pkg, local, peak)
     return line if rank == 0 else None
+
+
+def gemv_configs(lib, ctx, peak):
+    """BASELINE config 1 on the GPU: the single BF16 GEMV at 4096 x 4096 and its
+    8-row-block variant 14336 x 4096 (synthetic N(0, 0.02)-like weights, x
+    N(0, 1)). Both matrices fit in the 126 MB L2, so consecutive launches
+    rotate through enough copies (> 400 MB) that each streams its weights from
+    HBM; CUDA-event time over 200 launches, algorithmic bytes."""
+    out = {}
+    for rows, cols in ((4096, 4096), (14336, 4096)):
+        copies = -(-400_000_000 // (2 * rows * cols))
+        dw = lib.plamo_cuda_device_alloc(ctx, copies * rows * cols * 2)
+        dx = lib.plamo_cuda_device_alloc(ctx, cols * 4)
+        dy = lib.plamo_cuda_device_alloc(ctx, rows * 4)
+        lib.plamo_cuda_fill_synthetic_bf16(ctx, dw, copies * rows * cols, 7, 0.0, 0.02)
+        lib.plamo_cuda_fill_synthetic_f32(ctx, dx, cols, 6, 0.0, 1.0)
+        lib.plamo_cuda_time_gemv_copies(ctx, dw, copies, dx, dy, rows, cols, 2 * copies)
+        ms = lib.plamo_cuda_time_gemv_copies(ctx, dw, copies, dx, dy, rows, cols, 200) / 200
+        for q in (dw, dx, dy):
+            lib.plamo_cuda_device_free(ctx, q)
+        nbytes = 2 * rows * cols + 4 * cols + 4 * rows
+        gbs = nbytes / (ms / 1000) / 1e9
+        out[f"{rows}x{cols}"] = {"us": ms * 1000, "GB_s": gbs, "frac": gbs / peak, "copies_rotated": copies,
+                                 "algorithmic_bytes": nbytes}
+    return out
+
+
+def decode_2b(args, pkg, local, peak):
+    """BASELINE config 3 on the GPU: the 2B profile, 81-id prompt
+    (default_rng(1)), batch-1 greedy decode; tok/s and the HBM roofline."""
+    lib = pkg.load()
+    profile = pkg.PROFILES["2b"]
+    be = pkg.Backend(device=local, max_context=8192 + 16, max_prefill=4096)
+    try:
+        hm = pkg.HostModel(profile, weights="synthetic", full_capacity=8208)
+        be.preload_synthetic(hm, seed=3)
+        be.prepare(hm)
+        ids = np.random.default_rng(1).integers(3, 100000, size=81).astype(np.uint32)
+        nxt = ctypes.c_uint32()
+        assert lib.plamo_cuda_prefill_greedy(be.ctx, hm.ptr, ids.ctypes.data, 81, ctypes.byref(nxt)) == 1
+        assert lib.plamo_cuda_time_decode(be.ctx, hm.ptr, 3) > 0, be.info().note
+        steps = 60
+        ms = lib.plamo_cuda_time_decode(be.ctx, hm.ptr, steps)
+        assert ms > 0, be.info().note
+        ctx_mean = 81 + 3 + (steps + 1) / 2.0
+        step_bytes = (profile.weight_bytes_per_token() + profile.norm_bytes_per_token() + 2 * profile.hidden +
+                      profile.layers * ctx_mean * profile.kh * profile.dim * 4 * 2)
+        gbs = step_bytes / (ms / steps / 1000) / 1e9
+        return {"value": steps / (ms / 1000), "unit": "tok/s", "ms_per_step": ms / steps, "steps": steps,
+                "roofline": {"achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "algorithmic_bytes": step_bytes}}
+    finally:
+        be.close()
 
 
 def run_batch(args, pkg, lib, be, hm, profile, world, rank, dist, peak):

@@ -247,6 +247,11 @@ double plamo_cuda_time_decode(struct plamo_cuda *, struct model *, uint64_t repe
 /* Same for the standalone GEMV over `repeats` launches. */
 double plamo_cuda_time_gemv(struct plamo_cuda *, const uint16_t *w, const float *x, float *y,
                             uint64_t rows, uint64_t cols, uint64_t repeats);
+/* Same, launch i reading the weights of copy i % copies (copies consecutive
+   [rows, cols] matrices at w): rotating through more bytes than L2 holds
+   makes each launch stream its weights from HBM. */
+double plamo_cuda_time_gemv_copies(struct plamo_cuda *, const uint16_t *w, uint64_t copies, const float *x, float *y,
+                                   uint64_t rows, uint64_t cols, uint64_t repeats);
 /* Same for `repeats` back-to-back prompt projections (split + GEMM). */
 double plamo_cuda_time_gemm(struct plamo_cuda *, const float *x, const uint16_t *w, float *y, uint64_t tokens,
                             uint64_t rows, uint64_t cols, uint64_t repeats);

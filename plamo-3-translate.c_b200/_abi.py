@@ -158,6 +158,7 @@ SIGNATURES = {
     "plamo_cuda_synchronize": (c_int, [P]),
     "plamo_cuda_time_decode": (c_double, [P, M, c_uint64]),
     "plamo_cuda_time_gemv": (c_double, [P, P, P, P, c_uint64, c_uint64, c_uint64]),
+    "plamo_cuda_time_gemv_copies": (c_double, [P, P, c_uint64, P, P, c_uint64, c_uint64, c_uint64]),
     "plamo_cuda_kernel_launches": (c_uint64, [P]),
     "plamo_cuda_decode_path": (c_char_p, [P, M]),
     "plamo_cuda_read_outputs": (c_int, [P, M]),

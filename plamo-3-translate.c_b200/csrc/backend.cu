@@ -947,7 +947,7 @@ bool record_batch(plamo_cuda *c, plamo_cuda_batch *b, DModel *m) {
                         1.0f, m->p_norm, H, f);
         if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H, f.split != nullptr))
             return false;
-        if (!launch(c, decode_attention128_batch_kernel, dim3(static_cast<uint32_t>(m->KH), kDec128Splits, b->B),
+        if (!launch(c, decode_attention128_batch_kernel, dim3(static_cast<uint32_t>(m->KH), kDec128BatchSplits, b->B),
                     dim3(kDecThreads), decode_attention128_smem(G),
                     static_cast<const DecodeAttnParams *>(b->d_attn + l * b->B)))
             return false;
@@ -2817,6 +2817,20 @@ double plamo_cuda_time_gemv(struct plamo_cuda *c, const uint16_t *w, const float
     cudaEventRecord(c->ev0, c->stream);
     for (uint64_t i = 0; i < repeats; ++i)
         if (plamo_cuda_gemv_device(c, w, x, y, rows, cols) != 1) return -1;
+    cudaEventRecord(c->ev1, c->stream);
+    if (!note(c, "time gemv", cudaStreamSynchronize(c->stream))) return -1;
+    float ms = 0;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    return ms;
+}
+
+double plamo_cuda_time_gemv_copies(struct plamo_cuda *c, const uint16_t *w, uint64_t copies, const float *x, float *y,
+                                   uint64_t rows, uint64_t cols, uint64_t repeats) {
+    if (!c || !repeats || !copies) return -1;
+    cudaStreamSynchronize(c->stream);
+    cudaEventRecord(c->ev0, c->stream);
+    for (uint64_t i = 0; i < repeats; ++i)
+        if (plamo_cuda_gemv_device(c, w + (i % copies) * rows * cols, x, y, rows, cols) != 1) return -1;
     cudaEventRecord(c->ev1, c->stream);
     if (!note(c, "time gemv", cudaStreamSynchronize(c->stream))) return -1;
     float ms = 0;
