@@ -80,6 +80,32 @@ def measured_peaks():
     return 6650.0, "fallback (6.65 TB/s, earlier measurement on this pool)"
 
 
+def tensor_peak():
+    """Dense BF16 peak for a kernel timed inside a long step (the sustained
+    cuBLAS loop under the power cap), else the pool's earlier measurement."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        if "bf16_tflops_sustained" in p:
+            return float(p["bf16_tflops_sustained"]), "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    return 1400.0, "fallback (1.4 PFLOP/s sustained, earlier measurement on this pool)"
+
+
+def prefill_flops(profile, tokens):
+    """Algorithmic FLOP of a layer-major prefill of `tokens` prompt ids: every
+    projection for every token, causal attention (QK^T and PV over the keys a
+    query sees, all query heads) and the head for the last token only."""
+    h = profile.hidden
+    per_token = profile.qkv_rows * h + h * profile.attention_width + 3 * profile.inter * h
+    flops = 2.0 * tokens * profile.layers * per_token + 2.0 * profile.vocab * h
+    for layer in range(profile.layers):
+        span = tokens if profile.full(layer) else profile.window
+        keys = sum(min(t + 1, span) for t in range(tokens))
+        flops += 4.0 * profile.qh * profile.dim * keys
+    return flops
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled during the timed region."""
 
@@ -415,6 +441,7 @@ def run_ours(args, world, rank, local, dist):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": workload_config(world),
             "prefill_tok_s": prefill_rate,
+            "prefill_roofline": prefill_roofline(profile, prefill_rate / world),
             "decode_path": decode_path,
             "roofline": {"bound": "hbm",
                          "kernel": ("decode_token_kernel (one persistent launch per token)"
@@ -444,6 +471,15 @@ def run_ours(args, world, rank, local, dist):
     if rank == 0 and world == 1:
         line["config3_2b_decode"] = decode_2b(args, pkg, local, peak)
     return line if rank == 0 else None
+
+
+def prefill_roofline(profile, rate):
+    """Per-GPU prefill of the PROMPT-id prompt against the sustained tensor peak."""
+    tflops = prefill_flops(profile, PROMPT) * rate / PROMPT / 1e12
+    peak, src = tensor_peak()
+    return {"bound": "tensor", "kernel": "layer-major prefill (tcgen05 projections, prompt attention)",
+            "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
+            "algorithmic_flops": prefill_flops(profile, PROMPT), "peak_source": src}
 
 
 def gemv_configs(lib, ctx, peak):

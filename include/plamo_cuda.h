@@ -271,8 +271,15 @@ const char *plamo_cuda_decode_path(struct plamo_cuda *, struct model *);
    attention, after o_proj, after gate_up, after down_proj; last: after the
    head); [1 + B + p] when its producer warp issued the first weight chunk of
    projection p, p < 4 * layers + 1 (qkv, o_proj, gate_up, down_proj per
-   layer, then the head). Returns the number of stamps, or -1 when the model
-   does not decode with the persistent step or capacity is too small. */
+   layer, then the head).
+   On the graph path (per-projection kernels) a graph of the same step with
+   timestamping launches is captured and run once instead: six stamps per
+   launch, 5 * layers + 1 launches in step order (per layer qkv, attention,
+   o_proj, gate_up, down_proj; then the head): [0] the first CTA's entry,
+   [1] the last CTA past its dependency wait and prologue, [2] the first CTA
+   done with its weight stream (attention: done), [3] the last one, [4] the
+   last CTA past its dependency wait alone, [5] the last CTA's entry.
+   Returns the number of stamps, or -1 when capacity is too small. */
 double plamo_cuda_decode_trace(struct plamo_cuda *, struct model *, uint64_t token, uint64_t *stamps,
                                uint64_t capacity);
 

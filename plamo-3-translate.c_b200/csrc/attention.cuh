@@ -461,6 +461,7 @@ struct DecodeAttnParams {
     uint32_t qh, kh, dim;
     float *qkv;  // [qh + 2 kh][dim] projection of the token (read only)
     float *out;  // [qh][dim]
+    unsigned long long *trace = nullptr;  // launch timeline record (trace_stamp), or null
 };
 
 // Key tile row stride: D + 4 keeps 16-byte alignment and spreads the rows of
@@ -512,6 +513,7 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     float *lrow = mrow + G;
     float *corr = lrow + G;
     cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+    const uint64_t t_entry = p.trace ? global_ns() : 0;
 
     pdl_launch_dependents();  // the next projection may start streaming its weights
     // The committed rows and their counter were final before this step began
@@ -540,6 +542,13 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     };
     if (k0 < k1) stage(k0, static_cast<uint32_t>(k1 - k0 < kDecTile ? k1 - k0 : kDecTile));
     pdl_wait();
+    if (p.trace && threadIdx.x == 0) {
+        const uint64_t t = global_ns();
+        trace_stamp(p.trace, 0, t_entry);
+        trace_stamp(p.trace, 5, t_entry);
+        trace_stamp(p.trace, 4, t);
+        trace_stamp(p.trace, 1, t);
+    }
 
     // Q heads of the group (one warp each): lane l < 16 owns coordinate pairs
     // 4l..4l+3 / 64+4l..64+4l+3; RMSNorm(+1), rotate at the query position.
@@ -721,6 +730,11 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
         }
     }
     cluster.sync();
+    if (p.trace && threadIdx.x == 0) {
+        const uint64_t t = global_ns();
+        trace_stamp(p.trace, 2, t);
+        trace_stamp(p.trace, 3, t);
+    }
 }
 
 __global__ void __cluster_dims__(1, kDec128Splits, 1) __launch_bounds__(kDecThreads)

@@ -126,6 +126,8 @@ struct DModel {
     uint32_t pt_grid = 0;
     size_t pt_smem = 0;
     char pt_reason[96] = "";  // why the persistent step is not used
+    unsigned long long *trace = nullptr;  // timeline records of a traced graph step (plamo_cuda_decode_trace)
+    uint32_t trace_slot = 0;
     std::vector<void *> allocations;
     std::vector<uintptr_t> signature;  // host descriptor identity at prepare time
 };
@@ -333,27 +335,36 @@ bool launch_gemv_shape(plamo_cuda *c, const GemvParams &p, int U, uint32_t grid,
     }
 }
 
+// Shared-memory carveout preference (percent of the unified L1/shared
+// array, -1: the driver's choice). Kernels whose CTAs are to share an SM
+// must run with the same carveout: an SM only changes its split when idle.
+template <typename K>
+void prefer_carveout(K kernel, int carveout) {
+    if (carveout >= 0) cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, carveout);
+}
+
 // Allow each kernel the device's opt-in shared memory minus its static part.
 template <typename K>
-void allow_smem(K kernel, int optin) {
+void allow_smem(K kernel, int optin, int carveout) {
     cudaFuncAttributes a{};
     if (cudaFuncGetAttributes(&a, kernel) == cudaSuccess)
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - static_cast<int>(a.sharedSizeBytes));
+    prefer_carveout(kernel, carveout);
 }
 
 template <int PRO, int EPI>
-void set_gemv_smem_limits(int optin) {
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 1, false>, optin);
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 2, false>, optin);
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 4, false>, optin);
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 1, true>, optin);
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 2, true>, optin);
-    allow_smem(gemv_bulk_kernel<PRO, EPI, 4, true>, optin);
-    allow_smem(gemv_kernel<PRO, EPI, 4>, optin);
-    allow_smem(gemv_kernel<PRO, EPI, 2>, optin);
-    allow_smem(gemv_kernel<PRO, EPI, 1>, optin);
-    allow_smem(gemv_kernel<PRO, EPI, 0>, optin);
+void set_gemv_smem_limits(int optin, int carveout) {
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 1, false>, optin, carveout);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 2, false>, optin, carveout);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 4, false>, optin, carveout);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 1, true>, optin, carveout);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 2, true>, optin, carveout);
+    allow_smem(gemv_bulk_kernel<PRO, EPI, 4, true>, optin, carveout);
+    allow_smem(gemv_kernel<PRO, EPI, 4>, optin, carveout);
+    allow_smem(gemv_kernel<PRO, EPI, 2>, optin, carveout);
+    allow_smem(gemv_kernel<PRO, EPI, 1>, optin, carveout);
+    allow_smem(gemv_kernel<PRO, EPI, 0>, optin, carveout);
 }
 
 // Grid of a projection: one CTA per SM (times the configured factor), fewer
@@ -728,9 +739,15 @@ bool fits(const DModel *m, uint64_t tokens) {
 }
 
 // ---- decode step -----------------------------------------------------------
+// The next launch's timeline record while a traced step is recorded, else null.
+unsigned long long *next_trace(DModel *m) {
+    return m->trace ? m->trace + kTraceWords * m->trace_slot++ : nullptr;
+}
+
 bool launch_decode_attention(plamo_cuda *c, DModel *m, uint64_t l) {
     DecodeAttnParams dp{attn_layer(m, l), static_cast<uint32_t>(m->QH), static_cast<uint32_t>(m->KH),
                         static_cast<uint32_t>(m->D), m->qkv, m->attn};
+    dp.trace = next_trace(m);
     const size_t smem = decode_attention_smem(static_cast<uint32_t>(m->QH / m->KH), static_cast<uint32_t>(m->D));
     const dim3 block(kDecThreads);
     if (m->D == 128 && m->QH / m->KH <= 32)
@@ -822,6 +839,7 @@ bool record_decode(plamo_cuda *c, DModel *m) {
         p.off2 = 1.0f;
         p.y = m->qkv;
         p.error = m->d_error;
+        p.trace = next_trace(m);
         bool ok;
         if (l == 0) {
             p.embedding = m->emb;
@@ -850,6 +868,7 @@ bool record_decode(plamo_cuda *c, DModel *m) {
         o.cols = m->AW;
         o.x = m->attn;
         o.y = m->branch;
+        o.trace = next_trace(m);
         if (m->tp.active) {
             o.tp_role = 2;
             o.tp = tp_point(m, false, 2 * l);
@@ -868,6 +887,7 @@ bool record_decode(plamo_cuda *c, DModel *m) {
         g.state_out = m->state[s ^ 1];
         s ^= 1;
         g.y = m->mid;
+        g.trace = next_trace(m);
         if (m->tp.active) {
             g.tp_role = 1;
             g.tp = tp_point(m, false, 2 * l);
@@ -879,6 +899,7 @@ bool record_decode(plamo_cuda *c, DModel *m) {
         d.cols = m->I;
         d.x = m->mid;
         d.y = m->branch;
+        d.trace = next_trace(m);
         if (m->tp.active) {
             d.tp_role = 2;
             d.tp = tp_point(m, false, 2 * l + 1);
@@ -896,6 +917,7 @@ bool record_decode(plamo_cuda *c, DModel *m) {
     h.norm2 = m->norm;
     h.off2 = 1.0f;
     h.state_out = m->state[s ^ 1];
+    h.trace = next_trace(m);
     m->final_state = m->state[s ^ 1];
     h.norm_out = m->normalized;
     h.y = m->logits;
@@ -1429,27 +1451,34 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     int per_sm = 0;
     cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, cfg.device);
     c->smem_per_sm = per_sm > 0 ? per_sm : optin;
-    set_gemv_smem_limits<PRO_X, EPI_STORE>(optin);
-    set_gemv_smem_limits<PRO_NORM, EPI_STORE>(optin);
-    set_gemv_smem_limits<PRO_RESID_NORM, EPI_STORE>(optin);
-    set_gemv_smem_limits<PRO_EMBED_NORM, EPI_STORE>(optin);
-    set_gemv_smem_limits<PRO_RESID_NORM, EPI_SWIGLU>(optin);
-    set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>(optin);
-    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_STORE>(optin);
-    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_SWIGLU>(optin);
-    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_ARGMAX>(optin);
-    set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin);
-    allow_smem(attention_kernel, optin);
-    allow_smem(prompt_attention_kernel, optin);
-    allow_smem(decode_attention128_kernel, optin);
-    allow_smem(gemm_tc_kernel<16>, optin);
-    allow_smem(gemm_tc_kernel<32>, optin);
-    allow_smem(gemm_tc_kernel<64>, optin);
-    allow_smem(gemm_tc_kernel<128>, optin);
-    allow_smem(decode_attention_kernel<128>, optin);
-    allow_smem(decode_attention128_batch_kernel, optin);
-    allow_smem(decode_attention_kernel<0>, optin);
-    allow_smem(decode_token_kernel, optin);
+    const char *carve = getenv("PLAMO_CUDA_CARVEOUT");
+    // Max-shared carveout by default: the decode kernels' CTAs then land on SMs
+    // still running the previous kernel (batched 8B decode step 4.77 -> 4.33 ms).
+    const int carveout = carve ? std::max(-1, std::min(atoi(carve), 100)) : 100;
+    set_gemv_smem_limits<PRO_X, EPI_STORE>(optin, carveout);
+    set_gemv_smem_limits<PRO_NORM, EPI_STORE>(optin, carveout);
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_STORE>(optin, carveout);
+    set_gemv_smem_limits<PRO_EMBED_NORM, EPI_STORE>(optin, carveout);
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_SWIGLU>(optin, carveout);
+    set_gemv_smem_limits<PRO_RESID_NORM, EPI_ARGMAX>(optin, carveout);
+    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_STORE>(optin, carveout);
+    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_SWIGLU>(optin, carveout);
+    set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_ARGMAX>(optin, carveout);
+    set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin, carveout);
+    allow_smem(attention_kernel, optin, carveout);
+    allow_smem(prompt_attention_kernel, optin, carveout);
+    allow_smem(decode_attention128_kernel, optin, carveout);
+    allow_smem(gemm_tc_kernel<16>, optin, carveout);
+    allow_smem(gemm_tc_kernel<32>, optin, carveout);
+    allow_smem(gemm_tc_kernel<64>, optin, carveout);
+    allow_smem(gemm_tc_kernel<128>, optin, carveout);
+    allow_smem(decode_attention_kernel<128>, optin, carveout);
+    allow_smem(decode_attention128_batch_kernel, optin, carveout);
+    allow_smem(decode_attention_kernel<0>, optin, carveout);
+    allow_smem(decode_token_kernel, optin, carveout);
+    prefer_carveout(argmax_merge_kernel, carveout);
+    prefer_carveout(advance_kernel, carveout);
+    prefer_carveout(tp_epoch_kernel, carveout);
     cudaFuncSetAttribute(decode_attention128_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaFuncSetAttribute(decode_attention128_batch_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if ((e = cudaGetLastError()) != cudaSuccess) {
@@ -2860,13 +2889,53 @@ uint64_t plamo_cuda_kernel_launches(const struct plamo_cuda *c) {
     return c ? c->info.launches : 0;
 }
 
+// One decode step of the graph path with every projection and attention
+// launch stamping its timeline record: a graph of the traced step is
+// captured, launched once and released.
+double graph_trace(plamo_cuda *c, DModel *m, uint64_t token, uint64_t *stamps, uint64_t capacity) {
+    const uint64_t n = kTraceWords * (5 * m->L + 1);
+    if (capacity < n) return -1;
+    auto *trace = static_cast<unsigned long long *>(plamo_cuda_device_alloc(c, n * 8));
+    if (!trace) return -1;
+    m->trace = trace;
+    m->trace_slot = 0;
+    const uint64_t before = c->info.launches;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    bool ok = note(c, "capture", cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    if (ok) {
+        const bool recorded = record_decode(c, m);
+        ok = note(c, "capture end", cudaStreamEndCapture(c->stream, &graph)) && recorded;
+    }
+    m->trace = nullptr;
+    c->info.launches = before;
+    ok = ok && note(c, "instantiate", cudaGraphInstantiate(&exec, graph, 0));
+    m->verify_valid = false;
+    c->pinned_u32[0] = static_cast<uint32_t>(token);
+    ok = ok && note(c, "trace", cudaMemsetAsync(trace, 0, n * 8, c->stream)) &&
+         note(c, "token", cudaMemcpyAsync(m->d_token, c->pinned_u32, 4, cudaMemcpyHostToDevice, c->stream)) &&
+         note(c, "graph launch", cudaGraphLaunch(exec, c->stream)) &&
+         note(c, "trace", cudaMemcpyAsync(stamps, trace, n * 8, cudaMemcpyDeviceToHost, c->stream)) &&
+         note(c, "trace", cudaStreamSynchronize(c->stream));
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    cudaFree(trace);
+    if (!ok || !check_device_error(c, m)) return -1;
+    for (uint64_t i = 0; i < n; i += kTraceWords) {  // minima were kept complemented
+        stamps[i] = ~0ull - stamps[i];
+        stamps[i + 2] = ~0ull - stamps[i + 2];
+    }
+    publish_counts(m, 1);
+    return static_cast<double>(n);
+}
+
 double plamo_cuda_decode_trace(struct plamo_cuda *c, struct model *model, uint64_t token, uint64_t *stamps,
                                uint64_t capacity) {
     if (!c || !stamps) return -1;
     cudaSetDevice(c->device);
     DModel *m = find_model(c, model);
-    if (!m || token >= model->vocab || !reconcile(c, m) || !fits(m, 1) || !ensure_graph(c, m) || !m->pt_ready)
-        return -1;
+    if (!m || token >= model->vocab || !reconcile(c, m) || !fits(m, 1) || !ensure_graph(c, m)) return -1;
+    if (!m->pt_ready) return graph_trace(c, m, token, stamps, capacity);
     const uint64_t n = 1 + (5 * m->L + 1) + (4 * m->L + 1);
     if (capacity < n) return -1;
     auto *trace = static_cast<unsigned long long *>(plamo_cuda_device_alloc(c, n * 8));

@@ -154,6 +154,17 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Launch timeline of a traced decode step: one record of kTraceWords words
+// per traced launch, all starting at zero; minima are kept as UINT64_MAX - t
+// so that every field is an atomicMax: [0] first CTA entry, [1] last CTA past
+// its dependency wait and prologue, [2] first CTA done streaming, [3] last,
+// [4] last CTA past the dependency wait alone, [5] last CTA entry.
+constexpr int kTraceWords = 6;
+__device__ __forceinline__ void trace_stamp(unsigned long long *rec, int field, uint64_t t) {
+    if (field == 0 || field == 2) atomicMax(rec + field, ~0ull - t);
+    else atomicMax(rec + field, static_cast<unsigned long long>(t));
+}
+
 // Wait for the phase of `parity` to complete, giving up after ~2 s of wall
 // time (returns false; the caller records an error and drains).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {

@@ -57,6 +57,7 @@ struct GemvParams {
     // epilogue pushes its rows into every rank's slot of the point.
     int tp_role;
     TpPoint tp;
+    unsigned long long *trace;  // launch timeline record (trace_stamp), or null
 };
 
 constexpr int kGemvThreads = 512;
@@ -99,8 +100,34 @@ __device__ __forceinline__ float dot8r(uint4 w, const float *x, float acc) {
 // registers, one L2 round trip per input instead of one per loop trip.
 constexpr int kPV = 4;
 
+// The vector path's norm weights, loaded before the dependency wait: they
+// are constants of the model, so their latency overlaps the previous kernel.
+struct NormWeights {
+    uint2 w1[kPV], w2[kPV];
+};
+
 template <int PRO>
-__device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, float *red) {
+__device__ __forceinline__ void gemv_norm_weights(const GemvParams &p, NormWeights &nw) {
+    constexpr bool kResid = PRO == PRO_RESID_NORM || PRO == PRO_RESID_NORM_TP;
+    if constexpr (PRO == PRO_X || PRO == PRO_EMBED_NORM) {
+        return;
+    } else {
+        const uint32_t nt = blockDim.x;
+        if (p.cols % 4 != 0 || p.cols > 4ull * kPV * nt) return;
+        const uint32_t n4 = static_cast<uint32_t>(p.cols / 4);
+#pragma unroll
+        for (int k = 0; k < kPV; ++k) {
+            const uint32_t i = threadIdx.x + k * nt;
+            if (i < n4) {
+                if (kResid) nw.w1[k] = *reinterpret_cast<const uint2 *>(p.norm1 + 4 * i);
+                nw.w2[k] = *reinterpret_cast<const uint2 *>(p.norm2 + 4 * i);
+            }
+        }
+    }
+}
+
+template <int PRO>
+__device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, float *red, const NormWeights &nw) {
     constexpr bool kResid = PRO == PRO_RESID_NORM || PRO == PRO_RESID_NORM_TP;
     constexpr bool reduce = PRO == PRO_RESID_NORM_TP;
     const uint64_t n = p.cols;
@@ -134,7 +161,6 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
     } else if (vec) {
         const uint32_t n4 = static_cast<uint32_t>(n / 4);
         float4 st[kPV], br[kPV];
-        uint2 w1[kPV];
         const uint32_t tag = reduce && p.tp.ll ? *p.tp.epoch + 1 : 0;
         if (reduce && !p.tp.ll) {
             if (threadIdx.x == 0) tp_wait_flags(p.tp);
@@ -149,7 +175,6 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
                 if (kResid) {
                     if (!reduce) br[k] = ld4(p.branch + 4 * i);
                     else if (!p.tp.ll) br[k] = tp_sum4(p.tp, 4 * i);
-                    w1[k] = *reinterpret_cast<const uint2 *>(p.norm1 + 4 * i);
                 }
             }
         }
@@ -163,19 +188,17 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
             for (int k = 0; k < kPV; ++k) {
                 const uint32_t i = threadIdx.x + k * nt;
                 if (i < n4) {
-                    const float4 b = apply4(br[k], inv, norm4(w1[k], p.off1));
+                    const float4 b = apply4(br[k], inv, norm4(nw.w1[k], p.off1));
                     st[k] = make_float4(__fadd_rn(st[k].x, b.x), __fadd_rn(st[k].y, b.y),
                                         __fadd_rn(st[k].z, b.z), __fadd_rn(st[k].w, b.w));
                 }
             }
         }
-        uint2 w2[kPV];
         float s = 0.0f;
 #pragma unroll
         for (int k = 0; k < kPV; ++k) {
             const uint32_t i = threadIdx.x + k * nt;
             if (i < n4) {
-                w2[k] = *reinterpret_cast<const uint2 *>(p.norm2 + 4 * i);
                 s += sq4(st[k]);
                 if (publish && p.state_out) *reinterpret_cast<float4 *>(p.state_out + 4 * i) = st[k];
             }
@@ -185,7 +208,7 @@ __device__ __forceinline__ bool gemv_prologue(const GemvParams &p, float *xs, fl
         for (int k = 0; k < kPV; ++k) {
             const uint32_t i = threadIdx.x + k * nt;
             if (i < n4) {
-                const float4 v = apply4(st[k], inv, norm4(w2[k], p.off2));
+                const float4 v = apply4(st[k], inv, norm4(nw.w2[k], p.off2));
                 *reinterpret_cast<float4 *>(xs + 4 * i) = v;
                 if (publish && p.norm_out) *reinterpret_cast<float4 *>(p.norm_out + 4 * i) = v;
             }
@@ -355,8 +378,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvParams p) {
         }
     }
 
+    NormWeights nw;
+    gemv_norm_weights<PRO>(p, nw);
     pdl_wait();
-    const bool ok = gemv_prologue<PRO>(p, xs, red);
+    const bool ok = gemv_prologue<PRO>(p, xs, red, nw);
     __syncthreads();
     if (!ok) return;
 
@@ -485,6 +510,7 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
     // selected, not indexed, so no local-memory array is formed.
     const uint16_t *const range_gate = p.w + u0 * cols;
     const uint16_t *const range_up = p.w + (u0 + half_rows) * cols;
+    const uint64_t t_entry = p.trace ? global_ns() : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -517,9 +543,17 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
     if (producer && lane == 0)
         for (; issued < primed; ++issued) issue(issued, issued);
 
+    NormWeights nw;
+    gemv_norm_weights<PRO>(p, nw);
     pdl_wait();
-    const bool ok = gemv_prologue<PRO>(p, xs, red);
+    if (p.trace && threadIdx.x == 0) trace_stamp(p.trace, 4, global_ns());
+    const bool ok = gemv_prologue<PRO>(p, xs, red, nw);
     __syncthreads();
+    if (p.trace && threadIdx.x == 0) {
+        trace_stamp(p.trace, 0, t_entry);
+        trace_stamp(p.trace, 5, t_entry);
+        trace_stamp(p.trace, 1, global_ns());
+    }
 
     // Register copy of this warp's input slots: set i serves sub-range
     // w+16i, which is row jr of a chunk at column slot js; the lane's two
@@ -622,6 +656,11 @@ __global__ void __launch_bounds__(kBulkThreads) gemv_bulk_kernel(GemvParams p, i
             for (uint32_t k = issued > static_cast<uint32_t>(stages) ? issued - stages : 0; k < issued; ++k)
                 mbar_wait(&full_bar[k % stages], (k / stages) & 1u);
         return;
+    }
+    if (p.trace && threadIdx.x == 0) {
+        const uint64_t t = global_ns();
+        trace_stamp(p.trace, 2, t);
+        trace_stamp(p.trace, 3, t);
     }
     gemv_epilogue<EPI>(p, partial, u0, u1, slots, red);
 }

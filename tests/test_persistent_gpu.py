@@ -147,3 +147,33 @@ def test_decode_trace_reports_every_phase():
         expect(be, be.lib.plamo_cuda_forward(be.ctx, hm.ptr, 11))
     finally:
         be.close()
+
+
+def test_graph_decode_trace_orders_every_launch():
+    """plamo_cuda_decode_trace on the graph path: a traced copy of the step's
+    graph stamps every projection and attention launch. Within a launch the
+    first entry precedes the last CTA past its wait, which precedes the last
+    CTA done; each launch's dependency wait ends after the previous launch's
+    last CTA is done (programmatic dependent launch orders them)."""
+    pkg = load_package()
+    prof = mini_profile(pkg)
+    be = backend_with(False)
+    try:
+        hm = pkg.HostModel(prof, weights="synthetic")
+        be.preload_synthetic(hm, seed=17)
+        be.prepare(hm)
+        ids = np.random.default_rng(9).integers(3, prof.vocab, size=5).astype(np.uint32)
+        expect(be, be.lib.plamo_cuda_prefill(be.ctx, hm.ptr, ids.ctypes.data, len(ids), None))
+        n = 6 * (5 * prof.layers + 1)
+        stamps = np.zeros(n, dtype=np.uint64)
+        assert be.lib.plamo_cuda_decode_trace(be.ctx, hm.ptr, 7, stamps.ctypes.data, n - 1) == -1
+        assert be.lib.plamo_cuda_decode_trace(be.ctx, hm.ptr, 7, stamps.ctypes.data, n) == n
+        t = stamps.reshape(-1, 6).astype(np.int64)
+        assert np.all(t > 0)
+        assert np.all(t[:, 0] <= t[:, 5]) and np.all(t[:, 5] <= t[:, 1]) and np.all(t[:, 4] <= t[:, 1])
+        assert np.all(t[:, 1] <= t[:, 3]) and np.all(t[:, 0] <= t[:, 2]) and np.all(t[:, 2] <= t[:, 3])
+        assert np.all(t[1:, 4] >= t[:-1, 3])
+        assert be.lib.plamo_cuda_decode_path(be.ctx, hm.ptr).startswith(b"graph")
+        expect(be, be.lib.plamo_cuda_forward(be.ctx, hm.ptr, 11))
+    finally:
+        be.close()
