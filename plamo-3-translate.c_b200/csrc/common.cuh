@@ -78,7 +78,10 @@ __device__ __forceinline__ float block_sum(float v, float *scratch) {
 // RMSNorm inverse 1/sqrt(sum/n + 1e-6) from a sum of squares (reference
 // src/math.s:349-366: divide, add eps, sqrt, reciprocal, each rounded).
 __device__ __forceinline__ float rms_inverse(float sum_squares, uint64_t n) {
-    float mean = __fdiv_rn(sum_squares, static_cast<float>(n));
+    // For a power-of-two n the product by the exact reciprocal is the same
+    // correctly rounded quotient, without the division's latency.
+    float mean = (n & (n - 1)) == 0 ? __fmul_rn(sum_squares, 1.0f / static_cast<float>(n))
+                                    : __fdiv_rn(sum_squares, static_cast<float>(n));
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-6f)));
 }
 // (x * inverse) * (w + offset)
