@@ -826,13 +826,20 @@ def run_profile(args):
                        for _ in range((args.requests if args.profile == "batch" else 1) - 1)]
         nxt = ctypes.c_uint32()
         toks = np.zeros(len(reqs), dtype=np.uint32)
-        prompt = PROMPT if args.profile == "step" else 16
+        prompt = PROMPT if args.profile in ("step", "prefill") else 16
         for i, r in enumerate(reqs):
             be.prepare(r)
             ids = np.random.default_rng(1 + i).integers(3, 100000, size=prompt).astype(np.uint32)
             assert lib.plamo_cuda_prefill_greedy(ctx, r.ptr, ids.ctypes.data, prompt, ctypes.byref(nxt)) == 1
             toks[i] = nxt.value
-        if args.profile == "step":
+        if args.profile == "prefill":
+            ids = np.random.default_rng(1).integers(3, 100000, size=PROMPT).astype(np.uint32)
+            lib.plamo_cuda_reset_request(ctx, hm.ptr)
+            before = lib.plamo_cuda_kernel_launches(ctx)
+            t0 = be.info().gpu_seconds
+            assert lib.plamo_cuda_prefill_greedy(ctx, hm.ptr, ids.ctypes.data, PROMPT, ctypes.byref(nxt)) == 1
+            ms = (be.info().gpu_seconds - t0) * 1000
+        elif args.profile == "step":
             assert lib.plamo_cuda_time_decode(ctx, hm.ptr, 3) > 0
             before = lib.plamo_cuda_kernel_launches(ctx)
             ms = lib.plamo_cuda_time_decode(ctx, hm.ptr, 1)
@@ -861,7 +868,7 @@ def main():
     ap.add_argument("--no-tp", action="store_true",
                     help="at N > 1, skip the 31B tensor-parallel section of the line")
     ap.add_argument("--workload", choices=["8b-decode", "31b-tp"], default="8b-decode")
-    ap.add_argument("--profile", choices=["step", "batch", "gemv", "gemm"],
+    ap.add_argument("--profile", choices=["step", "prefill", "batch", "gemv", "gemm"],
                     help="run one small fixed workload for an ncu capture instead of the benchmark")
     ap.add_argument("--model", default="8b", help="profile of --profile step/batch")
     ap.add_argument("--requests", type=int, default=8, help="requests of --profile batch")

@@ -245,19 +245,26 @@ inline size_t attention_smem_bytes(uint64_t G, uint64_t D) {
 
 // ---------------------------------------------------------------------------
 // Prompt attention, blocked over queries (dim 128). attention_kernel stages
-// and rotates every key once per query token; here one CTA takes 64 query
-// rows (64/G consecutive tokens x the G heads of one kv head) and every
-// staged, rotated key tile serves all of them, from registers:
+// and rotates every key once per query token; here every key of the layer is
+// rotated once (prompt_keys_kernel), and one CTA takes 64 query rows (64/G
+// consecutive tokens x the G heads of one kv head) so that every staged key
+// tile serves all of them, from registers:
+//   staging - rotated keys and values of the next tile are copied with
+//             cp.async (16-byte pieces) into the other half of a double
+//             buffer while the current tile is computed;
 //   scores  - each thread 4 rows x 2 keys, Q transposed in shared memory
-//             (one 128-bit load per 4 rows), keys in padded rows;
+//             (one 128-bit load per 4 rows and dim), keys read as 128-bit
+//             words of four dims (rows padded to 132 floats: the 8 threads of
+//             a quarter warp cover all 32 banks);
 //   softmax - row max by shuffles over the 16 threads of a row group, the
 //             reference exp per element, row sums sequential in key order;
 //   values  - each thread 8 rows x 4 dims, acc *= correction then sequential
 //             FMA over the tile's keys.
 // The arithmetic is attention_kernel's with one split, operation for
-// operation: 32-key tiles from the window start, sequential FMA dots over dim
-// times 1/sqrt(dim), running max, l = l*c + e in key order, acc = acc*c then
-// FMA in key order, out = acc / l. Keys past a row's causal end enter as
+// operation: keys rotated with the same products and roundings, 32-key tiles
+// from the window start, sequential FMA dots over dim (dim 0 first) times
+// 1/sqrt(dim), running max, l = l*c + e in key order, acc = acc*c then FMA in
+// key order, out = acc / l. Keys past a row's causal end enter as
 // exp(-inf) = 0, which leaves l, the max and acc unchanged, so every output
 // is bit-identical to attention_kernel's and independent of how the prompt is
 // batched. All queries of one launch must share the window start 0 (full
@@ -268,44 +275,87 @@ constexpr int kPaRows = 64;             // query rows (token x head) per CTA
 constexpr int kPaTile = kAttnTile;      // keys per tile
 constexpr int kPaD = 128;
 constexpr int kPaQS = kPaRows + 4;      // transposed Q / P row stride (floats, 16-byte multiple)
-constexpr int kPaKS = kPaD + 1;         // padded key row: conflict-free column reads
+constexpr int kPaKS = kPaD + 4;         // padded key row (16-byte multiple, conflict-free 128-bit reads)
 
 struct PromptAttnParams {
     AttnLayer L;
-    const float *q;    // [tokens][qh][128], rotated
-    const float *qkv;  // new rows: K at qh*128, V at (qh+kh)*128 of each token row
-    float *out;        // [tokens][qh][128]
+    const float *q;     // [tokens][qh][128], rotated
+    const float *qkv;   // new rows: K at qh*128, V at (qh+kh)*128 of each token row
+    const float *rotk;  // [keys][kh*128] rotated keys of rows [0, P + tokens) (prompt_keys_kernel)
+    float *out;         // [tokens][qh][128]
     uint32_t qh, kh, qkv_stride;
     uint32_t tokens;     // queries [0, tokens) of this call
     uint32_t per_block;  // query tokens per CTA: 64 / G
 };
 
+// Keys [0, keys) of a layer whose window starts at row 0, each rotated at its
+// own row (cached rows from the ring, new rows from the normalised K of the
+// projection), with attention_kernel's in-tile products and roundings.
+__global__ void prompt_keys_kernel(AttnLayer L, const float *qkv, uint32_t qkv_stride, uint32_t qh, uint32_t kh,
+                                   float *rotk, uint32_t keys) {
+    constexpr uint32_t D = kPaD, half = kPaD / 2;
+    pdl_wait();
+    const uint64_t P = *L.appended;
+    const uint64_t kvw = static_cast<uint64_t>(kh) * D;
+    const uint64_t total = static_cast<uint64_t>(keys) * kh * half;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t d = static_cast<uint32_t>(i % half);
+        const uint64_t rest = i / half, key = rest / kh, h = rest % kh;
+        const float *src = key < P ? L.ring_k + (key % L.ring) * kvw + h * D
+                                   : qkv + (key - P) * qkv_stride + static_cast<uint64_t>(qh) * D + h * D;
+        const float *c = L.table + key * D, *s = c + half;
+        const float a = src[d], b = src[d + half];
+        float *o = rotk + key * kvw + h * D;
+        o[d] = __fsub_rn(__fmul_rn(a, c[d]), __fmul_rn(b, s[d]));
+        o[d + half] = __fadd_rn(__fmul_rn(b, c[d]), __fmul_rn(a, s[d]));
+    }
+    pdl_launch_dependents();
+}
+
 inline size_t prompt_attention_smem_bytes() {
-    return (kPaD * kPaQS + kPaTile * kPaKS + kPaTile * kPaD + kPaTile * kPaQS + 2 * kPaRows) * sizeof(float);
+    return (kPaD * kPaQS + 2 * kPaTile * kPaKS + 2 * kPaTile * kPaD + kPaTile * kPaQS + 2 * kPaRows) *
+           sizeof(float);
 }
 
 __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttnParams p) {
     extern __shared__ __align__(16) float sm[];
-    float *qT = sm;                       // [128][kPaQS]  Q rows, transposed
-    float *kt = qT + kPaD * kPaQS;        // [tile][kPaKS] rotated keys
-    float *vt = kt + kPaTile * kPaKS;     // [tile][128]   values
-    float *pT = vt + kPaTile * kPaD;      // [tile][kPaQS] exp(score - max), transposed
-    float *corr = pT + kPaTile * kPaQS;   // [64] per-row correction of the tile
-    float *lsum = corr + kPaRows;         // [64] final row sums
-    constexpr uint32_t D = kPaD, half = kPaD / 2;
+    float *qT = sm;                        // [128][kPaQS]  Q rows, transposed
+    float *kt = qT + kPaD * kPaQS;         // [2][tile][kPaKS] rotated keys (double buffer)
+    float *vt = kt + 2 * kPaTile * kPaKS;  // [2][tile][128]   values
+    float *pT = vt + 2 * kPaTile * kPaD;   // [tile][kPaQS] exp(score - max), transposed
+    float *corr = pT + kPaTile * kPaQS;    // [64] per-row correction of the tile
+    float *lsum = corr + kPaRows;          // [64] final row sums
+    constexpr uint32_t D = kPaD;
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = p.qh / p.kh, BQ = p.per_block;
     const uint32_t kh = blockIdx.y;
     const uint32_t t0 = (gridDim.x - 1 - blockIdx.x) * BQ;  // latest (longest) blocks start first
     const uint32_t tq = min(BQ, p.tokens - t0), vrows = tq * G;
-    const uint32_t kvw = p.kh * D;
+    const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(D)));
     const float ninf = -__int_as_float(0x7f800000);
 
     pdl_wait();
     const uint32_t P = static_cast<uint32_t>(*p.L.appended);
-    const uint32_t ring = static_cast<uint32_t>(p.L.ring);
+    const uint64_t ring = p.L.ring;
     const uint32_t hi_max = P + t0 + tq;  // keys [0, hi_max)
+
+    // Asynchronous copy of the rotated keys and the values of one tile.
+    auto stage = [&](uint32_t base, uint32_t buf) {
+        const uint32_t trow = min(static_cast<uint32_t>(kPaTile), hi_max - base);
+        float *ktb = kt + buf * (kPaTile * kPaKS), *vtb = vt + buf * (kPaTile * kPaD);
+        for (uint32_t i = tid; i < trow * (D / 4); i += kPaThreads) {
+            const uint32_t r = i / (D / 4), c = (i - r * (D / 4)) * 4, key = base + r;
+            cp_async16(ktb + r * kPaKS + c, p.rotk + key * kvw + kh * D + c);
+            const float *vsrc = key < P ? p.L.ring_v + (key % ring) * kvw + kh * D
+                                        : p.qkv + static_cast<size_t>(key - P) * p.qkv_stride + (p.qh + p.kh) * D +
+                                              kh * D;
+            cp_async16(vtb + r * D + c, vsrc + c);
+        }
+        cp_async_commit();
+    };
+    stage(0, 0);
 
     for (uint32_t i = tid; i < kPaRows * D; i += kPaThreads) {
         const uint32_t r = i / D, d = i - r * D;
@@ -332,42 +382,39 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
     for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
     float l = 0.0f;  // row `tid` (tid < 64)
 
-    for (uint32_t base = 0; base < hi_max; base += kPaTile) {
+    uint32_t buf = 0;
+    for (uint32_t base = 0; base < hi_max; base += kPaTile, buf ^= 1u) {
         const uint32_t trow = min(static_cast<uint32_t>(kPaTile), hi_max - base);
-        for (uint32_t i = tid; i < trow * half; i += kPaThreads) {
-            const uint32_t r = i / half, d = i - r * half, key = base + r;
-            const float *ksrc = key < P ? p.L.ring_k + static_cast<size_t>(key % ring) * kvw + kh * D
-                                        : p.qkv + static_cast<size_t>(key - P) * p.qkv_stride + p.qh * D + kh * D;
-            const float *c = p.L.table + static_cast<size_t>(key) * D, *s = c + half;
-            const float a = ksrc[d], b = ksrc[d + half];
-            kt[r * kPaKS + d] = __fsub_rn(__fmul_rn(a, c[d]), __fmul_rn(b, s[d]));
-            kt[r * kPaKS + d + half] = __fadd_rn(__fmul_rn(b, c[d]), __fmul_rn(a, s[d]));
-        }
-        for (uint32_t i = tid; i < trow * (D / 4); i += kPaThreads) {
-            const uint32_t r = i / (D / 4), c4 = i - r * (D / 4), key = base + r;
-            const float *vsrc = key < P
-                                    ? p.L.ring_v + static_cast<size_t>(key % ring) * kvw + kh * D
-                                    : p.qkv + static_cast<size_t>(key - P) * p.qkv_stride + (p.qh + p.kh) * D + kh * D;
-            *reinterpret_cast<float4 *>(vt + r * D + c4 * 4) = ld4(vsrc + c4 * 4);
+        if (base + kPaTile < hi_max) {
+            stage(base + kPaTile, buf ^ 1u);  // that half was released by the last iteration's barrier
+            cp_async_wait_one();
+        } else {
+            cp_async_wait_all();
         }
         __syncthreads();
+        const float *ktb = kt + buf * (kPaTile * kPaKS), *vtb = vt + buf * (kPaTile * kPaD);
 
         float s[4][2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
-        const float *k0 = kt + tx * kPaKS, *k1 = kt + (tx + 16) * kPaKS;
-#pragma unroll 8
-        for (uint32_t d = 0; d < D; ++d) {
-            const float4 q = *reinterpret_cast<const float4 *>(qT + d * kPaQS + ty * 4);
-            const float a = k0[d], b = k1[d];
-            s[0][0] = fmaf(q.x, a, s[0][0]);
-            s[1][0] = fmaf(q.y, a, s[1][0]);
-            s[2][0] = fmaf(q.z, a, s[2][0]);
-            s[3][0] = fmaf(q.w, a, s[3][0]);
-            s[0][1] = fmaf(q.x, b, s[0][1]);
-            s[1][1] = fmaf(q.y, b, s[1][1]);
-            s[2][1] = fmaf(q.z, b, s[2][1]);
-            s[3][1] = fmaf(q.w, b, s[3][1]);
+        const float *k0 = ktb + tx * kPaKS, *k1 = ktb + (tx + 16) * kPaKS;
+#pragma unroll 2
+        for (uint32_t d = 0; d < D; d += 4) {
+            const float4 a4 = *reinterpret_cast<const float4 *>(k0 + d);
+            const float4 b4 = *reinterpret_cast<const float4 *>(k1 + d);
+            const float ka[4] = {a4.x, a4.y, a4.z, a4.w}, kb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float4 q = *reinterpret_cast<const float4 *>(qT + (d + e) * kPaQS + ty * 4);
+                s[0][0] = fmaf(q.x, ka[e], s[0][0]);
+                s[1][0] = fmaf(q.y, ka[e], s[1][0]);
+                s[2][0] = fmaf(q.z, ka[e], s[2][0]);
+                s[3][0] = fmaf(q.w, ka[e], s[3][0]);
+                s[0][1] = fmaf(q.x, kb[e], s[0][1]);
+                s[1][1] = fmaf(q.y, kb[e], s[1][1]);
+                s[2][1] = fmaf(q.z, kb[e], s[2][1]);
+                s[3][1] = fmaf(q.w, kb[e], s[3][1]);
+            }
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -401,7 +448,7 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
             acc[i][3] = __fmul_rn(acc[i][3], c);
         }
         for (uint32_t r = 0; r < trow; ++r) {
-            const float4 v = *reinterpret_cast<const float4 *>(vt + r * D + lane * 4);
+            const float4 v = *reinterpret_cast<const float4 *>(vtb + r * D + lane * 4);
             const float4 pa = *reinterpret_cast<const float4 *>(pT + r * kPaQS + warp * 8);
             const float4 pb = *reinterpret_cast<const float4 *>(pT + r * kPaQS + warp * 8 + 4);
             const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};

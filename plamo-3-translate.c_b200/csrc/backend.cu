@@ -110,6 +110,7 @@ struct DModel {
     // prompt / verification
     uint64_t tmax;
     float *p_states, *p_norm, *p_qkv, *p_q, *p_attn, *p_branch, *p_gu, *p_logits, *p_part;
+    float *p_rotk;  // rotated keys of the blocked prompt attention [max capacity][KVW]
     uint32_t *p_ids, *p_next, *p_tickets;
     uint16_t *p_split;  // BF16 hi/mid/lo terms of a projection input, 3 x [T][K]
     float *p_splitk;    // split-K partial tiles of small-token projections
@@ -1217,10 +1218,19 @@ bool prompt_attention(plamo_cuda *c, DModel *m, uint64_t l, uint64_t T, size_t a
     if (c->prompt_attn && T >= 16 && m->D == kPaD && G <= kPaRows)
         blocked = L.sliding ? (L.capacity > L.appended ? std::min(T, L.capacity - L.appended) : 0) : T;
     if (blocked) {
+        // Every key the blocked queries see, rotated once: rows [0, P + blocked).
+        const uint64_t keys = L.appended + blocked;
+        const uint32_t kgrid = static_cast<uint32_t>(
+            std::min<uint64_t>((keys * m->KH * (kPaD / 2) + 255) / 256, static_cast<uint64_t>(c->sm_count) * 8));
+        if (!launch(c, prompt_keys_kernel, dim3(kgrid), dim3(256), 0, al, static_cast<const float *>(m->p_qkv),
+                    static_cast<uint32_t>(m->QW), static_cast<uint32_t>(m->QH), static_cast<uint32_t>(m->KH),
+                    m->p_rotk, static_cast<uint32_t>(keys)))
+            return false;
         const uint32_t per_block = static_cast<uint32_t>(kPaRows / G);
         PromptAttnParams pp{al,
                             m->p_q,
                             m->p_qkv,
+                            m->p_rotk,
                             m->p_attn,
                             static_cast<uint32_t>(m->QH),
                             static_cast<uint32_t>(m->KH),
@@ -1719,6 +1729,9 @@ static int prepare_impl(struct plamo_cuda *c, struct model *model, uint64_t head
     m->p_logits = static_cast<float *>(dalloc(c, m.get(), kVerifyMax * m->Vh * 4));
     m->p_part = static_cast<float *>(dalloc(c, m.get(), kVerifyMax * m->QH * m->splits * (m->D + 2) * 4));
     m->p_tickets = static_cast<uint32_t *>(dalloc(c, m.get(), T * m->KH * 4));
+    uint64_t rot_rows = 0;
+    for (const DLayer &L : m->layers) rot_rows = std::max(rot_rows, L.capacity);
+    m->p_rotk = static_cast<float *>(dalloc(c, m.get(), rot_rows * m->KVW * 4));
     m->p_ids = static_cast<uint32_t *>(dalloc(c, m.get(), T * 4));
     m->p_next = static_cast<uint32_t *>(dalloc(c, m.get(), kVerifyMax * 4));
     m->v_kv = static_cast<float *>(dalloc(c, m.get(), m->L * kVerifyMax * 2 * m->KVW * 4));
