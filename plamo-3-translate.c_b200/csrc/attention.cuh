@@ -271,10 +271,9 @@ inline size_t attention_smem_bytes(uint64_t G, uint64_t D) {
 // layers, or sliding layers whose window is not yet full); the host sends the
 // other queries of a sliding layer to attention_kernel.
 constexpr int kPaThreads = 256;
-constexpr int kPaRows = 64;             // query rows (token x head) per CTA
+constexpr int kPaRows = 64;             // query rows (token x head) per CTA, at most
 constexpr int kPaTile = kAttnTile;      // keys per tile
 constexpr int kPaD = 128;
-constexpr int kPaQS = kPaRows + 4;      // transposed Q / P row stride (floats, 16-byte multiple)
 constexpr int kPaKS = kPaD + 4;         // padded key row (16-byte multiple, conflict-free 128-bit reads)
 
 struct PromptAttnParams {
@@ -285,7 +284,7 @@ struct PromptAttnParams {
     float *out;         // [tokens][qh][128]
     uint32_t qh, kh, qkv_stride;
     uint32_t tokens;     // queries [0, tokens) of this call
-    uint32_t per_block;  // query tokens per CTA: 64 / G
+    uint32_t per_block;  // query tokens per CTA: rows per CTA / G
 };
 
 // Keys [0, keys) of a layer whose window starts at row 0, each rotated at its
@@ -313,19 +312,29 @@ __global__ void prompt_keys_kernel(AttnLayer L, const float *qkv, uint32_t qkv_s
     pdl_launch_dependents();
 }
 
-inline size_t prompt_attention_smem_bytes() {
-    return (kPaD * kPaQS + 2 * kPaTile * kPaKS + 2 * kPaTile * kPaD + kPaTile * kPaQS + 2 * kPaRows) *
+// Shared memory of a CTA of ROWS query rows.
+template <int ROWS>
+constexpr size_t prompt_attention_smem_bytes() {
+    return (kPaD * (ROWS + 4) + 2 * kPaTile * kPaKS + 2 * kPaTile * kPaD + kPaTile * (ROWS + 4) + 2 * ROWS) *
            sizeof(float);
 }
 
+// ROWS query rows per CTA (64, or 32 for short prompts: twice the CTAs,
+// half the work per key tile, so the longest blocks finish sooner). Every
+// row's operations are the same for either ROWS.
+template <int ROWS>
 __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttnParams p) {
+    static_assert(ROWS == 64 || ROWS == 32, "64 or 32 query rows per CTA");
+    constexpr int QS = ROWS + 4;       // transposed Q / P row stride (16-byte multiple)
+    constexpr int RT = ROWS / 16;      // score phase: rows per thread (16 row groups)
+    constexpr int RW = ROWS / 8;       // value phase: rows per warp (8 warps)
     extern __shared__ __align__(16) float sm[];
-    float *qT = sm;                        // [128][kPaQS]  Q rows, transposed
-    float *kt = qT + kPaD * kPaQS;         // [2][tile][kPaKS] rotated keys (double buffer)
+    float *qT = sm;                        // [128][QS]  Q rows, transposed
+    float *kt = qT + kPaD * QS;            // [2][tile][kPaKS] rotated keys (double buffer)
     float *vt = kt + 2 * kPaTile * kPaKS;  // [2][tile][128]   values
-    float *pT = vt + 2 * kPaTile * kPaD;   // [tile][kPaQS] exp(score - max), transposed
-    float *corr = pT + kPaTile * kPaQS;    // [64] per-row correction of the tile
-    float *lsum = corr + kPaRows;          // [64] final row sums
+    float *pT = vt + 2 * kPaTile * kPaD;   // [tile][QS] exp(score - max), transposed
+    float *corr = pT + kPaTile * QS;       // [ROWS] per-row correction of the tile
+    float *lsum = corr + ROWS;             // [ROWS] final row sums
     constexpr uint32_t D = kPaD;
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = p.qh / p.kh, BQ = p.per_block;
@@ -357,30 +366,32 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
     };
     stage(0, 0);
 
-    for (uint32_t i = tid; i < kPaRows * D; i += kPaThreads) {
+    for (uint32_t i = tid; i < ROWS * D; i += kPaThreads) {
         const uint32_t r = i / D, d = i - r * D;
         float v = 0.0f;
         if (r < vrows) {
             const uint32_t qi = r / G, g = r - qi * G;
             v = p.q[(static_cast<size_t>(t0 + qi) * p.qh + kh * G + g) * D + d];
         }
-        qT[d * kPaQS + r] = v;
+        qT[d * QS + r] = v;
     }
 
-    // Score-phase roles: rows ty*4 .. ty*4+3, keys tx and tx+16.
+    // Score-phase roles: rows ty*RT .. ty*RT+RT-1, keys tx and tx+16.
     const uint32_t ty = tid >> 4, tx = tid & 15;
-    uint32_t hi[4];
+    uint32_t hi[RT];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t r = ty * 4 + i;
+    for (int i = 0; i < RT; ++i) {
+        const uint32_t r = ty * RT + i;
         hi[i] = r < vrows ? P + t0 + r / G + 1 : 0;
     }
-    float mrow[4] = {ninf, ninf, ninf, ninf};
-    // Value-phase roles: rows warp*8 .. warp*8+7, dims lane*4 .. lane*4+3.
-    float acc[8][4];
+    float mrow[RT];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-    float l = 0.0f;  // row `tid` (tid < 64)
+    for (int i = 0; i < RT; ++i) mrow[i] = ninf;
+    // Value-phase roles: rows warp*RW .. warp*RW+RW-1, dims lane*4 .. lane*4+3.
+    float acc[RW][4];
+#pragma unroll
+    for (int i = 0; i < RW; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+    float l = 0.0f;  // row `tid` (tid < ROWS)
 
     uint32_t buf = 0;
     for (uint32_t base = 0; base < hi_max; base += kPaTile, buf ^= 1u) {
@@ -394,9 +405,9 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
         __syncthreads();
         const float *ktb = kt + buf * (kPaTile * kPaKS), *vtb = vt + buf * (kPaTile * kPaD);
 
-        float s[4][2];
+        float s[RT][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) s[i][0] = s[i][1] = 0.0f;
+        for (int i = 0; i < RT; ++i) s[i][0] = s[i][1] = 0.0f;
         const float *k0 = ktb + tx * kPaKS, *k1 = ktb + (tx + 16) * kPaKS;
 #pragma unroll 2
         for (uint32_t d = 0; d < D; d += 4) {
@@ -405,19 +416,27 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
             const float ka[4] = {a4.x, a4.y, a4.z, a4.w}, kb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float4 q = *reinterpret_cast<const float4 *>(qT + (d + e) * kPaQS + ty * 4);
-                s[0][0] = fmaf(q.x, ka[e], s[0][0]);
-                s[1][0] = fmaf(q.y, ka[e], s[1][0]);
-                s[2][0] = fmaf(q.z, ka[e], s[2][0]);
-                s[3][0] = fmaf(q.w, ka[e], s[3][0]);
-                s[0][1] = fmaf(q.x, kb[e], s[0][1]);
-                s[1][1] = fmaf(q.y, kb[e], s[1][1]);
-                s[2][1] = fmaf(q.z, kb[e], s[2][1]);
-                s[3][1] = fmaf(q.w, kb[e], s[3][1]);
+                float q[RT];
+                if constexpr (RT == 4) {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qT + (d + e) * QS + ty * 4);
+                    q[0] = q4.x;
+                    q[1] = q4.y;
+                    q[2] = q4.z;
+                    q[3] = q4.w;
+                } else {
+                    const float2 q2 = *reinterpret_cast<const float2 *>(qT + (d + e) * QS + ty * 2);
+                    q[0] = q2.x;
+                    q[1] = q2.y;
+                }
+#pragma unroll
+                for (int i = 0; i < RT; ++i) {
+                    s[i][0] = fmaf(q[i], ka[e], s[i][0]);
+                    s[i][1] = fmaf(q[i], kb[e], s[i][1]);
+                }
             }
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < RT; ++i) {
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const uint32_t key = base + tx + 16 * j;
@@ -429,19 +448,19 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
             m = fmaxf(mrow[i], m);
             const float c = plamo_exp(__fsub_rn(mrow[i], m));
             mrow[i] = m;
-            pT[tx * kPaQS + ty * 4 + i] = plamo_exp(__fsub_rn(s[i][0], m));
-            pT[(tx + 16) * kPaQS + ty * 4 + i] = plamo_exp(__fsub_rn(s[i][1], m));
-            if (tx == 0) corr[ty * 4 + i] = c;
+            pT[tx * QS + ty * RT + i] = plamo_exp(__fsub_rn(s[i][0], m));
+            pT[(tx + 16) * QS + ty * RT + i] = plamo_exp(__fsub_rn(s[i][1], m));
+            if (tx == 0) corr[ty * RT + i] = c;
         }
         __syncthreads();
 
-        if (tid < kPaRows) {
+        if (tid < ROWS) {
             l = __fmul_rn(l, corr[tid]);
-            for (uint32_t r = 0; r < trow; ++r) l = __fadd_rn(l, pT[r * kPaQS + tid]);
+            for (uint32_t r = 0; r < trow; ++r) l = __fadd_rn(l, pT[r * QS + tid]);
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float c = corr[warp * 8 + i];
+        for (int i = 0; i < RW; ++i) {
+            const float c = corr[warp * RW + i];
             acc[i][0] = __fmul_rn(acc[i][0], c);
             acc[i][1] = __fmul_rn(acc[i][1], c);
             acc[i][2] = __fmul_rn(acc[i][2], c);
@@ -449,11 +468,17 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
         }
         for (uint32_t r = 0; r < trow; ++r) {
             const float4 v = *reinterpret_cast<const float4 *>(vtb + r * D + lane * 4);
-            const float4 pa = *reinterpret_cast<const float4 *>(pT + r * kPaQS + warp * 8);
-            const float4 pb = *reinterpret_cast<const float4 *>(pT + r * kPaQS + warp * 8 + 4);
-            const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+            float pr[RW];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int h = 0; h < RW; h += 4) {
+                const float4 p4 = *reinterpret_cast<const float4 *>(pT + r * QS + warp * RW + h);
+                pr[h] = p4.x;
+                pr[h + 1] = p4.y;
+                pr[h + 2] = p4.z;
+                pr[h + 3] = p4.w;
+            }
+#pragma unroll
+            for (int i = 0; i < RW; ++i) {
                 acc[i][0] = fmaf(pr[i], v.x, acc[i][0]);
                 acc[i][1] = fmaf(pr[i], v.y, acc[i][1]);
                 acc[i][2] = fmaf(pr[i], v.z, acc[i][2]);
@@ -463,11 +488,11 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
         __syncthreads();
     }
 
-    if (tid < kPaRows) lsum[tid] = l;
+    if (tid < ROWS) lsum[tid] = l;
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint32_t r = warp * 8 + i;
+    for (int i = 0; i < RW; ++i) {
+        const uint32_t r = warp * RW + i;
         if (r >= vrows) continue;
         const uint32_t qi = r / G, g = r - qi * G;
         const float inv = lsum[r];

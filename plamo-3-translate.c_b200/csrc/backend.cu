@@ -161,6 +161,7 @@ struct plamo_cuda {
     unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
     bool tc_gemm;
     bool prompt_attn;  // blocked prompt attention (PLAMO_CUDA_PROMPT_ATTN=0 disables)
+    int prompt_rows;   // its query rows per CTA: 64, 32, or 0 to choose by size (PLAMO_CUDA_PROMPT_ROWS)
     bool persistent;   // one-launch decode step where the shapes allow (opt-in: PLAMO_CUDA_PERSISTENT=1)
     bool cooperative;  // the device supports cooperative launches
     uint32_t pt_piece;  // bytes per bulk copy of the persistent step (PLAMO_CUDA_PT_PIECE_KB)
@@ -1226,7 +1227,12 @@ bool prompt_attention(plamo_cuda *c, DModel *m, uint64_t l, uint64_t T, size_t a
                     static_cast<uint32_t>(m->QW), static_cast<uint32_t>(m->QH), static_cast<uint32_t>(m->KH),
                     m->p_rotk, static_cast<uint32_t>(keys)))
             return false;
-        const uint32_t per_block = static_cast<uint32_t>(kPaRows / G);
+        // 32 query rows per CTA while 64-row blocks would not fill two waves
+        // of two CTAs per SM (the longest blocks would set the launch time).
+        const bool narrow = G <= 32 && (c->prompt_rows ? c->prompt_rows == 32
+                                                       : ((blocked + kPaRows / G - 1) / (kPaRows / G)) * m->KH <
+                                                             4ull * static_cast<uint64_t>(c->sm_count));
+        const uint32_t per_block = static_cast<uint32_t>((narrow ? 32 : kPaRows) / G);
         PromptAttnParams pp{al,
                             m->p_q,
                             m->p_qkv,
@@ -1238,7 +1244,10 @@ bool prompt_attention(plamo_cuda *c, DModel *m, uint64_t l, uint64_t T, size_t a
                             static_cast<uint32_t>(blocked),
                             per_block};
         const dim3 grid(static_cast<uint32_t>((blocked + per_block - 1) / per_block), static_cast<uint32_t>(m->KH));
-        if (!launch(c, prompt_attention_kernel, grid, dim3(kPaThreads), prompt_attention_smem_bytes(), pp))
+        if (!(narrow ? launch(c, prompt_attention_kernel<32>, grid, dim3(kPaThreads),
+                              prompt_attention_smem_bytes<32>(), pp)
+                     : launch(c, prompt_attention_kernel<64>, grid, dim3(kPaThreads),
+                              prompt_attention_smem_bytes<64>(), pp)))
             return false;
     }
     if (blocked == T) return true;
@@ -1410,6 +1419,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_gemm = !tc || strcmp(tc, "0");
     const char *pa = getenv("PLAMO_CUDA_PROMPT_ATTN");
     c->prompt_attn = !pa || strcmp(pa, "0");
+    const char *prow = getenv("PLAMO_CUDA_PROMPT_ROWS");
+    c->prompt_rows = prow && (atoi(prow) == 32 || atoi(prow) == 64) ? atoi(prow) : 0;
     // The one-launch step is opt-in: on the 8B profile it measured 4.8 ms per
     // token against 3.38 ms for the graph (its per-phase grid barriers and
     // prologues cost more than the graph's programmatic launch boundaries).
@@ -1476,7 +1487,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     set_gemv_smem_limits<PRO_RESID_NORM_TP, EPI_ARGMAX>(optin, carveout);
     set_gemv_smem_limits<PRO_NORM, EPI_ARGMAX>(optin, carveout);
     allow_smem(attention_kernel, optin, carveout);
-    allow_smem(prompt_attention_kernel, optin, carveout);
+    allow_smem(prompt_attention_kernel<64>, optin, carveout);
+    allow_smem(prompt_attention_kernel<32>, optin, carveout);
     allow_smem(decode_attention128_kernel, optin, carveout);
     allow_smem(gemm_tc_kernel<16>, optin, carveout);
     allow_smem(gemm_tc_kernel<32>, optin, carveout);

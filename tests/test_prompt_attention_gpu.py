@@ -3,9 +3,10 @@
 From 16 prompt tokens on, the backend sends queries whose window starts at row
 0 to a kernel that serves 64 query rows per CTA from each staged key tile; the
 others (a sliding layer whose window has filled) stay on the per-token kernel.
-Both must give the same bits: the blocked kernel performs the same operations
-in the same order, so a prefill with it disabled (PLAMO_CUDA_PROMPT_ATTN=0)
-must reproduce every prompt state and every KV row exactly. The cases cover
+Both must give the same bits, at 64 and at 32 query rows per CTA: the blocked
+kernel performs the same operations in the same order, so a prefill with it
+disabled (PLAMO_CUDA_PROMPT_ATTN=0) must reproduce every prompt state and
+every KV row exactly. The cases cover
 the grouped-query ratios of the profiles (G = 2, 6, 8, 16), a prompt longer
 than a sliding window (split between the kernels inside one launch pair), and
 a second prompt chunk that continues from cached rows.
@@ -20,11 +21,15 @@ from conftest import expect
 pytestmark = pytest.mark.gpu
 
 
-def run(pkg, monkeypatch, prof, chunks, blocked):
+def run(pkg, monkeypatch, prof, chunks, blocked, rows=None):
     if blocked:
         monkeypatch.delenv("PLAMO_CUDA_PROMPT_ATTN", raising=False)
     else:
         monkeypatch.setenv("PLAMO_CUDA_PROMPT_ATTN", "0")
+    if rows:
+        monkeypatch.setenv("PLAMO_CUDA_PROMPT_ROWS", str(rows))
+    else:
+        monkeypatch.delenv("PLAMO_CUDA_PROMPT_ROWS", raising=False)
     b = pkg.Backend(device=0, max_context=1024, max_prefill=512)
     try:
         hm = pkg.HostModel(prof, weights="synthetic")
@@ -52,11 +57,13 @@ def run(pkg, monkeypatch, prof, chunks, blocked):
     (16, 1, 64, (30, 50)),    # G 16: second chunk continues at row 30, window fills at 64
     (4, 2, 16, (20, 17)),     # G 2: the second chunk's sliding queries all per token
 ])
-def test_blocked_prompt_attention_matches_per_token_kernel(pkg, monkeypatch, qh, kh, window, chunks):
+@pytest.mark.parametrize("rows", [64, 32])
+def test_blocked_prompt_attention_matches_per_token_kernel(pkg, monkeypatch, qh, kh, window, chunks, rows):
+    """Both block heights (64 query rows per CTA, and 32 for short prompts)."""
     prof = pkg.Profile("attn", 512, 2, qh, kh, 128, 256, vocab=500, window=window, pattern=2,
                        max_position=1024)
     want = run(pkg, monkeypatch, prof, chunks, blocked=False)
-    got = run(pkg, monkeypatch, prof, chunks, blocked=True)
+    got = run(pkg, monkeypatch, prof, chunks, blocked=True, rows=rows)
     for c, (a, b) in enumerate(zip(got[0], want[0])):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), \
             f"chunk {c} states: max |d| {np.max(np.abs(a - b))}"
