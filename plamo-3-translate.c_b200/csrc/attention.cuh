@@ -77,6 +77,55 @@ __global__ void qk_prep_kernel(float *qkv, float *q_out, AttnLayer L, AttnShape 
     pdl_launch_dependents();
 }
 
+// Head dim 128: one warp per head, eight heads per CTA, with the decode
+// attention kernel's lane layout and reduction order, so prompt and decode
+// normalise (and rotate) Q and K to the same bits: a Q head's lanes l < 16
+// hold dims 4l..4l+3 and 64+4l..64+4l+3; a K head's 32 lanes hold 4l..4l+3.
+__global__ void __launch_bounds__(256) qk_prep128_kernel(float *qkv, float *q_out, AttnLayer L, AttnShape S) {
+    constexpr uint32_t D = 128, H = 64;
+    pdl_wait();
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t head = static_cast<uint64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5), t = blockIdx.y;
+    if (head < S.qh) {
+        const float *x = qkv + t * S.qkv_stride + head * D;
+        const uint64_t P = *L.appended;
+        const float *table = L.table + (P + t - window_start(L, P, t)) * D;
+        float4 a = make_float4(0, 0, 0, 0), b = a, c = a, sn = a;
+        uint2 wa = make_uint2(0, 0), wb = wa;
+        if (lane < 16) {
+            a = ld4(x + 4 * lane);
+            b = ld4(x + H + 4 * lane);
+            wa = *reinterpret_cast<const uint2 *>(L.qn + 4 * lane);
+            wb = *reinterpret_cast<const uint2 *>(L.qn + H + 4 * lane);
+            c = ld4(table + 4 * lane);
+            sn = ld4(table + H + 4 * lane);
+        }
+        const float inv = rms_inverse(warp_sum(sq4(a) + sq4(b)), D);
+        if (lane < 16) {
+            const float4 qa = apply4(a, inv, norm4(wa, 1.0f)), qb = apply4(b, inv, norm4(wb, 1.0f));
+            float4 lo4, hi4;
+            lo4.x = __fsub_rn(__fmul_rn(qa.x, c.x), __fmul_rn(qb.x, sn.x));
+            lo4.y = __fsub_rn(__fmul_rn(qa.y, c.y), __fmul_rn(qb.y, sn.y));
+            lo4.z = __fsub_rn(__fmul_rn(qa.z, c.z), __fmul_rn(qb.z, sn.z));
+            lo4.w = __fsub_rn(__fmul_rn(qa.w, c.w), __fmul_rn(qb.w, sn.w));
+            hi4.x = __fadd_rn(__fmul_rn(qb.x, c.x), __fmul_rn(qa.x, sn.x));
+            hi4.y = __fadd_rn(__fmul_rn(qb.y, c.y), __fmul_rn(qa.y, sn.y));
+            hi4.z = __fadd_rn(__fmul_rn(qb.z, c.z), __fmul_rn(qa.z, sn.z));
+            hi4.w = __fadd_rn(__fmul_rn(qb.w, c.w), __fmul_rn(qa.w, sn.w));
+            float *o = q_out + (t * S.qh + head) * D;
+            *reinterpret_cast<float4 *>(o + 4 * lane) = lo4;
+            *reinterpret_cast<float4 *>(o + H + 4 * lane) = hi4;
+        }
+    } else if (head < S.qh + S.kh) {
+        float *x = qkv + t * S.qkv_stride + head * D;
+        const float4 xk = ld4(x + 4 * lane);
+        const uint2 wk = *reinterpret_cast<const uint2 *>(L.kn + 4 * lane);
+        const float inv = rms_inverse(warp_sum(sq4(xk)), D);
+        *reinterpret_cast<float4 *>(x + 4 * lane) = apply4(xk, inv, norm4(wk, 1.0f));
+    }
+    pdl_launch_dependents();
+}
+
 constexpr int kAttnThreads = 128;
 constexpr int kAttnTile = 32;
 

@@ -445,6 +445,15 @@ bool gemv(plamo_cuda *c, GemvParams p, uint32_t *grid_out = nullptr) {
     return launch_gemv_shape<PRO, EPI>(c, p, U, grid, smem);
 }
 
+// SwiGLU of T rows of [gate | up] in place (and the split terms of `f`).
+bool swiglu_rows(plamo_cuda *c, float *gu, uint64_t I, uint64_t T, const RowFuse &f) {
+    if (I % 4 == 0)
+        return launch(c, swiglu_rows4_kernel, dim3(static_cast<uint32_t>((I / 4 + 255) / 256), static_cast<uint32_t>(T)),
+                      dim3(256), 0, gu, I, T, f);
+    return launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((I * T + 255) / 256, 4096)), dim3(256), 0, gu, I, T,
+                  f);
+}
+
 bool gemm(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t *W, float *Y, uint64_t ys,
           uint64_t T, uint64_t R, uint64_t K) {
     if (!T || !R) return true;
@@ -983,9 +992,7 @@ bool record_batch(plamo_cuda *c, plamo_cuda_batch *b, DModel *m) {
             return false;
         if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H, f.split != nullptr)) return false;
         f = row_fuse(c, m, L.down, T, H, m->I, Deferred{});
-        if (!launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((m->I * T + 255) / 256, 4096)), dim3(256), 0,
-                    m->p_gu, m->I, T, f))
-            return false;
+        if (!swiglu_rows(c, m->p_gu, m->I, T, f)) return false;
         if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I, f.split != nullptr,
                         &down_parts))
             return false;
@@ -1288,7 +1295,10 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
         if (!ok || !projection(c, m, m->p_norm, H, L.qkv_w, m->p_qkv, m->QW, T, m->QW, H, f.split != nullptr))
             return false;
         AttnLayer al = attn_layer(m, l);
-        if (!launch(c, qk_prep_kernel, dim3(m->QH + m->KH, T), dim3(128), 0, m->p_qkv, m->p_q, al, shape))
+        if (!(m->D == 128 ? launch(c, qk_prep128_kernel, dim3(static_cast<uint32_t>((m->QH + m->KH + 7) / 8), T),
+                                   dim3(256), 0, m->p_qkv, m->p_q, al, shape)
+                          : launch(c, qk_prep_kernel, dim3(m->QH + m->KH, T), dim3(128), 0, m->p_qkv, m->p_q, al,
+                                   shape)))
             return false;
         if (!prompt_attention(c, m, l, T, attn_smem)) return false;
         if (mode == 0) {
@@ -1314,9 +1324,7 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
             return false;
         if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H, f.split != nullptr)) return false;
         f = row_fuse(c, m, L.down, T, H, m->I, Deferred{});
-        if (!launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((m->I * T + 255) / 256, 4096)), dim3(256), 0,
-                    m->p_gu, m->I, T, f))
-            return false;
+        if (!swiglu_rows(c, m->p_gu, m->I, T, f)) return false;
         if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I, f.split != nullptr,
                         tp ? nullptr : &down_parts))
             return false;
@@ -2330,8 +2338,7 @@ int plamo_cuda_mlp(struct plamo_cuda *c, const struct mlp *p, float *states, uin
     ok = ok && launch(c, norm_rows_kernel<ROW_NORM>, dim3(T), dim3(512), 0, s, static_cast<const float *>(nullptr),
                       static_cast<const uint16_t *>(nullptr), 0.0f, pre, 1.0f, n, H, RowFuse{});
     ok = ok && projection_with(c, n, H, gu, g, 2 * I, T, 2 * I, H, split, err);
-    ok = ok && launch(c, swiglu_rows_kernel, dim3(std::min<uint64_t>((I * T + 255) / 256, 4096)), dim3(256), 0, g, I,
-                      T, RowFuse{});
+    ok = ok && swiglu_rows(c, g, I, T, RowFuse{});
     ok = ok && projection_with(c, g, 2 * I, down, b, H, T, H, I, split, err);
     ok = ok && launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(512), 0, s, static_cast<const float *>(b), post,
                       kPostMlpOffset, static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), H,

@@ -183,6 +183,21 @@ __global__ void norm_rows_kernel(float *states, const float *branch, const uint1
 
 // In place: gu[t][i] = swiglu(gu[t][i], gu[t][I + i]) (reference src/batch.s:22-45).
 // fuse.split: also the BF16 terms of the result, [3][tokens][inter].
+// Grid (inter / 1024 rounded up, tokens), 256 threads: four consecutive
+// units per thread (inter % 4 == 0), 128-bit loads and stores, no division.
+__global__ void swiglu_rows4_kernel(float *gu, uint64_t inter, uint64_t tokens, RowFuse fuse) {
+    pdl_wait();
+    const uint64_t t = blockIdx.y, i = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i < inter) {
+        float *row = gu + t * 2 * inter;
+        const float4 g = ld4(row + i), u = ld4(row + inter + i);
+        const float4 v = make_float4(swiglu(g.x, u.x), swiglu(g.y, u.y), swiglu(g.z, u.z), swiglu(g.w, u.w));
+        *reinterpret_cast<float4 *>(row + i) = v;
+        fuse_split4(fuse, inter * tokens, t * inter + i, v);
+    }
+    pdl_launch_dependents();
+}
+
 __global__ void swiglu_rows_kernel(float *gu, uint64_t inter, uint64_t tokens, RowFuse fuse) {
     pdl_wait();
     const uint64_t total = inter * tokens;
