@@ -826,13 +826,39 @@ def run_profile(args):
                        for _ in range((args.requests if args.profile == "batch" else 1) - 1)]
         nxt = ctypes.c_uint32()
         toks = np.zeros(len(reqs), dtype=np.uint32)
-        prompt = PROMPT if args.profile in ("step", "prefill") else 16
+        prompt = PROMPT if args.profile in ("step", "timeline", "prefill") else 16
         for i, r in enumerate(reqs):
             be.prepare(r)
             ids = np.random.default_rng(1 + i).integers(3, 100000, size=prompt).astype(np.uint32)
             assert lib.plamo_cuda_prefill_greedy(ctx, r.ptr, ids.ctypes.data, prompt, ctypes.byref(nxt)) == 1
             toks[i] = nxt.value
-        if args.profile == "prefill":
+        if args.profile == "timeline":
+            # Device timeline of one decode step of the graph path (the launch
+            # records of plamo_cuda_decode_trace), after three warm steps.
+            ids = np.random.default_rng(1).integers(3, 100000, size=PROMPT).astype(np.uint32)
+            lib.plamo_cuda_reset_request(ctx, hm.ptr)
+            assert lib.plamo_cuda_prefill_greedy(ctx, hm.ptr, ids.ctypes.data, PROMPT, ctypes.byref(nxt)) == 1
+            n = 6 * (5 * profile.layers + 1)
+            st = np.zeros(n, dtype=np.uint64)
+            before = lib.plamo_cuda_kernel_launches(ctx)
+            for k in range(4):
+                assert lib.plamo_cuda_decode_trace(ctx, hm.ptr, 5 + k, st.ctypes.data, n) == n, be.info().note
+            rel = (st.reshape(-1, 6).astype(np.int64) - int(st[0])) / 1000.0
+            kinds = ["qkv", "attention", "o_proj", "gate_up", "down"]
+            summary = {}
+            for j, kind in enumerate(kinds):
+                rows = [5 * l + j for l in range(1, profile.layers)]
+                summary[kind] = {
+                    "span_us": float(np.mean([rel[i, 3] - rel[i, 1] for i in rows])),
+                    "gap_us": float(np.mean([rel[i, 1] - rel[i - 1, 3] for i in rows])),
+                    "last_entry_us": float(np.mean([rel[i, 5] - rel[i - 1, 3] for i in rows])),
+                    "wait_passed_us": float(np.mean([rel[i, 4] - rel[i - 1, 3] for i in rows])),
+                    "prologue_us": float(np.mean([rel[i, 1] - rel[i, 4] for i in rows]))}
+            print(json.dumps({"timeline": summary, "step_us": float(rel[-1, 3]),
+                              "per_layer_us": float((rel[5 * (profile.layers - 1), 1] - rel[5, 1]) /
+                                                    (profile.layers - 2))}), flush=True)
+            ms = float(rel[-1, 3]) / 1000
+        elif args.profile == "prefill":
             ids = np.random.default_rng(1).integers(3, 100000, size=PROMPT).astype(np.uint32)
             lib.plamo_cuda_reset_request(ctx, hm.ptr)
             before = lib.plamo_cuda_kernel_launches(ctx)
@@ -868,7 +894,7 @@ def main():
     ap.add_argument("--no-tp", action="store_true",
                     help="at N > 1, skip the 31B tensor-parallel section of the line")
     ap.add_argument("--workload", choices=["8b-decode", "31b-tp"], default="8b-decode")
-    ap.add_argument("--profile", choices=["step", "prefill", "batch", "gemv", "gemm"],
+    ap.add_argument("--profile", choices=["step", "timeline", "prefill", "batch", "gemv", "gemm"],
                     help="run one small fixed workload for an ncu capture instead of the benchmark")
     ap.add_argument("--model", default="8b", help="profile of --profile step/batch")
     ap.add_argument("--requests", type=int, default=8, help="requests of --profile batch")
