@@ -44,6 +44,10 @@ struct plamo_cuda_info {
     uint64_t weight_bytes, kv_bytes, workspace_bytes, allocated_bytes;
     uint64_t sm_count;
     double gpu_seconds; /* device time of completed forward/prefill/verify calls */
+    /* KV page pool: pages mapped into requests' page tables, and pages
+       allocated in all (kv_bytes counts the latter); a page holds 64 rows of
+       keys and values of one layer. */
+    uint64_t kv_pages_used, kv_pages_allocated;
 };
 
 struct plamo_cuda;

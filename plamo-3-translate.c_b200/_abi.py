@@ -82,7 +82,7 @@ class CudaInfo(ctypes.Structure):
             "launches", "graph_launches", "forwards", "prefills", "verification_batches",
             "verified_tokens", "committed_tokens", "declines", "errors", "weight_bytes",
             "kv_bytes", "workspace_bytes", "allocated_bytes", "sm_count")] + [
-        ("gpu_seconds", c_double)]
+        ("gpu_seconds", c_double), ("kv_pages_used", c_uint64), ("kv_pages_allocated", c_uint64)]
 
 
 class CudaTiming(ctypes.Structure):

@@ -1,8 +1,11 @@
 // Q/K head norm + RoPE, GQA attention over the KV ring, KV ring stores.
 //
-// KV layout in HBM (per layer): two FP32 rings K[ring][kh*dim] and
-// V[ring][kh*dim] holding normalised, UNROTATED keys and values, exactly the
-// rows the reference keeps in struct cache (reference src/cache.s). Logical
+// KV layout in HBM (per layer): a ring of `ring` slots of normalised,
+// UNROTATED FP32 keys and values, exactly the rows the reference keeps in
+// struct cache (reference src/cache.s), stored in pages of kKvPageRows slots
+// taken from a page pool the backend shares between requests: the layer's
+// page table maps slot s to page pages[s / kKvPageRows], whose first half
+// holds the keys [kKvPageRows][kh*dim] and second half the values. Logical
 // row p (0-based count of rows appended in the request) lives in slot
 // p % ring. A sliding layer keeps the last `capacity` rows; instead of the
 // reference's shift-and-rerotate of the whole window on every eviction
@@ -24,9 +27,11 @@
 
 namespace plamo {
 
+constexpr uint64_t kKvPageRows = 64;
+
 struct AttnLayer {
-    const float *ring_k, *ring_v;  // [ring][kh*dim]
-    float *ring_k_w, *ring_v_w;    // same, writable (stores)
+    float *const *pages;           // page table: [ring / kKvPageRows] page bases ([2][kKvPageRows][kvw] floats)
+    uint64_t kvw;                  // floats per K (or V) row: kh*dim
     const uint64_t *appended;      // device counter: rows committed before this call
     uint64_t ring, capacity;
     int sliding;
@@ -39,6 +44,16 @@ struct AttnShape {
     uint64_t tokens, qh, kh, dim;
     uint64_t qkv_stride;  // floats between token rows of the QKV buffer
 };
+
+// The key and value rows of logical row `row` (slot row % ring).
+__device__ __forceinline__ float *kv_key(const AttnLayer &L, uint64_t row) {
+    const uint64_t s = row % L.ring;
+    return L.pages[s / kKvPageRows] + (s % kKvPageRows) * L.kvw;
+}
+__device__ __forceinline__ float *kv_value(const AttnLayer &L, uint64_t row) {
+    const uint64_t s = row % L.ring;
+    return L.pages[s / kKvPageRows] + (kKvPageRows + s % kKvPageRows) * L.kvw;
+}
 
 __device__ __forceinline__ uint64_t window_start(const AttnLayer &L, uint64_t P, uint64_t t) {
     if (!L.sliding) return 0;
@@ -168,7 +183,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     const uint64_t n = hi - lo;
     const uint64_t k0 = lo + n * split / p.splits, k1 = lo + n * (split + 1) / p.splits;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(D)));
-    const uint64_t kvw = KH * D;
 
     for (uint64_t i = threadIdx.x; i < G * D; i += blockDim.x) {
         const uint64_t g = i / D, d = i % D;
@@ -189,9 +203,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
             const uint64_t key = base + r;
             const float *ksrc, *vsrc;
             if (key < P) {
-                const uint64_t slot = key % p.L.ring;
-                ksrc = p.L.ring_k + slot * kvw + kh * D;
-                vsrc = p.L.ring_v + slot * kvw + kh * D;
+                ksrc = kv_key(p.L, key) + kh * D;
+                vsrc = kv_value(p.L, key) + kh * D;
             } else {
                 const float *row = p.qkv + (key - P) * p.S.qkv_stride;
                 ksrc = row + QH * D + kh * D;
@@ -350,7 +363,7 @@ __global__ void prompt_keys_kernel(AttnLayer L, const float *qkv, uint32_t qkv_s
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         const uint32_t d = static_cast<uint32_t>(i % half);
         const uint64_t rest = i / half, key = rest / kh, h = rest % kh;
-        const float *src = key < P ? L.ring_k + (key % L.ring) * kvw + h * D
+        const float *src = key < P ? kv_key(L, key) + h * D
                                    : qkv + (key - P) * qkv_stride + static_cast<uint64_t>(qh) * D + h * D;
         const float *c = L.table + key * D, *s = c + half;
         const float a = src[d], b = src[d + half];
@@ -396,7 +409,6 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
 
     pdl_wait();
     const uint32_t P = static_cast<uint32_t>(*p.L.appended);
-    const uint64_t ring = p.L.ring;
     const uint32_t hi_max = P + t0 + tq;  // keys [0, hi_max)
 
     // Asynchronous copy of the rotated keys and the values of one tile.
@@ -406,7 +418,7 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
         for (uint32_t i = tid; i < trow * (D / 4); i += kPaThreads) {
             const uint32_t r = i / (D / 4), c = (i - r * (D / 4)) * 4, key = base + r;
             cp_async16(ktb + r * kPaKS + c, p.rotk + key * kvw + kh * D + c);
-            const float *vsrc = key < P ? p.L.ring_v + (key % ring) * kvw + kh * D
+            const float *vsrc = key < P ? kv_value(p.L, key) + kh * D
                                         : p.qkv + static_cast<size_t>(key - P) * p.qkv_stride + (p.qh + p.kh) * D +
                                               kh * D;
             cp_async16(vtb + r * D + c, vsrc + c);
@@ -575,6 +587,7 @@ constexpr int kDecSplits = 8;
 // measured faster with 8 splits each (4.80 against 4.95 ms per 8-request
 // 8B step).
 constexpr int kDec128Splits = 16;
+constexpr uint32_t kDecPageCache = 64;  // page bases held in shared memory (rows 0..4095 of a ring)
 constexpr int kDec128BatchSplits = 8;
 
 struct DecodeAttnParams {
@@ -638,14 +651,30 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
 
     pdl_launch_dependents();  // the next projection may start streaming its weights
     // The committed rows and their counter were final before this step began
-    // (only the new row comes from the projection still in flight), so the
-    // first tile of old rows is requested before waiting for that projection.
+    // (only the new row comes from the projection still in flight), and so
+    // were the page table's entries, so the first tile of old rows is
+    // requested before waiting for that projection. The first pages' bases
+    // are read into shared memory alongside the counter, keeping the page
+    // lookups off the chain of dependent global loads.
+    __shared__ float *page_base[kDecPageCache];
+    const uint64_t npages = (p.L.ring + kKvPageRows - 1) / kKvPageRows;
+    if (threadIdx.x < kDecPageCache && threadIdx.x < npages)
+        page_base[threadIdx.x] =
+            reinterpret_cast<float *>(load_u64_keep(p.L.pages + threadIdx.x, evict_last_policy()));
     const uint64_t P = *p.L.appended;
     const uint64_t lo = window_start(p.L, P, 0);
     const uint32_t n = static_cast<uint32_t>(P + 1 - lo);
     const uint64_t k0 = lo + static_cast<uint64_t>(n) * split / S;
     const uint64_t k1 = lo + static_cast<uint64_t>(n) * (split + 1) / S;
-    const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
+    __syncthreads();
+    auto page_of = [&](uint64_t row, uint64_t half) -> float * {
+        const uint64_t slot = row % p.L.ring, pi = slot / kKvPageRows;
+        float *const base = pi < kDecPageCache ? page_base[pi] : p.L.pages[pi];
+        return base + (half * kKvPageRows + slot % kKvPageRows) * p.L.kvw + kh * D;
+    };
+    // Where this step's new row goes (its page was mapped before the launch).
+    float *const knew_dst = k1 == P + 1 ? page_of(P, 0) : nullptr;
+    float *const vnew_dst = k1 == P + 1 ? page_of(P, 1) : nullptr;
 
     // Asynchronous staging of one tile: 32 16-byte pieces per 512-byte row.
     auto stage = [&](uint64_t base, uint32_t rows) {
@@ -654,9 +683,8 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
             const uint64_t key = base + r;
             cp_async16(tab + r * D + c, p.L.table + (key - lo) * D + c);
             if (key < P) {
-                const uint64_t slot = key % p.L.ring;
-                cp_async16(kt + r * KS + c, p.L.ring_k + slot * kvw + kh * D + c);
-                cp_async16(vt + r * D + c, p.L.ring_v + slot * kvw + kh * D + c);
+                cp_async16(kt + r * KS + c, page_of(key, 0) + c);
+                cp_async16(vt + r * D + c, page_of(key, 1) + c);
             }
         }
         cp_async_commit();
@@ -712,11 +740,10 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
         const uint2 wk = *reinterpret_cast<const uint2 *>(p.L.kn + 4 * lane);
         const float inv = rms_inverse(warp_sum(sq4(xk)), D);
         const float4 k4 = apply4(xk, inv, norm4(wk, 1.0f));
-        const uint64_t slot = P % p.L.ring;
         *reinterpret_cast<float4 *>(knew + 4 * lane) = k4;
         *reinterpret_cast<float4 *>(vnew + 4 * lane) = xv;
-        *reinterpret_cast<float4 *>(p.L.ring_k_w + slot * kvw + kh * D + 4 * lane) = k4;
-        *reinterpret_cast<float4 *>(p.L.ring_v_w + slot * kvw + kh * D + 4 * lane) = xv;
+        *reinterpret_cast<float4 *>(knew_dst + 4 * lane) = k4;
+        *reinterpret_cast<float4 *>(vnew_dst + 4 * lane) = xv;
     }
     for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) acc[i] = 0.0f;
     for (uint32_t g = threadIdx.x; g < G; g += kDecThreads) {
@@ -926,14 +953,13 @@ __global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads
         float ss = 0.0f;
         for (uint32_t i = lane; i < D; i += 32) ss += x[i] * x[i];
         const float inv = rms_inverse(warp_sum(ss), D);
-        const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
-        const uint64_t slot = P % p.L.ring;
+        float *const kdst = kv_key(p.L, P) + kh * D, *const vdst = kv_value(p.L, P) + kh * D;
         for (uint32_t i = lane; i < D; i += 32) {
             const float k = rms_apply(x[i], inv, p.L.kn[i], 1.0f);
             knew[i] = k;
             vnew[i] = v[i];
-            p.L.ring_k_w[slot * kvw + kh * D + i] = k;
-            p.L.ring_v_w[slot * kvw + kh * D + i] = v[i];
+            kdst[i] = k;
+            vdst[i] = v[i];
         }
     }
     for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) acc[i] = 0.0f;
@@ -944,7 +970,6 @@ __global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads
     __syncthreads();
 
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(D)));
-    const uint64_t kvw = static_cast<uint64_t>(p.kh) * D;
     for (uint64_t base = k0; base < k1; base += kDecTile) {
         const uint32_t rows = static_cast<uint32_t>(k1 - base < kDecTile ? k1 - base : kDecTile);
         if constexpr (DT != 0) {
@@ -963,9 +988,8 @@ __global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads
                         const uint64_t key = base + r;
                         const float *ksrc, *vsrc;
                         if (key < P) {
-                            const uint64_t slot = key % p.L.ring;
-                            ksrc = p.L.ring_k + slot * kvw + kh * DT;
-                            vsrc = p.L.ring_v + slot * kvw + kh * DT;
+                            ksrc = kv_key(p.L, key) + kh * DT;
+                            vsrc = kv_value(p.L, key) + kh * DT;
                         } else {
                             ksrc = knew;
                             vsrc = vnew;
@@ -1008,9 +1032,8 @@ __global__ void __cluster_dims__(1, kDecSplits, 1) __launch_bounds__(kDecThreads
                 const uint64_t key = base + r;
                 const float *ksrc, *vsrc;
                 if (key < P) {
-                    const uint64_t slot = key % p.L.ring;
-                    ksrc = p.L.ring_k + slot * kvw + kh * D;
-                    vsrc = p.L.ring_v + slot * kvw + kh * D;
+                    ksrc = kv_key(p.L, key) + kh * D;
+                    vsrc = kv_value(p.L, key) + kh * D;
                 } else {
                     ksrc = knew;
                     vsrc = vnew;
@@ -1140,11 +1163,11 @@ __global__ void kv_store_kernel(AttnLayer L, AttnShape S, const float *qkv, uint
     const uint64_t t = first + blockIdx.x;
     const uint64_t P = *L.appended;
     const uint64_t kvw = S.kh * S.dim;
-    const uint64_t slot = (P + t) % L.ring;
     const float *row = qkv + t * S.qkv_stride;
+    float *const kdst = kv_key(L, P + t), *const vdst = kv_value(L, P + t);
     for (uint64_t i = threadIdx.x; i < kvw; i += blockDim.x) {
-        L.ring_k_w[slot * kvw + i] = row[S.qh * S.dim + i];
-        L.ring_v_w[slot * kvw + i] = row[(S.qh + S.kh) * S.dim + i];
+        kdst[i] = row[S.qh * S.dim + i];
+        vdst[i] = row[(S.qh + S.kh) * S.dim + i];
     }
     pdl_launch_dependents();
 }
@@ -1153,10 +1176,10 @@ __global__ void kv_store_kernel(AttnLayer L, AttnShape S, const float *qkv, uint
 // ring slot of the next committed row.
 __global__ void kv_commit_kernel(AttnLayer L, uint64_t kvw, const float *k_row, const float *v_row) {
     const uint64_t P = *L.appended;
-    const uint64_t slot = P % L.ring;
+    float *const kdst = kv_key(L, P), *const vdst = kv_value(L, P);
     for (uint64_t i = threadIdx.x; i < kvw; i += blockDim.x) {
-        L.ring_k_w[slot * kvw + i] = k_row[i];
-        L.ring_v_w[slot * kvw + i] = v_row[i];
+        kdst[i] = k_row[i];
+        vdst[i] = v_row[i];
     }
 }
 
@@ -1179,30 +1202,18 @@ __global__ void kv_gather_kernel(AttnLayer L, uint64_t kvw, uint64_t heads, uint
                                  uint64_t count, float *k_out, float *v_out, float *rot_out) {
     const uint64_t r = blockIdx.x;
     const uint64_t P = *L.appended;
-    const uint64_t slot = (P - count + r) % L.ring;
+    const float *const krow = kv_key(L, P - count + r), *const vrow = kv_value(L, P - count + r);
     const uint64_t half = dim / 2;
     const float *c = L.table + r * dim, *s = c + half;
     for (uint64_t i = threadIdx.x; i < kvw; i += blockDim.x) {
-        k_out[r * kvw + i] = L.ring_k[slot * kvw + i];
-        v_out[r * kvw + i] = L.ring_v[slot * kvw + i];
+        k_out[r * kvw + i] = krow[i];
+        v_out[r * kvw + i] = vrow[i];
     }
     for (uint64_t i = threadIdx.x; i < heads * half; i += blockDim.x) {
         const uint64_t h = i / half, d = i % half;
-        const float a = L.ring_k[slot * kvw + h * dim + d], b = L.ring_k[slot * kvw + h * dim + d + half];
+        const float a = krow[h * dim + d], b = krow[h * dim + d + half];
         rot_out[r * kvw + h * dim + d] = __fsub_rn(__fmul_rn(a, c[d]), __fmul_rn(b, s[d]));
         rot_out[r * kvw + h * dim + d + half] = __fadd_rn(__fmul_rn(b, c[d]), __fmul_rn(a, s[d]));
-    }
-}
-
-// Upload view: token-major host rows [0, count) into ring slots 0..count-1
-// (the request restarts with count committed rows).
-__global__ void kv_scatter_kernel(float *ring_k, float *ring_v, uint64_t ring, uint64_t kvw,
-                                  const float *k_in, const float *v_in) {
-    const uint64_t r = blockIdx.x;
-    const uint64_t slot = r % ring;
-    for (uint64_t i = threadIdx.x; i < kvw; i += blockDim.x) {
-        ring_k[slot * kvw + i] = k_in[r * kvw + i];
-        ring_v[slot * kvw + i] = v_in[r * kvw + i];
     }
 }
 

@@ -62,7 +62,13 @@ struct Rope {
 struct DLayer {
     struct layer *host;
     const uint16_t *qkv_w, *qn, *kn, *o_w, *pre, *post, *mpre, *mpost, *gu, *down;
-    float *ring_k, *ring_v;
+    // KV slots [0, ring) in pages of kKvPageRows rows from the context's pool:
+    // pages[i] (host mirror) and d_pages[i] (device table) hold page i's base,
+    // the first `mapped` of them taken from the pool, the rest the pool's
+    // zeroed spare page.
+    std::vector<float *> pages;
+    float **d_pages;
+    uint64_t mapped;
     uint64_t ring, capacity;
     int sliding;
     Rope *rope;
@@ -139,6 +145,18 @@ struct DModel {
 // returned by cudaGetSymbolAddress (the name is a host-side stand-in).
 static __device__ __align__(256) float g_linear_static_scratch[kStaticLinearFloats];
 
+// Pages of KV rows shared by every request of a context with the same row
+// width: chunks of kKvChunkPages pages are allocated as requests need them
+// and stay with the context; pages return to `free` when a request resets or
+// is released.
+constexpr uint64_t kKvChunkPages = 16;
+struct KvPool {
+    std::vector<float *> chunks;
+    std::vector<float *> free;
+    float *spare = nullptr;  // zeroed page for the unmapped entries of page tables
+    uint64_t used = 0;
+};
+
 struct plamo_cuda {
     int device;
     cudaStream_t stream;
@@ -169,6 +187,7 @@ struct plamo_cuda {
     int gemv_ctas;
     uint32_t *sink;
     float *static_scratch;  // device address of g_linear_static_scratch (set on first use)
+    std::map<uint64_t, KvPool> kv_pools;  // by floats per K row (kv heads x head dim)
     char *staging = nullptr;   // grow-only device staging of linear / mlp (host buffers in and out)
     uint64_t staging_bytes = 0;
 };
@@ -597,10 +616,8 @@ RowFuse row_fuse(plamo_cuda *c, DModel *m, const uint16_t *next_w, uint64_t T, u
 AttnLayer attn_layer(const DModel *m, uint64_t l) {
     const DLayer &L = m->layers[l];
     AttnLayer a;
-    a.ring_k = L.ring_k;
-    a.ring_v = L.ring_v;
-    a.ring_k_w = L.ring_k;
-    a.ring_v_w = L.ring_v;
+    a.pages = L.d_pages;
+    a.kvw = m->KVW;
     a.appended = m->d_appended + l;
     a.ring = L.ring;
     a.capacity = L.capacity;
@@ -626,14 +643,124 @@ void *dalloc(plamo_cuda *c, DModel *m, uint64_t bytes) {
     return p;
 }
 
+// ---- KV pages -----------------------------------------------------------------
+uint64_t kv_page_floats(uint64_t kvw) { return 2 * kKvPageRows * kvw; }
+
+// The pool of row width kvw, with its zeroed spare page (0 if it cannot be made).
+KvPool *kv_pool(plamo_cuda *c, uint64_t kvw) {
+    KvPool &pool = c->kv_pools[kvw];
+    if (!pool.spare) {
+        const uint64_t bytes = kv_page_floats(kvw) * 4;
+        if (!note(c, "kv spare page", cudaMalloc(&pool.spare, bytes))) {
+            pool.spare = nullptr;
+            return nullptr;
+        }
+        cudaMemset(pool.spare, 0, bytes);
+        c->info.kv_bytes += bytes;
+        c->info.allocated_bytes += bytes;
+    }
+    return &pool;
+}
+
+// One page from the pool, growing it by a chunk when it is empty.
+float *kv_page_take(plamo_cuda *c, uint64_t kvw) {
+    KvPool *pool = kv_pool(c, kvw);
+    if (!pool) return nullptr;
+    if (pool->free.empty()) {
+        const uint64_t floats = kv_page_floats(kvw);
+        float *chunk = nullptr;
+        if (!note(c, "kv page chunk", cudaMalloc(&chunk, kKvChunkPages * floats * 4))) return nullptr;
+        pool->chunks.push_back(chunk);
+        c->info.kv_bytes += kKvChunkPages * floats * 4;
+        c->info.allocated_bytes += kKvChunkPages * floats * 4;
+        c->info.kv_pages_allocated += kKvChunkPages;
+        for (uint64_t i = kKvChunkPages; i-- > 0;) pool->free.push_back(chunk + i * floats);
+    }
+    float *page = pool->free.back();
+    pool->free.pop_back();
+    ++pool->used;
+    ++c->info.kv_pages_used;
+    return page;
+}
+
+void kv_page_give(plamo_cuda *c, uint64_t kvw, float *page) {
+    KvPool &pool = c->kv_pools[kvw];
+    pool.free.push_back(page);
+    --pool.used;
+    --c->info.kv_pages_used;
+}
+
+// Map the pages of slots [0, min(rows, ring)) of layer L and upload the new
+// page-table entries. False (nothing changed) when the pool cannot grow.
+bool kv_map(plamo_cuda *c, const DModel *m, DLayer &L, uint64_t rows) {
+    const uint64_t need = (std::min(rows, L.ring) + kKvPageRows - 1) / kKvPageRows;
+    const uint64_t first = L.mapped;
+    if (need <= first) return true;
+    for (uint64_t i = first; i < need; ++i) {
+        float *page = kv_page_take(c, m->KVW);
+        if (!page) {
+            for (uint64_t j = first; j < i; ++j) {
+                kv_page_give(c, m->KVW, L.pages[j]);
+                L.pages[j] = c->kv_pools[m->KVW].spare;
+            }
+            snprintf(c->info.note, sizeof c->info.note, "KV page pool cannot grow (device memory)");
+            return false;
+        }
+        L.pages[i] = page;
+    }
+    if (!note(c, "kv page table", cudaMemcpyAsync(L.d_pages + first, L.pages.data() + first,
+                                                  (need - first) * sizeof(float *), cudaMemcpyHostToDevice,
+                                                  c->stream)))
+        return false;
+    L.mapped = need;
+    return true;
+}
+
+// Return the pages of layer L past the first `keep` to the pool (their table
+// entries point at the spare page again).
+bool kv_unmap(plamo_cuda *c, const DModel *m, DLayer &L, uint64_t keep) {
+    if (L.mapped <= keep) return true;
+    KvPool &pool = c->kv_pools[m->KVW];
+    for (uint64_t i = keep; i < L.mapped; ++i) {
+        kv_page_give(c, m->KVW, L.pages[i]);
+        L.pages[i] = pool.spare;
+    }
+    const uint64_t first = keep;
+    const bool ok = note(c, "kv page table", cudaMemcpyAsync(L.d_pages + first, L.pages.data() + first,
+                                                             (L.mapped - first) * sizeof(float *),
+                                                             cudaMemcpyHostToDevice, c->stream));
+    L.mapped = keep;
+    return ok;
+}
+
+// Copy rows [0, rows) of layer L between its pages and row-major K and V
+// arrays ([rows][kvw] each), toward the pages when `to_pages`.
+bool kv_copy_rows(plamo_cuda *c, const DModel *m, const DLayer &L, uint64_t rows, float *k, float *v,
+                  bool to_pages, cudaMemcpyKind kind) {
+    const uint64_t kvw = m->KVW;
+    for (uint64_t p = 0; p * kKvPageRows < rows; ++p) {
+        const uint64_t n = std::min(kKvPageRows, rows - p * kKvPageRows);
+        float *pk = L.pages[p], *pv = L.pages[p] + kKvPageRows * kvw;
+        float *lk = k + p * kKvPageRows * kvw, *lv = v + p * kKvPageRows * kvw;
+        const uint64_t bytes = n * kvw * 4;
+        if (!note(c, "kv rows", cudaMemcpyAsync(to_pages ? pk : lk, to_pages ? lk : pk, bytes, kind, c->stream)) ||
+            !note(c, "kv rows", cudaMemcpyAsync(to_pages ? pv : lv, to_pages ? lv : pv, bytes, kind, c->stream)))
+            return false;
+    }
+    return true;
+}
+
 void free_model(plamo_cuda *c, DModel *m) {
     if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     for (uint32_t r = 0; r < m->tp.size; ++r)
         if (r != m->tp.rank && m->tp.peer[r]) cudaIpcCloseMemHandle(m->tp.peer[r]);
+    for (DLayer &L : m->layers) {
+        for (uint64_t i = 0; i < L.mapped; ++i) kv_page_give(c, m->KVW, L.pages[i]);
+        L.mapped = 0;
+    }
     for (void *p : m->allocations) cudaFree(p);
     m->allocations.clear();
-    (void)c;
 }
 
 // Identity of a host descriptor tree: dimensions, every weight and KV pointer.
@@ -705,12 +832,12 @@ bool reconcile(plamo_cuda *c, DModel *m) {
         changed = true;
         L.stale = false;
         if (hc->count > L.ring || hc->count > L.capacity) return false;
-        if (hc->count) {
-            const uint64_t bytes = hc->count * m->KVW * 4;
-            if (!note(c, "kv upload", cudaMemcpyAsync(L.ring_k, hc->k, bytes, cudaMemcpyHostToDevice, c->stream)) ||
-                !note(c, "kv upload", cudaMemcpyAsync(L.ring_v, hc->v, bytes, cudaMemcpyHostToDevice, c->stream)))
-                return false;
-        }
+        // A full layer keeps pages for the rows it holds; the others go back
+        // to the pool (a reset returns all of them).
+        if (!L.sliding && !kv_unmap(c, m, L, (hc->count + kKvPageRows - 1) / kKvPageRows)) return false;
+        if (hc->count && (!kv_map(c, m, L, hc->count) ||
+                          !kv_copy_rows(c, m, L, hc->count, hc->k, hc->v, true, cudaMemcpyHostToDevice)))
+            return false;
         L.appended = hc->count;
     }
     if (changed) {
@@ -738,14 +865,17 @@ void publish_counts(DModel *m, uint64_t rows) {
 }
 
 // Rows a decode/prefill of `tokens` would need; false when a full-attention
-// cache cannot take them (the reference declines: src/cache.s global full).
-bool fits(const DModel *m, uint64_t tokens) {
+// cache cannot take them (the reference declines: src/cache.s global full) or
+// the KV pages for them cannot be mapped. Maps those pages otherwise.
+bool fits(plamo_cuda *c, DModel *m, uint64_t tokens) {
     for (const DLayer &L : m->layers) {
         if (!L.sliding && L.appended + tokens > L.capacity) return false;
         if (!L.sliding && L.appended + tokens > L.ring) return false;
         if (L.sliding && std::min(L.appended + tokens, L.capacity) > L.rope->positions) return false;
         if (!L.sliding && L.appended + tokens > L.rope->positions) return false;
     }
+    for (DLayer &L : m->layers)
+        if (!L.sliding && !kv_map(c, m, L, L.appended + tokens)) return false;
     return true;
 }
 
@@ -1524,6 +1654,10 @@ void plamo_cuda_close(struct plamo_cuda *c) {
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     for (auto &kv : c->models) free_model(c, kv.second.get());
+    for (auto &kv : c->kv_pools) {
+        for (float *chunk : kv.second.chunks) cudaFree(chunk);
+        cudaFree(kv.second.spare);
+    }
     for (auto &r : c->ropes) cudaFree(r->dev);
     for (Range &r : c->ranges) cudaFree(r.dev);
     cudaFreeHost(c->pinned_u32);
@@ -1703,12 +1837,21 @@ static int prepare_impl(struct plamo_cuda *c, struct model *model, uint64_t head
         const uint64_t positions = L.sliding ? kc->capacity : std::min<uint64_t>(kc->capacity, c->config.max_context);
         L.rope = get_rope(c, hl->mixer->rotation->freq, m->D, L.scale, positions);
         if (!L.rope) return 0;
-        L.ring_k = static_cast<float *>(dalloc(c, m.get(), L.ring * m->KVW * 4));
-        L.ring_v = static_cast<float *>(dalloc(c, m.get(), L.ring * m->KVW * 4));
-        if (!L.ring_k || !L.ring_v) return 0;
-        c->info.kv_bytes += 2 * L.ring * m->KVW * 4;
+        // Page table: every entry on the spare page until a page is mapped;
+        // a sliding ring maps all its pages now, a full layer as rows arrive.
+        KvPool *pool = kv_pool(c, m->KVW);
+        if (!pool) return 0;
+        const uint64_t npages = (L.ring + kKvPageRows - 1) / kKvPageRows;
+        L.pages.assign(npages, pool->spare);
+        L.mapped = 0;
+        L.d_pages = static_cast<float **>(dalloc(c, m.get(), npages * sizeof(float *)));
+        if (!L.d_pages ||
+            !note(c, "kv page table", cudaMemcpy(L.d_pages, L.pages.data(), npages * sizeof(float *),
+                                                 cudaMemcpyHostToDevice)))
+            return 0;
         L.appended = 0;
         m->layers.push_back(L);
+        if (L.sliding && !kv_map(c, m.get(), m->layers.back(), L.ring)) return 0;
     }
     // Decode buffers.
     const uint64_t G = m->QH / m->KH;
@@ -1883,7 +2026,7 @@ int plamo_cuda_forward_greedy_margin(struct plamo_cuda *c, struct model *model, 
         return 0;
     }
     if (!reconcile(c, m)) return -1;
-    if (!fits(m, 1)) {
+    if (!fits(c, m, 1)) {
         c->info.declines++;
         return 0;
     }
@@ -1928,7 +2071,7 @@ static int prompt(struct plamo_cuda *c, struct model *model, const uint32_t *ids
         return 0;
     }
     if (!reconcile(c, m)) return -1;
-    if (!fits(m, tokens)) {
+    if (!fits(c, m, tokens)) {
         c->info.declines++;
         return 0;
     }
@@ -1978,7 +2121,7 @@ int plamo_cuda_verify(struct plamo_cuda *c, struct model *model, const uint32_t 
             return 0;
         }
     if (!reconcile(c, m)) return -1;
-    if (!fits(m, tokens)) {
+    if (!fits(c, m, tokens)) {
         c->info.declines++;
         return 0;
     }
@@ -2018,7 +2161,7 @@ int plamo_cuda_commit(struct plamo_cuda *c, struct model *model, uint64_t index)
         if (c) c->info.declines++;
         return 0;
     }
-    if (!fits(m, 1)) return 0;
+    if (!fits(c, m, 1)) return 0;
     for (uint64_t l = 0; l < m->L; ++l) {
         AttnLayer al = attn_layer(m, l);
         const float *row = m->v_kv + (l * kVerifyMax + index) * 2 * m->KVW;
@@ -2081,7 +2224,7 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
     }
     if (!reconcile(c, m)) return -1;
     DLayer &L = m->layers[index];
-    if (!L.sliding && (L.appended + 1 > L.capacity || L.appended + 1 > L.ring)) {
+    if (!L.sliding && (L.appended + 1 > L.capacity || L.appended + 1 > L.ring || !kv_map(c, m, L, L.appended + 1))) {
         c->info.declines++;
         return 0;
     }
@@ -2515,7 +2658,7 @@ static bool batch_ready(plamo_cuda_batch *b, uint64_t steps, std::vector<DModel 
     plamo_cuda *c = b->c;
     for (struct model *h : b->hosts) {
         DModel *m = find_model(c, h);
-        if (!m || !reconcile(c, m) || !fits(m, steps)) return false;
+        if (!m || !reconcile(c, m) || !fits(c, m, steps)) return false;
         m->verify_valid = false;
         ms.push_back(m);
     }
@@ -2663,10 +2806,8 @@ struct plamo_cuda_prompt_cache *plamo_cuda_prompt_cache_capture(struct plamo_cud
         const DLayer &L = m->layers[l];
         s->width.push_back(model->layers[l]->mixer->cache->width);
         s->scale_bits.push_back(model->layers[l]->mixer->rotation->scale_bits);
-        ok = note(c, "prompt cache capture", cudaMemcpyAsync(s->rows + (2 * l) * words, L.ring_k, words * 4,
-                                                             cudaMemcpyDeviceToDevice, c->stream)) &&
-             note(c, "prompt cache capture", cudaMemcpyAsync(s->rows + (2 * l + 1) * words, L.ring_v, words * 4,
-                                                             cudaMemcpyDeviceToDevice, c->stream));
+        ok = kv_copy_rows(c, m, L, tokens, s->rows + (2 * l) * words, s->rows + (2 * l + 1) * words, false,
+                          cudaMemcpyDeviceToDevice);
     }
     ok = ok && note(c, "prompt cache capture", cudaStreamSynchronize(c->stream));
     if (!ok) {
@@ -2694,15 +2835,16 @@ uint64_t plamo_cuda_prompt_cache_restore(struct plamo_cuda *c, const struct plam
             !mx->rotation->out || L.capacity < s->tokens || L.ring < s->tokens)
             return 0;
     }
+    // Pages for the snapshot's rows, before anything is written.
+    for (uint64_t l = 0; l < model->count; ++l)
+        if (!kv_map(c, m, m->layers[l], s->tokens)) return 0;
     m->verify_valid = false;  // a pending verification's rows are gone
     const uint64_t words = s->tokens * s->kvw;
     bool ok = true;
     for (uint64_t l = 0; l < model->count && ok; ++l) {
         DLayer &L = m->layers[l];
-        ok = note(c, "prompt cache restore", cudaMemcpyAsync(L.ring_k, s->rows + (2 * l) * words, words * 4,
-                                                             cudaMemcpyDeviceToDevice, c->stream)) &&
-             note(c, "prompt cache restore", cudaMemcpyAsync(L.ring_v, s->rows + (2 * l + 1) * words, words * 4,
-                                                             cudaMemcpyDeviceToDevice, c->stream));
+        ok = kv_copy_rows(c, m, L, s->tokens, s->rows + (2 * l) * words, s->rows + (2 * l + 1) * words, true,
+                          cudaMemcpyDeviceToDevice);
         L.appended = s->tokens;
         L.stale = false;
         struct mixer *mx = model->layers[l]->mixer;
@@ -2902,7 +3044,7 @@ double plamo_cuda_time_gemv_copies(struct plamo_cuda *c, const uint16_t *w, uint
 double plamo_cuda_time_decode(struct plamo_cuda *c, struct model *model, uint64_t repeats) {
     if (!c || !repeats) return -1;
     DModel *m = find_model(c, model);
-    if (!m || !reconcile(c, m) || !fits(m, repeats) || !ensure_graph(c, m)) return -1;
+    if (!m || !reconcile(c, m) || !fits(c, m, repeats) || !ensure_graph(c, m)) return -1;
     m->verify_valid = false;
     cudaStreamSynchronize(c->stream);
     cudaEventRecord(c->ev0, c->stream);
@@ -2966,7 +3108,7 @@ double plamo_cuda_decode_trace(struct plamo_cuda *c, struct model *model, uint64
     if (!c || !stamps) return -1;
     cudaSetDevice(c->device);
     DModel *m = find_model(c, model);
-    if (!m || token >= model->vocab || !reconcile(c, m) || !fits(m, 1) || !ensure_graph(c, m)) return -1;
+    if (!m || token >= model->vocab || !reconcile(c, m) || !fits(c, m, 1) || !ensure_graph(c, m)) return -1;
     if (!m->pt_ready) return graph_trace(c, m, token, stamps, capacity);
     const uint64_t n = 1 + (5 * m->L + 1) + (4 * m->L + 1);
     if (capacity < n) return -1;

@@ -106,6 +106,18 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
     return policy;
 }
+// A small, hot table read once per launch (KV page bases): keep its lines in
+// L2 past the weight streams, which are marked evict-first.
+__device__ __forceinline__ uint64_t evict_last_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+__device__ __forceinline__ uint64_t load_u64_keep(const void *p, uint64_t policy) {
+    uint64_t v;
+    asm volatile("ld.global.L2::cache_hint.u64 %0, [%1], %2;" : "=l"(v) : "l"(p), "l"(policy));
+    return v;
+}
 __device__ __forceinline__ uint4 load_stream(const void *p, uint64_t policy) {
     uint4 v;
     asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"

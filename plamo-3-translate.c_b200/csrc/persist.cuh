@@ -471,7 +471,6 @@ __device__ __noinline__ void pt_attention(const PtParams &p, uint32_t l, float *
     const uint32_t n = static_cast<uint32_t>(P + 1 - lo);
     const uint64_t k0 = lo + static_cast<uint64_t>(n) * split / S;
     const uint64_t k1 = lo + static_cast<uint64_t>(n) * (split + 1) / S;
-    const uint64_t kvw = static_cast<uint64_t>(p.KH) * D;
 
     auto stage = [&](uint64_t base, uint32_t rows) {
         for (uint32_t i = threadIdx.x; i < rows * 32; i += nt) {
@@ -479,9 +478,8 @@ __device__ __noinline__ void pt_attention(const PtParams &p, uint32_t l, float *
             const uint64_t key = base + r;
             cp_async16(tab + r * D + c, A.table + (key - lo) * D + c);
             if (key < P) {
-                const uint64_t slot = key % A.ring;
-                cp_async16(kt + r * KS + c, A.ring_k + slot * kvw + kh * D + c);
-                cp_async16(vt + r * D + c, A.ring_v + slot * kvw + kh * D + c);
+                cp_async16(kt + r * KS + c, kv_key(A, key) + kh * D + c);
+                cp_async16(vt + r * D + c, kv_value(A, key) + kh * D + c);
             }
         }
         cp_async_commit();
@@ -530,11 +528,10 @@ __device__ __noinline__ void pt_attention(const PtParams &p, uint32_t l, float *
         const uint2 wk = *reinterpret_cast<const uint2 *>(A.kn + 4 * lane);
         const float inv = rms_inverse(warp_sum(sq4(xk)), D);
         const float4 k4 = apply4(xk, inv, norm4(wk, 1.0f));
-        const uint64_t slot = P % A.ring;
         *reinterpret_cast<float4 *>(knew + 4 * lane) = k4;
         *reinterpret_cast<float4 *>(vnew + 4 * lane) = xv;
-        *reinterpret_cast<float4 *>(A.ring_k_w + slot * kvw + kh * D + 4 * lane) = k4;
-        *reinterpret_cast<float4 *>(A.ring_v_w + slot * kvw + kh * D + 4 * lane) = xv;
+        *reinterpret_cast<float4 *>(kv_key(A, P) + kh * D + 4 * lane) = k4;
+        *reinterpret_cast<float4 *>(kv_value(A, P) + kh * D + 4 * lane) = xv;
     }
     for (uint32_t i = threadIdx.x; i < G * D; i += nt) acc[i] = 0.0f;
     for (uint32_t g = threadIdx.x; g < G; g += nt) {
