@@ -418,7 +418,7 @@ static std::string compute_json(plamo_engine *e) {
              "\"command_buffers\":%llu,\"fused_mlps\":0,\"fused_decodes\":%llu,\"fused_prefills\":%llu,"
              "\"cpu_fallbacks\":0,\"errors\":%llu,\"gpu_seconds\":%.9f,\"allocated_bytes\":%llu,"
              "\"recommended_working_set_bytes\":0,\"kv_bytes\":%llu,\"workspace_bytes\":%llu,"
-             "\"sm_count\":%llu,\"declines\":%llu,",
+             "\"sm_count\":%llu,\"declines\":%llu,\"kv_pages_used\":%llu,\"kv_pages_allocated\":%llu,",
              static_cast<unsigned long long>(g.weight_bytes), static_cast<unsigned long long>(g.verification_batches),
              static_cast<unsigned long long>(g.verified_tokens), static_cast<unsigned long long>(g.committed_tokens),
              static_cast<unsigned long long>(g.launches), static_cast<unsigned long long>(g.graph_launches),
@@ -426,7 +426,8 @@ static std::string compute_json(plamo_engine *e) {
              static_cast<unsigned long long>(g.errors), g.gpu_seconds,
              static_cast<unsigned long long>(g.allocated_bytes), static_cast<unsigned long long>(g.kv_bytes),
              static_cast<unsigned long long>(g.workspace_bytes), static_cast<unsigned long long>(g.sm_count),
-             static_cast<unsigned long long>(g.declines));
+             static_cast<unsigned long long>(g.declines), static_cast<unsigned long long>(g.kv_pages_used),
+             static_cast<unsigned long long>(g.kv_pages_allocated));
     return "{\"backend\":" + json_text(e->info.backend) + ",\"device\":" + json_text(g.device) + "," + buf +
            "\"decode_path\":" + json_text(path ? path : "") + ",\"note\":" + json_text(g.note) + "}";
 }

@@ -237,4 +237,5 @@ def test_translate_streams_the_greedy_ids_of_the_device_loop(engine_files, mode)
     assert compute["backend"] == "cuda" and compute["gpu_dispatches"] > 0 and compute["errors"] == 0
     assert compute["fused_prefills"] >= 1 and compute["gpu_seconds"] > 0
     assert compute["decode_path"].startswith(("graph", "persistent"))
+    assert compute["kv_pages_used"] > 0 and compute["kv_pages_allocated"] >= compute["kv_pages_used"]
     assert re.fullmatch(r"[0-9a-f]{16}", report["verification"]["logits_hash"])
