@@ -517,7 +517,7 @@ bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, cons
     int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, budget / tc_stage_bytes(N)));
     if (c->tc_stages) stages = std::min(stages, c->tc_stages);
     const dim3 grid((T + N - 1) / N, (R + kTcM - 1) / kTcM, splits);
-    return launch(c, gemm_tc_kernel<N>, grid, dim3(kTcThreads), tc_smem_bytes(N, stages), mw, mh, mm, ml, p,
+    return launch(c, gemm_tc_kernel<N>, grid, dim3(tc_threads<N>()), tc_smem_bytes(N, stages), mw, mh, mm, ml, p,
                   stages);
 }
 

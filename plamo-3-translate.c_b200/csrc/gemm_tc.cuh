@@ -44,7 +44,19 @@ namespace plamo {
 
 constexpr int kTcM = 128;
 constexpr int kTcK = 64;  // BF16 elements per stage row: 128 bytes, one swizzle atom
-constexpr int kTcThreads = 192;
+// Warps: TMA producer, MMA issuer, then the epilogue warps that fold every K
+// block's accumulator into registers. A tile of 64 or more tokens gets two
+// epilogue warps per TMEM lane quadrant, each folding half of the columns:
+// with one, the fold (tcgen05.ld of 128 columns and 128 adds per K block)
+// took longer than the block's three MMAs and held the tensor pipe at ~52 %.
+template <int N>
+__host__ __device__ constexpr int tc_epi_warps() {
+    return N >= 64 ? 8 : 4;
+}
+template <int N>
+__host__ __device__ constexpr int tc_threads() {
+    return (2 + tc_epi_warps<N>()) * 32;
+}
 constexpr int kTcMaxStages = 10;
 constexpr int kTcAccMax = 16;
 // TMEM accumulators (one K block each) in a ring of 256 columns: with few
@@ -141,7 +153,7 @@ inline size_t tc_smem_bytes(uint32_t n, int stages) { return stages * tc_stage_b
 
 // N: tokens per tile (multiple of 16, <= 256).
 template <int N>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(tc_threads<N>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
                    const __grid_constant__ CUtensorMap map_mid, const __grid_constant__ CUtensorMap map_lo,
                    TcGemmParams p, int stages) {
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int a = 0; a < kTcAcc; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+            mbar_init(&acc_empty[a], tc_epi_warps<N>());  // one arrival per epilogue warp
         }
         abort_flag = 0;
         fence_barrier_init();
@@ -257,12 +269,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else if (warp >= 2) {
-        // Fold every K block's partial into FP32 registers (IEEE adds, in order).
+        // Fold every K block's partial into FP32 registers (IEEE adds, in order):
+        // this warp's TMEM lane quadrant, columns [col0, col0 + NC).
+        constexpr int NC = N * 4 / tc_epi_warps<N>();
         const uint32_t quad = warp & 3;  // TMEM lanes this warp may access
         const uint32_t lanes = (quad * 32) << 16;
-        float sum[N];
+        const uint32_t col0 = static_cast<uint32_t>((warp - 2) / 4) * NC;
+        float sum[NC];
 #pragma unroll
-        for (int i = 0; i < N; ++i) sum[i] = 0.0f;
+        for (int i = 0; i < NC; ++i) sum[i] = 0.0f;
         bool ok = true;
         for (uint32_t kb = 0; kb < kblocks; ++kb) {
             const uint32_t a = kb % kTcAcc;
@@ -272,16 +287,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 break;
             }
             tc_fence_after();
-            if constexpr (N == 16) {
+            if constexpr (NC == 16) {
                 float v[16];
-                tmem_ld16(tmem + lanes + a * N, v);
+                tmem_ld16(tmem + lanes + a * N + col0, v);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) sum[i] = __fadd_rn(sum[i], v[i]);
             } else {
 #pragma unroll
-                for (int c = 0; c < N; c += 32) {
+                for (int c = 0; c < NC; c += 32) {
                     float v[32];
-                    tmem_ld32(tmem + lanes + a * N + c, v);
+                    tmem_ld32(tmem + lanes + a * N + col0 + c, v);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) sum[c + i] = __fadd_rn(sum[c + i], v[i]);
                 }
@@ -295,8 +310,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             float *out = gridDim.z > 1 ? p.part + static_cast<uint64_t>(blockIdx.z) * p.T * p.R : p.y;
             const uint64_t stride = gridDim.z > 1 ? p.R : p.ys;
 #pragma unroll
-            for (int j = 0; j < N; ++j) {
-                const uint32_t t = tok0 + j;
+            for (int j = 0; j < NC; ++j) {
+                const uint32_t t = tok0 + col0 + j;
                 if (t < p.T) out[static_cast<uint64_t>(t) * stride + row] = sum[j];
             }
         }
