@@ -175,6 +175,8 @@ struct plamo_cuda {
     bool bulk_gemv;
     int gemv_ring_kb;
     int tc_stages;  // tcgen05 projection ring depth (0: as many as shared memory holds)
+    uint32_t tc_n;  // largest token tile of the tcgen05 projections (PLAMO_CUDA_TC_N: 16/32/64; 0: 128)
+    int tc_tokm;    // token-major tcgen05 tiles for prompts: -1 by waves, 0 never, 1 always (PLAMO_CUDA_TC_TOKM)
     float draft_margin;         // PLAMO_DRAFT_MIN_MARGIN, or -1: the reference's default rule
     unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
     bool tc_gemm;
@@ -521,6 +523,34 @@ bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, cons
                   stages);
 }
 
+// Token-major tiles (128 tokens x kTcTokN weight rows) or weight-major ones
+// (128 weight rows x 128 tokens) for a prompt of more than 64 tokens: one CTA
+// per SM either way, so the choice compares waves of tiles, a token-major tile
+// costing 1.2 weight-major ones (1.5 times the MMAs at 0.81 of the cost per
+// MMA, measured on the 8B gate_up projection). 8B, 455 tokens: qkv 116.8 ->
+// 85.8 us and gate_up 408 -> 356 us token-major; o_proj and down_proj (4096
+// rows, one wave either way) stay weight-major. PLAMO_CUDA_TC_TOKM=0 / 1
+// forces weight-major / token-major tiles.
+constexpr uint32_t kTcTokN = 192;
+bool tc_token_major(plamo_cuda *c, uint64_t T, uint64_t R) {
+    if (T <= 64 || c->tc_tokm == 0) return false;
+    if (c->tc_tokm == 1) return true;
+    const uint64_t sms = static_cast<uint64_t>(c->sm_count);
+    const uint64_t wm = (((T + 127) / 128) * ((R + kTcM - 1) / kTcM) + sms - 1) / sms;
+    const uint64_t tm = (((T + kTcM - 1) / kTcM) * ((R + kTcTokN - 1) / kTcTokN) + sms - 1) / sms;
+    return tm * 6 < wm * 5;
+}
+
+bool launch_tc_tokm(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &mm,
+                    const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T) {
+    const size_t budget = static_cast<size_t>(c->smem_optin) - 2048;
+    int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, budget / tc_stage_bytes(kTcTokN, true)));
+    if (c->tc_stages) stages = std::min(stages, c->tc_stages);
+    const dim3 grid((T + kTcM - 1) / kTcM, (R + kTcTokN - 1) / kTcTokN, 1);
+    return launch(c, gemm_tc_kernel<kTcTokN, true>, grid, dim3(tc_threads<kTcTokN>()),
+                  tc_smem_bytes(kTcTokN, stages, true), mw, mh, mm, ml, p, stages);
+}
+
 // Y[T][R] (row stride ys) = X[T][K] (row stride xs, FP32) . W[R][K]^T on the
 // tensor cores when the shapes allow TMA (16-byte aligned rows), else on the
 // FP32 CUDA-core kernel otherwise. split: BF16 scratch of 3*T*K elements
@@ -554,7 +584,17 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
     if (!presplit && !launch(c, split_hilo_kernel, dim3(blocks), dim3(256), 0, X, xs, static_cast<uint32_t>(T),
                              static_cast<uint32_t>(K), hi, mid, lo))
         return false;
-    const uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    if (tc_token_major(c, T, R)) {
+        CUtensorMap mw, mh, mm, ml;
+        if (bf16_map(&mw, W, R, K, kTcTokN) && bf16_map(&mh, hi, T, K, kTcM) && bf16_map(&mm, mid, T, K, kTcM) &&
+            bf16_map(&ml, lo, T, K, kTcM)) {
+            TcGemmParams p{Y, ys, static_cast<uint32_t>(T), static_cast<uint32_t>(R), static_cast<uint32_t>(K),
+                           error, part};
+            return launch_tc_tokm(c, mw, mh, mm, ml, p, static_cast<uint32_t>(R), static_cast<uint32_t>(T));
+        }
+    }
+    uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    if (c->tc_n && c->tc_n < N) N = c->tc_n;
     CUtensorMap mw, mh, mm, ml;
     if (!bf16_map(&mw, W, R, K, kTcM) || !bf16_map(&mh, hi, T, K, N) || !bf16_map(&mm, mid, T, K, N) ||
         !bf16_map(&ml, lo, T, K, N)) {
@@ -1587,6 +1627,10 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     }
     const char *tc_st = getenv("PLAMO_CUDA_TC_STAGES");
     c->tc_stages = tc_st ? std::max(2, std::min(atoi(tc_st), kTcMaxStages)) : 0;
+    const char *tokm = getenv("PLAMO_CUDA_TC_TOKM");
+    c->tc_tokm = tokm && (!strcmp(tokm, "0") || !strcmp(tokm, "1")) ? atoi(tokm) : -1;
+    const char *tcn = getenv("PLAMO_CUDA_TC_N");
+    c->tc_n = tcn && (atoi(tcn) == 16 || atoi(tcn) == 32 || atoi(tcn) == 64) ? static_cast<uint32_t>(atoi(tcn)) : 0;
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
     c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
@@ -1632,6 +1676,7 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     allow_smem(gemm_tc_kernel<32>, optin, carveout);
     allow_smem(gemm_tc_kernel<64>, optin, carveout);
     allow_smem(gemm_tc_kernel<128>, optin, carveout);
+    allow_smem(gemm_tc_kernel<kTcTokN, true>, optin, carveout);
     allow_smem(decode_attention_kernel<128>, optin, carveout);
     allow_smem(decode_attention128_batch_kernel, optin, carveout);
     allow_smem(decode_attention_kernel<0>, optin, carveout);

@@ -55,3 +55,25 @@ def test_tc_projection_matches_oracle(backend, T, R, K):
     want = oracle_rows(w, x)
     assert np.all(np.isfinite(got))
     assert rel_l2(got, want) <= 1e-5, rel_l2(got, want)
+
+
+@pytest.mark.parametrize("layout", ["0", "1"])
+@pytest.mark.parametrize("T,R,K", [(65, 200, 72), (129, 385, 1024), (455, 5120, 4096), (300, 1000, 520)])
+def test_tc_tile_layouts_match_oracle(monkeypatch, layout, T, R, K):
+    """Both tile layouts of a prompt projection (PLAMO_CUDA_TC_TOKM=0:
+    128 weight rows x 128 tokens; =1: 128 tokens x 192 weight rows, stored
+    through shared memory), with ragged token and row tiles and K tails."""
+    from conftest import load_package
+    monkeypatch.setenv("PLAMO_CUDA_TC_TOKM", layout)
+    pkg = load_package()
+    b = pkg.Backend(device=0, max_context=64, max_prefill=512)
+    try:
+        rng = np.random.default_rng(T * 17 + R + K)
+        w = np.ascontiguousarray(synthetic.bf16_round(rng.normal(0, 0.02, size=(R, K)).astype(np.float32)))
+        x = rng.normal(0, 1, size=(T, K)).astype(np.float32)
+        got = gpu_gemm(b, w, x)
+        want = oracle_rows(w, x)
+        assert np.all(np.isfinite(got))
+        assert rel_l2(got, want) <= 1e-5, rel_l2(got, want)
+    finally:
+        b.close()
