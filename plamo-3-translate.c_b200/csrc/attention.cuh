@@ -374,27 +374,28 @@ __global__ void prompt_keys_kernel(AttnLayer L, const float *qkv, uint32_t qkv_s
     pdl_launch_dependents();
 }
 
-// Shared memory of a CTA of ROWS query rows.
-template <int ROWS>
+// Shared memory of a CTA of ROWS query rows (BUFS key/value tile buffers).
+template <int ROWS, int BUFS = 2>
 constexpr size_t prompt_attention_smem_bytes() {
-    return (kPaD * (ROWS + 4) + 2 * kPaTile * kPaKS + 2 * kPaTile * kPaD + kPaTile * (ROWS + 4) + 2 * ROWS) *
+    return (kPaD * (ROWS + 4) + BUFS * kPaTile * kPaKS + BUFS * kPaTile * kPaD + kPaTile * (ROWS + 4) + 2 * ROWS) *
            sizeof(float);
 }
 
 // ROWS query rows per CTA (64, or 32 for short prompts: twice the CTAs,
 // half the work per key tile, so the longest blocks finish sooner). Every
 // row's operations are the same for either ROWS.
-template <int ROWS>
+template <int ROWS, int BUFS = 2>
 __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttnParams p) {
     static_assert(ROWS == 64 || ROWS == 32, "64 or 32 query rows per CTA");
+    static_assert(BUFS == 1 || BUFS == 2, "one or two tile buffers");
     constexpr int QS = ROWS + 4;       // transposed Q / P row stride (16-byte multiple)
     constexpr int RT = ROWS / 16;      // score phase: rows per thread (16 row groups)
     constexpr int RW = ROWS / 8;       // value phase: rows per warp (8 warps)
     extern __shared__ __align__(16) float sm[];
     float *qT = sm;                        // [128][QS]  Q rows, transposed
-    float *kt = qT + kPaD * QS;            // [2][tile][kPaKS] rotated keys (double buffer)
-    float *vt = kt + 2 * kPaTile * kPaKS;  // [2][tile][128]   values
-    float *pT = vt + 2 * kPaTile * kPaD;   // [tile][QS] exp(score - max), transposed
+    float *kt = qT + kPaD * QS;               // [BUFS][tile][kPaKS] rotated keys
+    float *vt = kt + BUFS * kPaTile * kPaKS;  // [BUFS][tile][128]   values
+    float *pT = vt + BUFS * kPaTile * kPaD;   // [tile][QS] exp(score - max), transposed
     float *corr = pT + kPaTile * QS;       // [ROWS] per-row correction of the tile
     float *lsum = corr + ROWS;             // [ROWS] final row sums
     constexpr uint32_t D = kPaD;
@@ -455,12 +456,13 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
     float l = 0.0f;  // row `tid` (tid < ROWS)
 
     uint32_t buf = 0;
-    for (uint32_t base = 0; base < hi_max; base += kPaTile, buf ^= 1u) {
+    for (uint32_t base = 0; base < hi_max; base += kPaTile, buf ^= (BUFS - 1)) {
         const uint32_t trow = min(static_cast<uint32_t>(kPaTile), hi_max - base);
-        if (base + kPaTile < hi_max) {
+        if (BUFS == 2 && base + kPaTile < hi_max) {
             stage(base + kPaTile, buf ^ 1u);  // that half was released by the last iteration's barrier
             cp_async_wait_one();
         } else {
+            if (BUFS == 1 && base > 0) stage(base, 0);  // the single buffer was released by the last barrier
             cp_async_wait_all();
         }
         __syncthreads();

@@ -57,9 +57,11 @@ def run(pkg, monkeypatch, prof, chunks, blocked, rows=None):
     (16, 1, 64, (30, 50)),    # G 16: second chunk continues at row 30, window fills at 64
     (4, 2, 16, (20, 17)),     # G 2: the second chunk's sliding queries all per token
 ])
-@pytest.mark.parametrize("rows", [64, 32])
-def test_blocked_prompt_attention_matches_per_token_kernel(pkg, monkeypatch, qh, kh, window, chunks, rows):
-    """Both block heights (64 query rows per CTA, and 32 for short prompts)."""
+@pytest.mark.parametrize("rows,bufs", [(64, 2), (32, 1), (32, 2)])
+def test_blocked_prompt_attention_matches_per_token_kernel(pkg, monkeypatch, qh, kh, window, chunks, rows, bufs):
+    """Both block heights (64 query rows per CTA, and 32 for short prompts),
+    the 32-row kernel with one and with two key/value tile buffers."""
+    monkeypatch.setenv("PLAMO_CUDA_PROMPT_BUFS", str(bufs))
     prof = pkg.Profile("attn", 512, 2, qh, kh, 128, 256, vocab=500, window=window, pattern=2,
                        max_position=1024)
     want = run(pkg, monkeypatch, prof, chunks, blocked=False)
