@@ -175,7 +175,6 @@ struct plamo_cuda {
     bool bulk_gemv;
     int gemv_ring_kb;
     int tc_stages;  // tcgen05 projection ring depth (0: as many as shared memory holds)
-    uint32_t tc_n;  // largest token tile of the tcgen05 projections (PLAMO_CUDA_TC_N: 16/32/64; 0: 128)
     int tc_tokm;    // token-major tcgen05 tiles for prompts: -1 by waves, 0 never, 1 always (PLAMO_CUDA_TC_TOKM)
     float draft_margin;         // PLAMO_DRAFT_MIN_MARGIN, or -1: the reference's default rule
     unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
@@ -594,8 +593,7 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
             return launch_tc_tokm(c, mw, mh, mm, ml, p, static_cast<uint32_t>(R), static_cast<uint32_t>(T));
         }
     }
-    uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
-    if (c->tc_n && c->tc_n < N) N = c->tc_n;
+    const uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
     CUtensorMap mw, mh, mm, ml;
     if (!bf16_map(&mw, W, R, K, kTcM) || !bf16_map(&mh, hi, T, K, N) || !bf16_map(&mm, mid, T, K, N) ||
         !bf16_map(&ml, lo, T, K, N)) {
@@ -1636,8 +1634,6 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_stages = tc_st ? std::max(2, std::min(atoi(tc_st), kTcMaxStages)) : 0;
     const char *tokm = getenv("PLAMO_CUDA_TC_TOKM");
     c->tc_tokm = tokm && (!strcmp(tokm, "0") || !strcmp(tokm, "1")) ? atoi(tokm) : -1;
-    const char *tcn = getenv("PLAMO_CUDA_TC_N");
-    c->tc_n = tcn && (atoi(tcn) == 16 || atoi(tcn) == 32 || atoi(tcn) == 64) ? static_cast<uint32_t>(atoi(tcn)) : 0;
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
     c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
