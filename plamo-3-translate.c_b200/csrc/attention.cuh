@@ -632,6 +632,7 @@ inline size_t decode_attention128_smem(uint32_t G) {
 
 template <int S>
 __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams &p) {
+    static_assert(S >= 2 && 32 % S == 0, "a head's splits share one warp in the merge");
     constexpr uint32_t D = 128, H = 64, KS = kD128Stride;
     extern __shared__ __align__(16) float sm[];
     const uint32_t G = p.qh / p.kh;
@@ -678,15 +679,23 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     float *const knew_dst = k1 == P + 1 ? page_of(P, 0) : nullptr;
     float *const vnew_dst = k1 == P + 1 ? page_of(P, 1) : nullptr;
 
-    // Asynchronous staging of one tile: 32 16-byte pieces per 512-byte row.
+    // Asynchronous staging of one tile: thread i copies columns c..c+3 and
+    // c+64..c+67 (r = i / 16, c = 4 (i % 16)) of a row's key, value and
+    // cos|sin entries - exactly the pairs it later rotates, so it can rotate
+    // them as soon as its own copies have landed.
     auto stage = [&](uint64_t base, uint32_t rows) {
-        for (uint32_t i = threadIdx.x; i < rows * 32; i += kDecThreads) {
-            const uint32_t r = i >> 5, c = (i & 31) * 4;
+        for (uint32_t i = threadIdx.x; i < rows * 16; i += kDecThreads) {
+            const uint32_t r = i >> 4, c = (i & 15) * 4;
             const uint64_t key = base + r;
-            cp_async16(tab + r * D + c, p.L.table + (key - lo) * D + c);
+            const float *trow = p.L.table + (key - lo) * D;
+            cp_async16(tab + r * D + c, trow + c);
+            cp_async16(tab + r * D + H + c, trow + H + c);
             if (key < P) {
-                cp_async16(kt + r * KS + c, page_of(key, 0) + c);
-                cp_async16(vt + r * D + c, page_of(key, 1) + c);
+                const float *krow = page_of(key, 0), *vrow = page_of(key, 1);
+                cp_async16(kt + r * KS + c, krow + c);
+                cp_async16(kt + r * KS + H + c, krow + H + c);
+                cp_async16(vt + r * D + c, vrow + c);
+                cp_async16(vt + r * D + H + c, vrow + H + c);
             }
         }
         cp_async_commit();
@@ -735,6 +744,10 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     // The new row: normalised K (unrotated) and V, stored to the ring by the
     // CTA whose split contains it.
     const bool has_new = k1 == P + 1;
+    // One tile (the common case): the new row goes straight into its tile row
+    // (the tile's copies skip it), its key rotated here at the query's
+    // position, so the tile needs no barrier before its keys are rotated.
+    const bool single = k1 - k0 <= kDecTile;
     if (has_new && warp == warps - 1) {
         const float *x = p.qkv + static_cast<uint64_t>(p.qh + kh) * D;
         const float *v = p.qkv + static_cast<uint64_t>(p.qh + p.kh + kh) * D;
@@ -742,10 +755,37 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
         const uint2 wk = *reinterpret_cast<const uint2 *>(p.L.kn + 4 * lane);
         const float inv = rms_inverse(warp_sum(sq4(xk)), D);
         const float4 k4 = apply4(xk, inv, norm4(wk, 1.0f));
-        *reinterpret_cast<float4 *>(knew + 4 * lane) = k4;
-        *reinterpret_cast<float4 *>(vnew + 4 * lane) = xv;
         *reinterpret_cast<float4 *>(knew_dst + 4 * lane) = k4;
         *reinterpret_cast<float4 *>(vnew_dst + 4 * lane) = xv;
+        if (single) {
+            // Lane l < 16 holds dims 4l.. of the first half, lane l + 16 the
+            // matching dims of the second half: the rotation pairs them.
+            float4 o;
+            o.x = __shfl_xor_sync(0xffffffffu, k4.x, 16);
+            o.y = __shfl_xor_sync(0xffffffffu, k4.y, 16);
+            o.z = __shfl_xor_sync(0xffffffffu, k4.z, 16);
+            o.w = __shfl_xor_sync(0xffffffffu, k4.w, 16);
+            const float4 a = lane < 16 ? k4 : o, b = lane < 16 ? o : k4;
+            const float4 c = ld4(table_q + 4 * (lane & 15)), sn = ld4(table_q + H + 4 * (lane & 15));
+            float4 rk;
+            if (lane < 16) {
+                rk.x = __fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(b.x, sn.x));
+                rk.y = __fsub_rn(__fmul_rn(a.y, c.y), __fmul_rn(b.y, sn.y));
+                rk.z = __fsub_rn(__fmul_rn(a.z, c.z), __fmul_rn(b.z, sn.z));
+                rk.w = __fsub_rn(__fmul_rn(a.w, c.w), __fmul_rn(b.w, sn.w));
+            } else {
+                rk.x = __fadd_rn(__fmul_rn(b.x, c.x), __fmul_rn(a.x, sn.x));
+                rk.y = __fadd_rn(__fmul_rn(b.y, c.y), __fmul_rn(a.y, sn.y));
+                rk.z = __fadd_rn(__fmul_rn(b.z, c.z), __fmul_rn(a.z, sn.z));
+                rk.w = __fadd_rn(__fmul_rn(b.w, c.w), __fmul_rn(a.w, sn.w));
+            }
+            const uint32_t rn = static_cast<uint32_t>(P - k0);
+            *reinterpret_cast<float4 *>(kt + rn * KS + 4 * lane) = rk;
+            *reinterpret_cast<float4 *>(vt + rn * D + 4 * lane) = xv;
+        } else {
+            *reinterpret_cast<float4 *>(knew + 4 * lane) = k4;
+            *reinterpret_cast<float4 *>(vnew + 4 * lane) = xv;
+        }
     }
     for (uint32_t i = threadIdx.x; i < G * D; i += kDecThreads) acc[i] = 0.0f;
     for (uint32_t g = threadIdx.x; g < G; g += kDecThreads) {
@@ -757,19 +797,24 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     for (uint64_t base = k0; base < k1; base += kDecTile) {
         const uint32_t rows = static_cast<uint32_t>(k1 - base < kDecTile ? k1 - base : kDecTile);
         cp_async_wait_all();
-        __syncthreads();
-        // The new row is not in the ring yet: take it from shared memory.
-        if (base + rows == P + 1) {
-            const uint32_t r = rows - 1;
-            for (uint32_t i = threadIdx.x; i < D; i += kDecThreads) {
-                kt[r * KS + i] = knew[i];
-                vt[r * D + i] = vnew[i];
-            }
+        if (!single) {
             __syncthreads();
+            // The new row is not in the ring yet: take it from shared memory.
+            if (base + rows == P + 1) {
+                const uint32_t r = rows - 1;
+                for (uint32_t i = threadIdx.x; i < D; i += kDecThreads) {
+                    kt[r * KS + i] = knew[i];
+                    vt[r * D + i] = vnew[i];
+                }
+                __syncthreads();
+            }
         }
-        // Rotate keys in place at their local positions (tab rows).
+        // Rotate keys in place at their local positions (tab rows): each
+        // thread the pieces it staged itself (a single tile's new row is
+        // already rotated).
         for (uint32_t i = threadIdx.x; i < rows * 16; i += kDecThreads) {
             const uint32_t r = i >> 4, d = (i & 15) * 4;
+            if (single && base + r == P) continue;
             const float4 a = ld4(kt + r * KS + d), b = ld4(kt + r * KS + H + d);
             const float4 c = ld4(tab + r * D + d), sn = ld4(tab + r * D + H + d);
             float4 lo4, hi4;
@@ -847,23 +892,26 @@ __device__ __forceinline__ void decode_attention128_body(const DecodeAttnParams 
     cluster.sync();
     {
         float *w = kt;  // [G][S] weights, then [G] denominators
-        if (threadIdx.x < G) {
-            const uint32_t g = threadIdx.x;
-            float ms[S];
-            float M = -__int_as_float(0x7f800000);
+        // One (head, split) pair per lane, a head's S splits on S consecutive
+        // lanes of one warp: the max over splits by shuffles, one exp each,
+        // then the denominator as the same in-order FMA chain over splits.
+        for (uint32_t t0 = static_cast<uint32_t>(warp) * 32; t0 < G * S; t0 += warps * 32) {
+            const uint32_t t = t0 + lane, g = t / S, r = t % S;
+            const bool valid = t < G * S;
+            const float m = valid ? cluster.map_shared_rank(mrow, r)[g] : -__int_as_float(0x7f800000);
+            const float l = valid ? cluster.map_shared_rank(lrow, r)[g] : 0.0f;
+            float M = m;
 #pragma unroll
-            for (int r = 0; r < S; ++r) {
-                ms[r] = cluster.map_shared_rank(mrow, r)[g];
-                M = fmaxf(M, ms[r]);
-            }
+            for (int o = S / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            const float e = plamo_exp(__fsub_rn(m, M));
+            if (valid) w[g * S + r] = e;
             float Ls = 0.0f;
 #pragma unroll
-            for (int r = 0; r < S; ++r) {
-                const float e = plamo_exp(__fsub_rn(ms[r], M));
-                w[g * S + r] = e;
-                Ls = fmaf(cluster.map_shared_rank(lrow, r)[g], e, Ls);
+            for (int q = 0; q < S; ++q) {
+                const int src = static_cast<int>((lane & ~static_cast<uint32_t>(S - 1)) + q);
+                Ls = fmaf(__shfl_sync(0xffffffffu, l, src), __shfl_sync(0xffffffffu, e, src), Ls);
             }
-            w[G * S + g] = Ls;
+            if (valid && r == 0) w[G * S + g] = Ls;
         }
         __syncthreads();
         const uint32_t per = (G * D + S - 1) / S, i0 = cluster.block_rank() * per;
