@@ -24,6 +24,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "rows.cuh"
 
 namespace plamo {
 
@@ -154,6 +155,10 @@ struct AttnParams {
     uint32_t *tickets; // [tokens][kh] arrival counters (zero between launches)
     uint32_t splits;
     uint32_t t0;       // first query token of this launch (blockIdx.y counts from it)
+    // When set, the output's BF16 terms for the next projection (three planes
+    // split_plane apart, indexed as out).
+    uint16_t *split = nullptr;
+    uint64_t split_plane = 0;
 };
 
 // One CTA per (kv head, query token, key split). Keys of the split are
@@ -256,7 +261,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
     if (p.splits == 1) {
         for (uint64_t i = threadIdx.x; i < G * D; i += blockDim.x) {
             const uint64_t g = i / D, d = i % D;
-            p.out[(t * QH + kh * G + g) * D + d] = __fdiv_rn(acc[i], lrow[g]);
+            const float o = __fdiv_rn(acc[i], lrow[g]);
+            const uint64_t at = (t * QH + kh * G + g) * D + d;
+            p.out[at] = o;
+            if (p.split) split3(o, p.split + at, p.split + p.split_plane + at, p.split + 2 * p.split_plane + at);
         }
         pdl_launch_dependents();
         return;
@@ -293,7 +301,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
             Ls = fmaf(base[s * pstride + D + 1], e, Ls);
             A = fmaf(base[s * pstride + d], e, A);
         }
-        p.out[(t * QH + kh * G + g) * D + d] = __fdiv_rn(A, Ls);
+        const float o = __fdiv_rn(A, Ls);
+        const uint64_t at = (t * QH + kh * G + g) * D + d;
+        p.out[at] = o;
+        if (p.split) split3(o, p.split + at, p.split + p.split_plane + at, p.split + 2 * p.split_plane + at);
     }
     __syncthreads();
     if (threadIdx.x == 0) p.tickets[t * KH + kh] = 0;
@@ -347,6 +358,8 @@ struct PromptAttnParams {
     uint32_t qh, kh, qkv_stride;
     uint32_t tokens;     // queries [0, tokens) of this call
     uint32_t per_block;  // query tokens per CTA: rows per CTA / G
+    uint16_t *split;     // the output's BF16 terms for the next projection (planes split_plane apart), or null
+    uint64_t split_plane;
 };
 
 // Keys [0, keys) of a layer whose window starts at row 0, each rotated at its
@@ -561,7 +574,13 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attention_kernel(PromptAttn
         const float inv = lsum[r];
         float4 o = make_float4(__fdiv_rn(acc[i][0], inv), __fdiv_rn(acc[i][1], inv), __fdiv_rn(acc[i][2], inv),
                                __fdiv_rn(acc[i][3], inv));
-        *reinterpret_cast<float4 *>(p.out + (static_cast<size_t>(t0 + qi) * p.qh + kh * G + g) * D + lane * 4) = o;
+        const uint64_t at = (static_cast<uint64_t>(t0 + qi) * p.qh + kh * G + g) * D + lane * 4;
+        *reinterpret_cast<float4 *>(p.out + at) = o;
+        if (p.split) {
+            RowFuse f{};
+            f.split = p.split;
+            fuse_split4(f, p.split_plane, at, o);
+        }
     }
     pdl_launch_dependents();
 }

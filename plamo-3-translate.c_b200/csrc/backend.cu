@@ -1388,6 +1388,10 @@ bool check_device_error(plamo_cuda *c, DModel *m) {
 // per-token kernel; both give the same bits.
 bool prompt_attention(plamo_cuda *c, DModel *m, uint64_t l, uint64_t T, size_t attn_smem) {
     const DLayer &L = m->layers[l];
+    // The o projection's BF16 input terms, written by the attention kernels
+    // themselves when that projection runs on the tensor cores.
+    uint16_t *const o_terms = row_fuse(c, m, L.o_w, T, m->H, m->AW, Deferred{}).split;
+    const uint64_t o_plane = T * m->AW;
     const AttnLayer al = attn_layer(m, l);
     const AttnShape shape{T, m->QH, m->KH, m->D, m->QW};
     const uint64_t G = m->QH / m->KH;
@@ -1418,7 +1422,9 @@ bool prompt_attention(plamo_cuda *c, DModel *m, uint64_t l, uint64_t T, size_t a
                             static_cast<uint32_t>(m->KH),
                             static_cast<uint32_t>(m->QW),
                             static_cast<uint32_t>(blocked),
-                            per_block};
+                            per_block,
+                            o_terms,
+                            o_plane};
         const dim3 grid(static_cast<uint32_t>((blocked + per_block - 1) / per_block), static_cast<uint32_t>(m->KH));
         if (!(narrow ? (c->prompt_bufs == 1 ? launch(c, prompt_attention_kernel<32, 1>, grid, dim3(kPaThreads),
                                                      prompt_attention_smem_bytes<32, 1>(), pp)
@@ -1431,7 +1437,7 @@ bool prompt_attention(plamo_cuda *c, DModel *m, uint64_t l, uint64_t T, size_t a
     if (blocked == T) return true;
     const uint32_t splits = T >= 16 ? 1u : m->splits;
     AttnParams ap{al, shape, m->p_q, m->p_qkv, m->p_attn, m->p_part, m->p_tickets, splits,
-                  static_cast<uint32_t>(blocked)};
+                  static_cast<uint32_t>(blocked), o_terms, o_plane};
     return launch(c, attention_kernel, dim3(m->KH, T - blocked, splits), dim3(kAttnThreads), attn_smem, ap);
 }
 
@@ -1486,7 +1492,9 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
                 return false;
         }
         Deferred o_parts;
-        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW, false, tp ? nullptr : &o_parts))
+        const bool o_terms = row_fuse(c, m, L.o_w, T, H, m->AW, Deferred{}).split != nullptr;
+        if (!projection(c, m, m->p_attn, m->AW, L.o_w, m->p_branch, H, T, H, m->AW, o_terms,
+                        tp ? nullptr : &o_parts))
             return false;
         if (tp && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l)) return false;
         f = row_fuse(c, m, L.gu, T, 2 * m->I, H, o_parts);
