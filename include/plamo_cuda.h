@@ -56,7 +56,8 @@ struct plamo_cuda;
 struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *, char *error, size_t cap);
 /* reference runtime/metal.h:49 */
 void plamo_cuda_close(struct plamo_cuda *);
-/* reference runtime/metal.h:50: releases scratch not needed by prepared models. */
+/* reference runtime/metal.h:50: releases scratch not needed by prepared models,
+   including the KV page chunks of a pool none of whose pages is mapped. */
 void plamo_cuda_maintain(struct plamo_cuda *);
 /* reference runtime/metal.h:51 */
 void plamo_cuda_get_info(const struct plamo_cuda *, struct plamo_cuda_info *);

@@ -1727,7 +1727,22 @@ void plamo_cuda_close(struct plamo_cuda *c) {
 }
 
 void plamo_cuda_maintain(struct plamo_cuda *c) {
-    if (c) cudaStreamSynchronize(c->stream);
+    if (!c) return;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    // KV page chunks go back to the device once no request maps any of their
+    // pool's pages (the spare page stays: page tables point at it).
+    for (auto &kv : c->kv_pools) {
+        KvPool &pool = kv.second;
+        if (pool.used || pool.chunks.empty()) continue;
+        const uint64_t chunk_bytes = kKvChunkPages * kv_page_floats(kv.first) * 4;
+        for (float *chunk : pool.chunks) cudaFree(chunk);
+        c->info.kv_bytes -= pool.chunks.size() * chunk_bytes;
+        c->info.allocated_bytes -= pool.chunks.size() * chunk_bytes;
+        c->info.kv_pages_allocated -= pool.chunks.size() * kKvChunkPages;
+        pool.chunks.clear();
+        pool.free.clear();
+    }
 }
 
 void plamo_cuda_get_info(const struct plamo_cuda *c, struct plamo_cuda_info *info) {

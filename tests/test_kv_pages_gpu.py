@@ -97,3 +97,7 @@ def test_reset_and_release_return_pages_for_reuse(backend):
     finally:
         backend.release(a)
     assert backend.info().kv_pages_used == 0
+    # With no page mapped, maintenance gives the pool's chunks back.
+    assert backend.info().kv_pages_allocated > 0
+    backend.lib.plamo_cuda_maintain(backend.ctx)
+    assert backend.info().kv_pages_allocated == 0
