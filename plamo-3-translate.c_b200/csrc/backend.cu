@@ -176,6 +176,7 @@ struct plamo_cuda {
     int gemv_ring_kb;
     int tc_stages;  // tcgen05 projection ring depth (0: as many as shared memory holds)
     int tc_tokm;    // token-major tcgen05 tiles for prompts: -1 by waves, 0 never, 1 always (PLAMO_CUDA_TC_TOKM)
+    int tc_tokn;    // token-major tile width: 0 by waves, else 144, 160 or 192 (PLAMO_CUDA_TC_TOKN)
     float draft_margin;         // PLAMO_DRAFT_MIN_MARGIN, or -1: the reference's default rule
     unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
     bool tc_gemm;
@@ -523,32 +524,47 @@ bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, cons
                   stages);
 }
 
-// Token-major tiles (128 tokens x kTcTokN weight rows) or weight-major ones
-// (128 weight rows x 128 tokens) for a prompt of more than 64 tokens: one CTA
-// per SM either way, so the choice compares waves of tiles, a token-major tile
-// costing 1.2 weight-major ones (1.5 times the MMAs at 0.81 of the cost per
-// MMA, measured on the 8B gate_up projection). 8B, 455 tokens: qkv 116.8 ->
-// 85.8 us and gate_up 408 -> 356 us token-major; o_proj and down_proj (4096
-// rows, one wave either way) stay weight-major. PLAMO_CUDA_TC_TOKM=0 / 1
-// forces weight-major / token-major tiles.
-constexpr uint32_t kTcTokN = 192;
-bool tc_token_major(plamo_cuda *c, uint64_t T, uint64_t R) {
-    if (T <= 64 || c->tc_tokm == 0) return false;
-    if (c->tc_tokm == 1) return true;
-    const uint64_t sms = static_cast<uint64_t>(c->sm_count);
-    const uint64_t wm = (((T + 127) / 128) * ((R + kTcM - 1) / kTcM) + sms - 1) / sms;
-    const uint64_t tm = (((T + kTcM - 1) / kTcM) * ((R + kTcTokN - 1) / kTcTokN) + sms - 1) / sms;
-    return tm * 6 < wm * 5;
+// Token-major tiles (128 tokens x 144, 160 or 192 weight rows) or weight-major
+// ones (128 weight rows x 128 tokens) for a prompt of more than 64 tokens: one
+// CTA per SM either way, so the choice compares waves of tiles times a wave's
+// cost, measured on the 8B projections of a 455-token prompt (CUDA events,
+// B200) relative to a weight-major wave: 1.06 for 144 rows, 1.11 for 160,
+// 1.18 for 192. That sends qkv (5120 rows) to one wave of 144-row tiles
+// (66.5 us; 192 rows 73.3, weight-major 108.2), gate_up (32768 rows) to five
+// waves of 192-row tiles (316.4 us; 160 rows 352.9, weight-major 361.1) and
+// keeps o_proj and down_proj (4096 rows) weight-major (215.3 us against 224.7
+// for 144 rows). Ties go to the weight-major, then to the wider tile.
+// PLAMO_CUDA_TC_TOKM=0 / 1 forces weight-major / token-major tiles,
+// PLAMO_CUDA_TC_TOKN=144 / 160 / 192 the token-major width.
+constexpr uint32_t kTcTokWidths[3] = {192, 160, 144};
+constexpr uint64_t kTcTokCost[3] = {118, 111, 106};  // per wave, weight-major = 100
+uint32_t tc_token_cols(plamo_cuda *c, uint64_t T, uint64_t R) {
+    if (T <= 64 || c->tc_tokm == 0) return 0;
+    const uint64_t sms = static_cast<uint64_t>(c->sm_count), tt = (T + kTcM - 1) / kTcM;
+    auto waves = [&](uint64_t tiles) { return (tiles + sms - 1) / sms; };
+    uint64_t best_cost = c->tc_tokm == 1 ? ~0ull : waves(tt * ((R + kTcM - 1) / kTcM)) * 100;
+    uint32_t best = 0;
+    for (int i = 0; i < 3; ++i) {
+        const uint32_t n = kTcTokWidths[i];
+        if (c->tc_tokn && n != static_cast<uint32_t>(c->tc_tokn)) continue;
+        const uint64_t cost = waves(tt * ((R + n - 1) / n)) * kTcTokCost[i];
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = n;
+        }
+    }
+    return best;
 }
 
+template <int N>
 bool launch_tc_tokm(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &mm,
                     const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T) {
     const size_t budget = static_cast<size_t>(c->smem_optin) - 2048;
-    int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, budget / tc_stage_bytes(kTcTokN, true)));
+    int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, budget / tc_stage_bytes(N, true)));
     if (c->tc_stages) stages = std::min(stages, c->tc_stages);
-    const dim3 grid((T + kTcM - 1) / kTcM, (R + kTcTokN - 1) / kTcTokN, 1);
-    return launch(c, gemm_tc_kernel<kTcTokN, true>, grid, dim3(tc_threads<kTcTokN>()),
-                  tc_smem_bytes(kTcTokN, stages, true), mw, mh, mm, ml, p, stages);
+    const dim3 grid((T + kTcM - 1) / kTcM, (R + N - 1) / N, 1);
+    return launch(c, gemm_tc_kernel<N, true>, grid, dim3(tc_threads<N>()), tc_smem_bytes(N, stages, true), mw, mh,
+                  mm, ml, p, stages);
 }
 
 // Y[T][R] (row stride ys) = X[T][K] (row stride xs, FP32) . W[R][K]^T on the
@@ -584,13 +600,16 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
     if (!presplit && !launch(c, split_hilo_kernel, dim3(blocks), dim3(256), 0, X, xs, static_cast<uint32_t>(T),
                              static_cast<uint32_t>(K), hi, mid, lo))
         return false;
-    if (tc_token_major(c, T, R)) {
+    if (const uint32_t tn = tc_token_cols(c, T, R)) {
         CUtensorMap mw, mh, mm, ml;
-        if (bf16_map(&mw, W, R, K, kTcTokN) && bf16_map(&mh, hi, T, K, kTcM) && bf16_map(&mm, mid, T, K, kTcM) &&
+        if (bf16_map(&mw, W, R, K, tn) && bf16_map(&mh, hi, T, K, kTcM) && bf16_map(&mm, mid, T, K, kTcM) &&
             bf16_map(&ml, lo, T, K, kTcM)) {
             TcGemmParams p{Y, ys, static_cast<uint32_t>(T), static_cast<uint32_t>(R), static_cast<uint32_t>(K),
                            error, part};
-            return launch_tc_tokm(c, mw, mh, mm, ml, p, static_cast<uint32_t>(R), static_cast<uint32_t>(T));
+            const uint32_t r32 = static_cast<uint32_t>(R), t32 = static_cast<uint32_t>(T);
+            return tn == 144   ? launch_tc_tokm<144>(c, mw, mh, mm, ml, p, r32, t32)
+                   : tn == 160 ? launch_tc_tokm<160>(c, mw, mh, mm, ml, p, r32, t32)
+                               : launch_tc_tokm<192>(c, mw, mh, mm, ml, p, r32, t32);
         }
     }
     const uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
@@ -1642,6 +1661,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_stages = tc_st ? std::max(2, std::min(atoi(tc_st), kTcMaxStages)) : 0;
     const char *tokm = getenv("PLAMO_CUDA_TC_TOKM");
     c->tc_tokm = tokm && (!strcmp(tokm, "0") || !strcmp(tokm, "1")) ? atoi(tokm) : -1;
+    const char *tokn = getenv("PLAMO_CUDA_TC_TOKN");
+    c->tc_tokn = tokn && (!strcmp(tokn, "144") || !strcmp(tokn, "160") || !strcmp(tokn, "192")) ? atoi(tokn) : 0;
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
     c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
@@ -1688,7 +1709,9 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     allow_smem(gemm_tc_kernel<32>, optin, carveout);
     allow_smem(gemm_tc_kernel<64>, optin, carveout);
     allow_smem(gemm_tc_kernel<128>, optin, carveout);
-    allow_smem(gemm_tc_kernel<kTcTokN, true>, optin, carveout);
+    allow_smem(gemm_tc_kernel<144, true>, optin, carveout);
+    allow_smem(gemm_tc_kernel<160, true>, optin, carveout);
+    allow_smem(gemm_tc_kernel<192, true>, optin, carveout);
     allow_smem(decode_attention_kernel<128>, optin, carveout);
     allow_smem(decode_attention128_batch_kernel, optin, carveout);
     allow_smem(decode_attention_kernel<0>, optin, carveout);

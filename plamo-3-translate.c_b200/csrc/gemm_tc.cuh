@@ -62,9 +62,27 @@ constexpr int kTcAccMax = 16;
 // TMEM accumulators (one K block each) in a ring of 256 columns: with few
 // tokens per tile a K block is quick to multiply, so the MMAs may run up to
 // 16 blocks ahead of the epilogue's folds instead of stalling on it.
-template <int N>
+// TMEM columns between accumulators: a token-major tile's accumulators start
+// on 32-column boundaries (the folds' 32-column loads stay aligned).
+template <int N, bool TOKM = false>
+__host__ __device__ constexpr int tc_acc_stride() {
+    return TOKM ? (N + 31) / 32 * 32 : N;
+}
+// A token-major tile allocates all 512 columns (two accumulators of 192
+// columns round up to it), so it keeps as many accumulators as they hold:
+// two of 192 columns, three of 144 or 160. A 128-token weight-major tile
+// keeps two in 256 columns: four (all 512) measured slower on the 8B
+// down_proj (219 against 214 us), the next launch's CTAs then waiting for
+// TMEM.
+template <int N, bool TOKM = false>
 __host__ __device__ constexpr int tc_acc_count() {
-    return N <= 16 ? 16 : N <= 32 ? 8 : N <= 64 ? 4 : 2;
+    return TOKM ? 512 / tc_acc_stride<N, true>() : N <= 16 ? 16 : N <= 32 ? 8 : N <= 64 ? 4 : 2;
+}
+// Columns folded by the first of a lane quadrant's two epilogue warps (the
+// second takes the rest): a multiple of 32, so both start 32-aligned.
+template <int N>
+__host__ __device__ constexpr int tc_fold_split() {
+    return tc_epi_warps<N>() == 8 ? 32 * (N / 64) : N;
 }
 constexpr int kTcTerms = 3;  // BF16 terms of each FP32 activation (2 or 3: loads and MMAs follow it)
 static_assert(kTcTerms == 2 || kTcTerms == 3, "two or three BF16 terms");
@@ -134,6 +152,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 columns without the wait: several loads in flight, then one tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // 16 consecutive FP32 accumulator columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -163,6 +195,112 @@ __host__ __device__ constexpr uint32_t tc_pow2_cols(uint32_t cols) {
     return p;
 }
 
+// Everything an epilogue warp needs from its CTA.
+struct TcEpilogue {
+    TcGemmParams p;
+    uint32_t tmem, warp, lane, kblocks;
+    uint64_t *acc_full, *acc_empty;
+    int *abort_flag;
+    unsigned char *base;  // the stage buffers (the token-major store's staging tile)
+    uint32_t row0, tok0;
+};
+
+// Add COUNT accumulator columns at taddr (32-aligned start) into sum.
+template <int COUNT>
+__device__ __forceinline__ void tc_fold_block(float (&sum)[COUNT], uint32_t taddr) {
+    static_assert(COUNT % 16 == 0, "folds move 16 or 32 columns per load");
+    if constexpr (COUNT % 64 == 0) {
+        // Two loads in flight per wait.
+#pragma unroll
+        for (int c = 0; c < COUNT; c += 64) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32_async(taddr + c, r0);
+            tmem_ld32_async(taddr + c + 32, r1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                sum[c + i] = __fadd_rn(sum[c + i], __uint_as_float(r0[i]));
+                sum[c + 32 + i] = __fadd_rn(sum[c + 32 + i], __uint_as_float(r1[i]));
+            }
+        }
+    } else {
+        // One load per wait (96 or 80 columns: two in flight would spill).
+        constexpr int C32 = COUNT / 32 * 32;
+#pragma unroll
+        for (int c = 0; c < C32; c += 32) {
+            float v[32];
+            tmem_ld32(taddr + c, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sum[c + i] = __fadd_rn(sum[c + i], v[i]);
+        }
+        if constexpr (COUNT > C32) {
+            float v[16];
+            tmem_ld16(taddr + C32, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[C32 + i] = __fadd_rn(sum[C32 + i], v[i]);
+        }
+    }
+}
+
+// Fold every K block's partial into FP32 registers (IEEE adds, in order) for
+// this warp's TMEM lane quadrant, columns [COL0, COL0 + COUNT), then store
+// them (or the split-K partial tile).
+template <int N, bool TOKM, int COL0, int COUNT, int ACC, uint32_t STRIDE>
+__device__ __forceinline__ void tc_fold_store(const TcEpilogue &e) {
+    const TcGemmParams &p = e.p;
+    const uint32_t quad = e.warp & 3;  // TMEM lanes this warp may access
+    const uint32_t lanes = (quad * 32) << 16;
+    float sum[COUNT];
+#pragma unroll
+    for (int i = 0; i < COUNT; ++i) sum[i] = 0.0f;
+    bool ok = true;
+    for (uint32_t kb = 0; kb < e.kblocks; ++kb) {
+        const uint32_t a = kb % ACC;
+        if (!mbar_wait(&e.acc_full[a], (kb / ACC) & 1u) || *reinterpret_cast<volatile int *>(e.abort_flag)) {
+            ok = false;
+            if (p.error && e.lane == 0) atomicExch(p.error, 3u);
+            break;
+        }
+        tc_fence_after();
+        tc_fold_block<COUNT>(sum, e.tmem + lanes + a * STRIDE + COL0);
+        tc_fence_before();
+        __syncwarp();
+        if (e.lane == 0) mbar_arrive(&e.acc_empty[a]);
+    }
+    float *out = gridDim.z > 1 ? p.part + static_cast<uint64_t>(blockIdx.z) * p.T * p.R : p.y;
+    const uint64_t stride = gridDim.z > 1 ? p.R : p.ys;
+    if constexpr (TOKM) {
+        // This lane is one token and its columns are consecutive weight
+        // rows, so direct stores would scatter 32 output rows per
+        // instruction. The tile goes through shared memory instead (the
+        // stage buffers: every copy has landed and every MMA has read
+        // them once the last block is folded), then each warp writes
+        // whole token rows, 32 consecutive floats per instruction.
+        constexpr uint32_t OS = N + 1;  // odd row stride: the column writes hit 32 banks
+        float *tile = reinterpret_cast<float *>(e.base);
+        const uint32_t tl = quad * 32 + e.lane;
+#pragma unroll
+        for (int j = 0; j < COUNT; ++j) tile[tl * OS + COL0 + j] = sum[j];
+        asm volatile("bar.sync 1, %0;" ::"r"(tc_epi_warps<N>() * 32) : "memory");
+        const uint32_t ew = e.warp - 2;
+        for (uint32_t r = ew; r < kTcM; r += tc_epi_warps<N>()) {
+            const uint32_t t = e.tok0 + r;
+            if (!ok || t >= p.T) continue;
+            for (uint32_t c = e.lane; c < N; c += 32)
+                if (e.row0 + c < p.R) out[static_cast<uint64_t>(t) * stride + e.row0 + c] = tile[r * OS + c];
+        }
+    } else {
+        const uint32_t row = e.row0 + quad * 32 + e.lane;
+        if (ok && row < p.R) {
+#pragma unroll
+            for (int j = 0; j < COUNT; ++j) {
+                const uint32_t t = e.tok0 + COL0 + j;
+                if (t < p.T) out[static_cast<uint64_t>(t) * stride + row] = sum[j];
+            }
+        }
+    }
+}
+
 // Two tile layouts (TOKM):
 //   weight-major (false): A = 128 weight rows, B = N tokens' terms; the
 //     accumulator's TMEM lanes are weight rows, its columns tokens (N a
@@ -179,7 +317,7 @@ __global__ void __launch_bounds__(tc_threads<N>(), 1)
     extern __shared__ __align__(128) unsigned char tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kTcMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kTcMaxStages];
-    constexpr int kTcAcc = tc_acc_count<N>();
+    constexpr int kTcAcc = tc_acc_count<N, TOKM>();
     __shared__ __align__(8) uint64_t acc_full[kTcAccMax];
     __shared__ __align__(8) uint64_t acc_empty[kTcAccMax];
     __shared__ uint32_t tmem_base;
@@ -213,7 +351,8 @@ __global__ void __launch_bounds__(tc_threads<N>(), 1)
         prefetch_tensormap(&map_mid);
         prefetch_tensormap(&map_lo);
     }
-    constexpr uint32_t kCols = tc_pow2_cols(kTcAcc * N);  // power of two >= 32
+    constexpr uint32_t kStride = tc_acc_stride<N, TOKM>();
+    constexpr uint32_t kCols = tc_pow2_cols(kTcAcc * kStride);  // power of two >= 32
     if (warp == 1) {  // the whole warp allocates the accumulators' TMEM columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                      "r"(kCols)
@@ -275,7 +414,7 @@ __global__ void __launch_bounds__(tc_threads<N>(), 1)
             }
             tc_fence_after();
             const uint32_t sa = smem_u32(base + s * stage_bytes);
-            const uint32_t acc = tmem + a * N;
+            const uint32_t acc = tmem + a * kStride;
             if constexpr (TOKM) {
                 // A: the terms' [128 tokens] tiles; B: the weight tile.
                 const uint32_t th = sa, tm = th + kTcM * 128, tl = tm + kTcM * 128;
@@ -305,73 +444,14 @@ __global__ void __launch_bounds__(tc_threads<N>(), 1)
             }
         }
     } else if (warp >= 2) {
-        // Fold every K block's partial into FP32 registers (IEEE adds, in order):
-        // this warp's TMEM lane quadrant, columns [col0, col0 + NC).
-        constexpr int NC = N * 4 / tc_epi_warps<N>();
-        const uint32_t quad = warp & 3;  // TMEM lanes this warp may access
-        const uint32_t lanes = (quad * 32) << 16;
-        const uint32_t col0 = static_cast<uint32_t>((warp - 2) / 4) * NC;
-        float sum[NC];
-#pragma unroll
-        for (int i = 0; i < NC; ++i) sum[i] = 0.0f;
-        bool ok = true;
-        for (uint32_t kb = 0; kb < kblocks; ++kb) {
-            const uint32_t a = kb % kTcAcc;
-            if (!mbar_wait(&acc_full[a], (kb / kTcAcc) & 1u) || *reinterpret_cast<volatile int *>(&abort_flag)) {
-                ok = false;
-                if (p.error && lane == 0) atomicExch(p.error, 3u);
-                break;
-            }
-            tc_fence_after();
-            if constexpr (NC == 16) {
-                float v[16];
-                tmem_ld16(tmem + lanes + a * N + col0, v);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) sum[i] = __fadd_rn(sum[i], v[i]);
-            } else {
-#pragma unroll
-                for (int c = 0; c < NC; c += 32) {
-                    float v[32];
-                    tmem_ld32(tmem + lanes + a * N + col0 + c, v);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) sum[c + i] = __fadd_rn(sum[c + i], v[i]);
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[a]);
-        }
-        float *out = gridDim.z > 1 ? p.part + static_cast<uint64_t>(blockIdx.z) * p.T * p.R : p.y;
-        const uint64_t stride = gridDim.z > 1 ? p.R : p.ys;
-        if constexpr (TOKM) {
-            // This lane is one token and its columns are consecutive weight
-            // rows, so direct stores would scatter 32 output rows per
-            // instruction. The tile goes through shared memory instead (the
-            // stage buffers: every copy has landed and every MMA has read
-            // them once the last block is folded), then each warp writes
-            // whole token rows, 32 consecutive floats per instruction.
-            constexpr uint32_t OS = N + 1;  // odd row stride: the column writes hit 32 banks
-            float *tile = reinterpret_cast<float *>(base);
-            const uint32_t tl = quad * 32 + lane;
-#pragma unroll
-            for (int j = 0; j < NC; ++j) tile[tl * OS + col0 + j] = sum[j];
-            asm volatile("bar.sync 1, %0;" ::"r"(tc_epi_warps<N>() * 32) : "memory");
-            const uint32_t ew = static_cast<uint32_t>(warp - 2);
-            for (uint32_t r = ew; r < kTcM; r += tc_epi_warps<N>()) {
-                const uint32_t t = tok0 + r;
-                if (!ok || t >= p.T) continue;
-                for (uint32_t c = lane; c < N; c += 32)
-                    if (row0 + c < p.R) out[static_cast<uint64_t>(t) * stride + row0 + c] = tile[r * OS + c];
-            }
+        constexpr int C0 = tc_fold_split<N>();
+        const TcEpilogue e{p, tmem, static_cast<uint32_t>(warp), static_cast<uint32_t>(lane), kblocks, acc_full,
+                           acc_empty, &abort_flag, base, row0, tok0};
+        if constexpr (C0 < N) {
+            if ((warp - 2) / 4 == 0) tc_fold_store<N, TOKM, 0, C0, kTcAcc, kStride>(e);
+            else tc_fold_store<N, TOKM, C0, N - C0, kTcAcc, kStride>(e);
         } else {
-            const uint32_t row = row0 + quad * 32 + lane;
-            if (ok && row < p.R) {
-#pragma unroll
-                for (int j = 0; j < NC; ++j) {
-                    const uint32_t t = tok0 + col0 + j;
-                    if (t < p.T) out[static_cast<uint64_t>(t) * stride + row] = sum[j];
-                }
-            }
+            tc_fold_store<N, TOKM, 0, N, kTcAcc, kStride>(e);
         }
     }
     tc_fence_before();

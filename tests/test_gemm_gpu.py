@@ -57,14 +57,20 @@ def test_tc_projection_matches_oracle(backend, T, R, K):
     assert rel_l2(got, want) <= 1e-5, rel_l2(got, want)
 
 
-@pytest.mark.parametrize("layout", ["0", "1"])
+@pytest.mark.parametrize("layout", ["0", "1:192", "1:160", "1:144"])
 @pytest.mark.parametrize("T,R,K", [(65, 200, 72), (129, 385, 1024), (455, 5120, 4096), (300, 1000, 520)])
 def test_tc_tile_layouts_match_oracle(monkeypatch, layout, T, R, K):
-    """Both tile layouts of a prompt projection (PLAMO_CUDA_TC_TOKM=0:
-    128 weight rows x 128 tokens; =1: 128 tokens x 192 weight rows, stored
-    through shared memory), with ragged token and row tiles and K tails."""
+    """Every tile layout of a prompt projection (PLAMO_CUDA_TC_TOKM=0:
+    128 weight rows x 128 tokens; =1: 128 tokens x 192, 160 or 144 weight
+    rows (PLAMO_CUDA_TC_TOKN), stored through shared memory), with ragged
+    token and row tiles and K tails."""
     from conftest import load_package
-    monkeypatch.setenv("PLAMO_CUDA_TC_TOKM", layout)
+    tokm, _, tokn = layout.partition(":")
+    monkeypatch.setenv("PLAMO_CUDA_TC_TOKM", tokm)
+    if tokn:
+        monkeypatch.setenv("PLAMO_CUDA_TC_TOKN", tokn)
+    else:
+        monkeypatch.delenv("PLAMO_CUDA_TC_TOKN", raising=False)
     pkg = load_package()
     b = pkg.Backend(device=0, max_context=64, max_prefill=512)
     try:
