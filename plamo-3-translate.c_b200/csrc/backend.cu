@@ -119,6 +119,7 @@ struct DModel {
     float *p_rotk;  // rotated keys of the blocked prompt attention [max capacity][KVW]
     uint32_t *p_ids, *p_next, *p_tickets;
     uint16_t *p_split;  // BF16 hi/mid/lo terms of a projection input, 3 x [T][K]
+    uint16_t *p_glu;    // BF16 terms of the SwiGLU output of a fused gate/up projection, 3 x [T][I]
     float *p_splitk;    // split-K partial tiles of small-token projections
     float *v_kv;  // [L][kVerifyMax][2][KVW]
     uint64_t verify_count = 0, verify_committed = 0;
@@ -177,6 +178,7 @@ struct plamo_cuda {
     int tc_stages;  // tcgen05 projection ring depth (0: as many as shared memory holds)
     int tc_tokm;    // token-major tcgen05 tiles for prompts: -1 by waves, 0 never, 1 always (PLAMO_CUDA_TC_TOKM)
     int tc_tokn;    // token-major tile width: 0 by waves, else 144, 160 or 192 (PLAMO_CUDA_TC_TOKN)
+    int tc_glu;     // prompt gate/up projection fused with SwiGLU (PLAMO_CUDA_TC_GLU, default 1)
     float draft_margin;         // PLAMO_DRAFT_MIN_MARGIN, or -1: the reference's default rule
     unsigned draft_min_tokens;  // PLAMO_DRAFT_MIN_TOKENS, or 0: the reference's default rule
     bool tc_gemm;
@@ -520,8 +522,8 @@ bool launch_tc(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, cons
     int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, budget / tc_stage_bytes(N)));
     if (c->tc_stages) stages = std::min(stages, c->tc_stages);
     const dim3 grid((T + N - 1) / N, (R + kTcM - 1) / kTcM, splits);
-    return launch(c, gemm_tc_kernel<N>, grid, dim3(tc_threads<N>()), tc_smem_bytes(N, stages), mw, mh, mm, ml, p,
-                  stages);
+    return launch(c, gemm_tc_kernel<N>, grid, dim3(tc_threads<N>()), tc_smem_bytes(N, stages), mw, mw, mh, mm, ml,
+                  p, stages);
 }
 
 // Token-major tiles (128 tokens x 144, 160 or 192 weight rows) or weight-major
@@ -556,15 +558,16 @@ uint32_t tc_token_cols(plamo_cuda *c, uint64_t T, uint64_t R) {
     return best;
 }
 
+// mu: the up rows' map of a gate/up-paired launch (p.glu), else mw again.
 template <int N>
-bool launch_tc_tokm(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mh, const CUtensorMap &mm,
-                    const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T) {
+bool launch_tc_tokm(plamo_cuda *c, const CUtensorMap &mw, const CUtensorMap &mu, const CUtensorMap &mh,
+                    const CUtensorMap &mm, const CUtensorMap &ml, const TcGemmParams &p, uint32_t R, uint32_t T) {
     const size_t budget = static_cast<size_t>(c->smem_optin) - 2048;
     int stages = static_cast<int>(std::min<size_t>(kTcMaxStages, budget / tc_stage_bytes(N, true)));
     if (c->tc_stages) stages = std::min(stages, c->tc_stages);
     const dim3 grid((T + kTcM - 1) / kTcM, (R + N - 1) / N, 1);
-    return launch(c, gemm_tc_kernel<N, true>, grid, dim3(tc_threads<N>()), tc_smem_bytes(N, stages, true), mw, mh,
-                  mm, ml, p, stages);
+    return launch(c, gemm_tc_kernel<N, true>, grid, dim3(tc_threads<N>()), tc_smem_bytes(N, stages, true), mw, mu,
+                  mh, mm, ml, p, stages);
 }
 
 // Y[T][R] (row stride ys) = X[T][K] (row stride xs, FP32) . W[R][K]^T on the
@@ -594,6 +597,7 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
     if (defer) *defer = Deferred{};
     if (!T || !R) return true;
     const bool tc = split && tc_projection(c, W, T, R, K);
+    if (!tc && !X) return false;  // only BF16 terms of the input exist
     if (!tc) return gemm(c, X, xs, W, Y, ys, T, R, K);
     uint16_t *hi = split, *mid = split + T * K, *lo = split + 2 * T * K;
     const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((T * K + 255) / 256, 8192));
@@ -607,9 +611,9 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
             TcGemmParams p{Y, ys, static_cast<uint32_t>(T), static_cast<uint32_t>(R), static_cast<uint32_t>(K),
                            error, part};
             const uint32_t r32 = static_cast<uint32_t>(R), t32 = static_cast<uint32_t>(T);
-            return tn == 144   ? launch_tc_tokm<144>(c, mw, mh, mm, ml, p, r32, t32)
-                   : tn == 160 ? launch_tc_tokm<160>(c, mw, mh, mm, ml, p, r32, t32)
-                               : launch_tc_tokm<192>(c, mw, mh, mm, ml, p, r32, t32);
+            return tn == 144   ? launch_tc_tokm<144>(c, mw, mw, mh, mm, ml, p, r32, t32)
+                   : tn == 160 ? launch_tc_tokm<160>(c, mw, mw, mh, mm, ml, p, r32, t32)
+                               : launch_tc_tokm<192>(c, mw, mw, mh, mm, ml, p, r32, t32);
         }
     }
     const uint32_t N = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : 128;
@@ -617,7 +621,7 @@ bool projection_with(plamo_cuda *c, const float *X, uint64_t xs, const uint16_t 
     if (!bf16_map(&mw, W, R, K, kTcM) || !bf16_map(&mh, hi, T, K, N) || !bf16_map(&mm, mid, T, K, N) ||
         !bf16_map(&ml, lo, T, K, N)) {
         snprintf(c->info.note, sizeof c->info.note, "tensor map encode failed");
-        return gemm(c, X, xs, W, Y, ys, T, R, K);
+        return X && gemm(c, X, xs, W, Y, ys, T, R, K);
     }
     TcGemmParams p{Y, ys, static_cast<uint32_t>(T), static_cast<uint32_t>(R), static_cast<uint32_t>(K), error, part};
     const uint32_t r32 = static_cast<uint32_t>(R), t32 = static_cast<uint32_t>(T);
@@ -654,6 +658,39 @@ bool projection(plamo_cuda *c, DModel *m, const float *X, uint64_t xs, const uin
                 uint64_t T, uint64_t R, uint64_t K, bool presplit = false, Deferred *defer = nullptr) {
     return projection_with(c, X, xs, W, Y, ys, T, R, K, T <= m->tmax ? m->p_split : nullptr, m->d_error,
                            m->p_splitk, kSplitkFloats, presplit, defer);
+}
+
+// The MLP's gate/up projection of a prompt fused with SwiGLU: token-major
+// tiles of 96 gate rows and the same 96 up rows (two tensor maps over the
+// halves of the [2I][K] weight), whose epilogue writes the BF16 terms of
+// SwiGLU(gate, up) for the down projection into `terms` ([3][T][I]) - the
+// same values swiglu_rows and its split would write, with no [T][2I]
+// round trip through HBM and no launch. The input's terms are in m->p_split.
+// Taken when the tile choice for the [2I][K] projection is 192-row
+// token-major tiles (PLAMO_CUDA_TC_GLU=0 turns it off).
+bool glu_fusable(plamo_cuda *c, DModel *m, const uint16_t *gu, const uint16_t *down, uint64_t T) {
+    return c->tc_glu && m->p_glu && T <= m->tmax && tc_projection(c, gu, T, 2 * m->I, m->H) &&
+           tc_projection(c, down, T, m->H, m->I) && tc_token_cols(c, T, 2 * m->I) == 192;
+}
+
+bool projection_glu(plamo_cuda *c, DModel *m, const uint16_t *gu, uint64_t T) {
+    const uint64_t I = m->I, K = m->H;
+    uint16_t *hi = m->p_split, *mid = hi + T * K, *lo = hi + 2 * T * K;
+    CUtensorMap mw, mu, mh, mm, ml;
+    if (!bf16_map(&mw, gu, I, K, 96) || !bf16_map(&mu, gu + I * K, I, K, 96) || !bf16_map(&mh, hi, T, K, kTcM) ||
+        !bf16_map(&mm, mid, T, K, kTcM) || !bf16_map(&ml, lo, T, K, kTcM)) {
+        snprintf(c->info.note, sizeof c->info.note, "tensor map encode failed");
+        return false;
+    }
+    TcGemmParams p{};
+    p.T = static_cast<uint32_t>(T);
+    p.R = static_cast<uint32_t>(2 * I);
+    p.K = static_cast<uint32_t>(K);
+    p.error = m->d_error;
+    p.glu = m->p_glu;
+    p.glu_plane = T * I;
+    p.glu_inter = static_cast<uint32_t>(I);
+    return launch_tc_tokm<192>(c, mw, mu, mh, mm, ml, p, static_cast<uint32_t>(2 * I), static_cast<uint32_t>(T));
 }
 
 // The RowFuse of a row kernel whose output feeds projection W next (split
@@ -1520,12 +1557,21 @@ bool record_prompt(plamo_cuda *c, DModel *m, uint64_t T, int mode, bool need_all
         if (!launch(c, norm_rows_kernel<ROW_RESID_NORM>, dim3(T), dim3(512), 0, m->p_states,
                     static_cast<const float *>(m->p_branch), L.post, kPostMixerOffset, L.mpre, 1.0f, m->p_norm, H, f))
             return false;
-        if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H, f.split != nullptr)) return false;
-        f = row_fuse(c, m, L.down, T, H, m->I, Deferred{});
-        if (!swiglu_rows(c, m->p_gu, m->I, T, f)) return false;
-        if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I, f.split != nullptr,
-                        tp ? nullptr : &down_parts))
-            return false;
+        if (f.split && glu_fusable(c, m, L.gu, L.down, T)) {
+            // gate/up + SwiGLU in one launch; down reads the terms it wrote.
+            if (!projection_glu(c, m, L.gu, T) ||
+                !projection_with(c, nullptr, 0, L.down, m->p_branch, H, T, H, m->I, m->p_glu, m->d_error,
+                                 m->p_splitk, kSplitkFloats, true, tp ? nullptr : &down_parts))
+                return false;
+        } else {
+            if (!projection(c, m, m->p_norm, H, L.gu, m->p_gu, 2 * m->I, T, 2 * m->I, H, f.split != nullptr))
+                return false;
+            f = row_fuse(c, m, L.down, T, H, m->I, Deferred{});
+            if (!swiglu_rows(c, m->p_gu, m->I, T, f)) return false;
+            if (!projection(c, m, m->p_gu, 2 * m->I, L.down, m->p_branch, H, T, H, m->I, f.split != nullptr,
+                            tp ? nullptr : &down_parts))
+                return false;
+        }
         if (tp && !tp_allreduce_rows(c, m, m->p_branch, T, 2 * l + 1)) return false;
     }
     if (!launch(c, norm_rows_kernel<ROW_RESID>, dim3(T), dim3(512), 0, m->p_states,
@@ -1663,6 +1709,8 @@ struct plamo_cuda *plamo_cuda_open(const struct plamo_cuda_config *config, char 
     c->tc_tokm = tokm && (!strcmp(tokm, "0") || !strcmp(tokm, "1")) ? atoi(tokm) : -1;
     const char *tokn = getenv("PLAMO_CUDA_TC_TOKN");
     c->tc_tokn = tokn && (!strcmp(tokn, "144") || !strcmp(tokn, "160") || !strcmp(tokn, "192")) ? atoi(tokn) : 0;
+    const char *glu = getenv("PLAMO_CUDA_TC_GLU");
+    c->tc_glu = !(glu && !strcmp(glu, "0"));
     const char *ring_kb = getenv("PLAMO_CUDA_GEMV_RING_KB");
     c->gemv_ring_kb = ring_kb ? std::max(16, atoi(ring_kb)) : 96;
     const char *ctas = getenv("PLAMO_CUDA_GEMV_CTAS");
@@ -1995,6 +2043,7 @@ static int prepare_impl(struct plamo_cuda *c, struct model *model, uint64_t head
     m->v_kv = static_cast<float *>(dalloc(c, m.get(), m->L * kVerifyMax * 2 * m->KVW * 4));
     const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(H, m->AW), m->I);
     m->p_split = static_cast<uint16_t *>(dalloc(c, m.get(), 3 * T * kmax * 2));
+    m->p_glu = T > 64 ? static_cast<uint16_t *>(dalloc(c, m.get(), 3 * T * m->I * 2)) : nullptr;
     m->p_splitk = static_cast<float *>(dalloc(c, m.get(), kSplitkFloats * 4));
     for (void *p : m->allocations)
         if (!p) return 0;

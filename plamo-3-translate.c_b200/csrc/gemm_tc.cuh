@@ -93,6 +93,14 @@ struct TcGemmParams {
     uint32_t T, R, K;
     uint32_t *error;
     float *part;  // split K: [splits][T][R] partial tiles
+    // Gate/up pairs (token-major tiles only, glu != nullptr): a tile's first
+    // N/2 weight rows are gate rows [tile*N/2, +N/2) of map_w and the other
+    // N/2 the same up rows of map_u; the epilogue writes the BF16 terms of
+    // SwiGLU(gate, up) to glu ([3][T][glu_inter], planes glu_plane apart)
+    // instead of Y.
+    uint16_t *glu;
+    uint64_t glu_plane;
+    uint32_t glu_inter;
 };
 
 // ---- tcgen05 / TMA primitives ------------------------------------------------
@@ -283,6 +291,30 @@ __device__ __forceinline__ void tc_fold_store(const TcEpilogue &e) {
         for (int j = 0; j < COUNT; ++j) tile[tl * OS + COL0 + j] = sum[j];
         asm volatile("bar.sync 1, %0;" ::"r"(tc_epi_warps<N>() * 32) : "memory");
         const uint32_t ew = e.warp - 2;
+        if (p.glu) {
+            // Columns [0, N/2) are gate rows, [N/2, N) the matching up rows:
+            // SwiGLU, then its hi/mid/lo BF16 terms (the split of
+            // split_hilo_kernel), 32 consecutive outputs per instruction.
+            constexpr uint32_t HN = N / 2;
+            const uint32_t j0 = blockIdx.y * HN;
+            for (uint32_t r = ew; r < kTcM; r += tc_epi_warps<N>()) {
+                const uint32_t t = e.tok0 + r;
+                if (!ok || t >= p.T) continue;
+                for (uint32_t c = e.lane; c < HN; c += 32) {
+                    if (j0 + c >= p.glu_inter) continue;
+                    const float v = swiglu(tile[r * OS + c], tile[r * OS + HN + c]);
+                    const uint16_t h = plamo_bf16_round(v);
+                    const float r1 = __fsub_rn(v, __uint_as_float(static_cast<uint32_t>(h) << 16));
+                    const uint16_t md = plamo_bf16_round(r1);
+                    const float r2 = __fsub_rn(r1, __uint_as_float(static_cast<uint32_t>(md) << 16));
+                    const uint64_t i = static_cast<uint64_t>(t) * p.glu_inter + j0 + c;
+                    p.glu[i] = h;
+                    p.glu[p.glu_plane + i] = md;
+                    p.glu[2 * p.glu_plane + i] = plamo_bf16_round(r2);
+                }
+            }
+            return;
+        }
         for (uint32_t r = ew; r < kTcM; r += tc_epi_warps<N>()) {
             const uint32_t t = e.tok0 + r;
             if (!ok || t >= p.T) continue;
@@ -311,9 +343,9 @@ __device__ __forceinline__ void tc_fold_store(const TcEpilogue &e) {
 //     and a 5120-row projection of 455 tokens is one wave of tiles.
 template <int N, bool TOKM = false>
 __global__ void __launch_bounds__(tc_threads<N>(), 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
-                   const __grid_constant__ CUtensorMap map_mid, const __grid_constant__ CUtensorMap map_lo,
-                   TcGemmParams p, int stages) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_u,
+                   const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_mid,
+                   const __grid_constant__ CUtensorMap map_lo, TcGemmParams p, int stages) {
     extern __shared__ __align__(128) unsigned char tc_smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kTcMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kTcMaxStages];
@@ -347,6 +379,7 @@ __global__ void __launch_bounds__(tc_threads<N>(), 1)
         abort_flag = 0;
         fence_barrier_init();
         prefetch_tensormap(&map_w);
+        if (TOKM && p.glu) prefetch_tensormap(&map_u);
         prefetch_tensormap(&map_hi);
         prefetch_tensormap(&map_mid);
         prefetch_tensormap(&map_lo);
@@ -381,7 +414,13 @@ __global__ void __launch_bounds__(tc_threads<N>(), 1)
             // terms hi, mid(, lo) one after another.
             constexpr uint32_t wofs = TOKM ? kTcTerms * kTcM * 128 : 0;
             constexpr uint32_t tofs = TOKM ? 0 : kTcM * 128, tstep = (TOKM ? kTcM : N) * 128;
-            tma_load_2d(st + wofs, &map_w, kx, static_cast<int>(row0), &full_bar[s]);
+            if (TOKM && p.glu) {  // gate rows, then the same up rows
+                const int g0 = static_cast<int>(blockIdx.y * (N / 2));
+                tma_load_2d(st + wofs, &map_w, kx, g0, &full_bar[s]);
+                tma_load_2d(st + wofs + (N / 2) * 128, &map_u, kx, g0, &full_bar[s]);
+            } else {
+                tma_load_2d(st + wofs, &map_w, kx, static_cast<int>(row0), &full_bar[s]);
+            }
             tma_load_2d(st + tofs, &map_hi, kx, static_cast<int>(tok0), &full_bar[s]);
             tma_load_2d(st + tofs + tstep, &map_mid, kx, static_cast<int>(tok0), &full_bar[s]);
             if constexpr (kTcTerms == 3)
