@@ -470,6 +470,7 @@ def run_ours(args, world, rank, local, dist):
     be.close()
     if rank == 0 and world == 1:
         line["config3_2b_decode"] = decode_2b(args, pkg, local, peak)
+        line["config2_layer"] = layer_config2(pkg, local, peak)
     return line if rank == 0 else None
 
 
@@ -531,6 +532,56 @@ def decode_2b(args, pkg, local, peak):
         return {"value": steps / (ms / 1000), "unit": "tok/s", "ms_per_step": ms / steps, "steps": steps,
                 "roofline": {"achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                              "algorithmic_bytes": step_bytes}}
+    finally:
+        be.close()
+
+
+def layer_config2(pkg, local, peak):
+    """BASELINE config 2 on the GPU: one decoder layer at hidden 2048 (Q 16 x
+    128, K/V 4 x 128, SwiGLU 8192, BF16 weights N(0, 0.02) generated in HBM,
+    norm weights 1.0: the time does not depend on their values), one decode
+    step over 511 cached rows of FP32 N(0, 1) keys and
+    values, through plamo_cuda_layer (the reference's plamo_metal_layer
+    entry). Device time per step from the entry's own events
+    (plamo_cuda_info.gpu_seconds), e2e per call with the state's host copies;
+    each step appends one row, so the context grows from 511 to 511 + steps."""
+    lib = pkg.load()
+    prof = pkg.Profile("config2", 2048, 1, 16, 4, 128, 8192, vocab=16, window=2048, pattern=1,
+                       max_position=1024)
+    specs = [pkg.LayerSpec(False, 1024, pkg.rope_frequencies(1e4, 64), 1.0)]
+    be = pkg.Backend(device=local, max_context=1024, max_prefill=64)
+    try:
+        hm = pkg.HostModel(prof, specs, weights="synthetic")
+        be.preload_synthetic(hm, seed=2)
+        rng = np.random.default_rng(0)
+        cached, kvw = 511, 4 * 128
+        c = hm.caches[0]
+        hm.view(c.k, cached * kvw)[:] = rng.normal(0, 1, size=cached * kvw).astype(np.float32)
+        hm.view(c.v, cached * kvw)[:] = rng.normal(0, 1, size=cached * kvw).astype(np.float32)
+        c.count = cached
+        be.prepare(hm)
+        state = rng.normal(0, 1, size=2048).astype(np.float32)
+        buf = state.copy()
+        for _ in range(3):
+            buf[:] = state
+            assert lib.plamo_cuda_layer(be.ctx, hm.ptr, 0, buf.ctypes.data) == 1, be.info().note
+        steps = 200
+        g0, t0 = be.info().gpu_seconds, time.perf_counter()
+        for _ in range(steps):
+            buf[:] = state
+            assert lib.plamo_cuda_layer(be.ctx, hm.ptr, 0, buf.ctypes.data) == 1, be.info().note
+        wall = (time.perf_counter() - t0) / steps
+        dev = (be.info().gpu_seconds - g0) / steps
+        weights = 2 * (prof.hidden * (prof.qh + 2 * prof.kh) * prof.dim + prof.hidden * prof.qh * prof.dim +
+                       2 * prof.inter * prof.hidden + prof.hidden * prof.inter)
+        ctx_mean = cached + 3 + (steps + 1) / 2.0
+        step_bytes = weights + ctx_mean * kvw * 4 * 2
+        gbs = step_bytes / dev / 1e9
+        return {"workload": "config 2: one decoder layer, hidden 2048, 511 cached rows, plamo_cuda_layer",
+                "us_per_step": dev * 1e6, "steps": steps,
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "algorithmic_bytes": step_bytes},
+                "e2e": {"us_per_call": wall * 1e6, "h2d_bytes_per_step": 2048 * 4, "d2h_bytes_per_step": 2048 * 4}}
     finally:
         be.close()
 

@@ -156,7 +156,9 @@ int64_t plamo_cuda_generate(struct plamo_cuda *, struct model *, const uint32_t 
                             struct plamo_cuda_timing *timing);
 /* One decoder layer of one decode step on a host hidden vector, in place
    (reference src/layer.s:8-48 plamo_layer): appends one KV row to layer
-   `index` and advances only that layer. */
+   `index` and advances only that layer. The layer's launches are recorded
+   as a CUDA graph on its first call and replayed after (positions and KV
+   pages are read on the device). */
 int plamo_cuda_layer(struct plamo_cuda *, struct model *, uint64_t index, float *state);
 /* Drop the newest `rows` committed rows of every layer of `model` (at most
    PLAMO_CUDA_VERIFY_MAX + 1): the draft model's rollback after a partially

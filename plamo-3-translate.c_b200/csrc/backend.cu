@@ -127,6 +127,8 @@ struct DModel {
     // graph
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
+    std::vector<cudaGraphExec_t> layer_exec;  // plamo_cuda_layer: one recorded step per layer
+    std::vector<uint64_t> layer_nodes;
     uint64_t graph_nodes = 0;
     // persistent decode (one launch per token, single GPU)
     bool pt_ready = false;
@@ -847,6 +849,9 @@ bool kv_copy_rows(plamo_cuda *c, const DModel *m, const DLayer &L, uint64_t rows
 
 void free_model(plamo_cuda *c, DModel *m) {
     if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
+    for (cudaGraphExec_t e : m->layer_exec)
+        if (e) cudaGraphExecDestroy(e);
+    m->layer_exec.clear();
     if (m->graph) cudaGraphDestroy(m->graph);
     for (uint32_t r = 0; r < m->tp.size; ++r)
         if (r != m->tp.rank && m->tp.peer[r]) cudaIpcCloseMemHandle(m->tp.peer[r]);
@@ -2358,24 +2363,12 @@ int plamo_cuda_read_weights(struct plamo_cuda *c, const void *key, void *dst, ui
     return note(c, "read weights", cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost)) ? 1 : 0;
 }
 
-int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, float *state) {
-    if (!c || !state) return 0;
-    cudaSetDevice(c->device);
-    DModel *m = find_model(c, model);
-    if (!m || index >= m->L || m->tp.size) {
-        c->info.declines++;
-        return 0;
-    }
-    if (!reconcile(c, m)) return -1;
+// One decoder layer's decode step for plamo_cuda_layer: state[0] -> state[1],
+// the layer's K/V row appended (positions and page tables are read on the
+// device, so the sequence is recorded once per layer and replayed).
+bool record_layer(plamo_cuda *c, DModel *m, uint64_t index) {
     DLayer &L = m->layers[index];
-    if (!L.sliding && (L.appended + 1 > L.capacity || L.appended + 1 > L.ring || !kv_map(c, m, L, L.appended + 1))) {
-        c->info.declines++;
-        return 0;
-    }
-    m->verify_valid = false;
-    bool ok = note(c, "layer state", cudaMemcpyAsync(m->state[0], state, m->H * 4, cudaMemcpyHostToDevice,
-                                                     c->stream));
-    cudaEventRecord(c->ev0, c->stream);
+    bool ok = true;
     GemvParams p{};
     p.w = L.qkv_w;
     p.rows = m->QW;
@@ -2384,7 +2377,7 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
     p.norm2 = L.pre;
     p.off2 = 1.0f;
     p.y = m->qkv;
-    ok = ok && gemv<PRO_NORM, EPI_STORE>(c, p);
+    ok = gemv<PRO_NORM, EPI_STORE>(c, p);
     ok = ok && launch_decode_attention(c, m, index);
     GemvParams o{};
     o.w = L.o_w;
@@ -2417,6 +2410,50 @@ int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, 
                       static_cast<const float *>(m->branch), L.mpost, kPostMlpOffset,
                       static_cast<const uint16_t *>(nullptr), 0.0f, static_cast<float *>(nullptr), m->H, RowFuse{});
     ok = ok && launch(c, advance_kernel, dim3(1), dim3(32), 0, m->d_appended + index, uint64_t{1}, uint64_t{1});
+    return ok;
+}
+
+int plamo_cuda_layer(struct plamo_cuda *c, struct model *model, uint64_t index, float *state) {
+    if (!c || !state) return 0;
+    cudaSetDevice(c->device);
+    DModel *m = find_model(c, model);
+    if (!m || index >= m->L || m->tp.size) {
+        c->info.declines++;
+        return 0;
+    }
+    if (!reconcile(c, m)) return -1;
+    DLayer &L = m->layers[index];
+    if (!L.sliding && (L.appended + 1 > L.capacity || L.appended + 1 > L.ring || !kv_map(c, m, L, L.appended + 1))) {
+        c->info.declines++;
+        return 0;
+    }
+    m->verify_valid = false;
+    if (m->layer_exec.size() != m->L) {
+        m->layer_exec.assign(m->L, nullptr);
+        m->layer_nodes.assign(m->L, 0);
+    }
+    if (!m->layer_exec[index]) {  // record this layer's launches once
+        if (!note(c, "capture", cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal))) return -1;
+        const uint64_t before = c->info.launches;
+        const bool rec = record_layer(c, m, index);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+        m->layer_nodes[index] = c->info.launches - before;
+        c->info.launches = before;
+        const bool inst = rec && note(c, "capture end", e) &&
+                          note(c, "instantiate", cudaGraphInstantiate(&m->layer_exec[index], graph, 0));
+        if (graph) cudaGraphDestroy(graph);
+        if (!inst) {
+            m->layer_exec[index] = nullptr;
+            return -1;
+        }
+    }
+    bool ok = note(c, "layer state", cudaMemcpyAsync(m->state[0], state, m->H * 4, cudaMemcpyHostToDevice,
+                                                     c->stream));
+    cudaEventRecord(c->ev0, c->stream);
+    ok = ok && note(c, "layer graph", cudaGraphLaunch(m->layer_exec[index], c->stream));
+    c->info.graph_launches++;
+    c->info.launches += m->layer_nodes[index];
     cudaEventRecord(c->ev1, c->stream);
     ok = ok && note(c, "layer out", cudaMemcpyAsync(state, m->state[1], m->H * 4, cudaMemcpyDeviceToHost,
                                                     c->stream)) &&

@@ -72,3 +72,28 @@ def test_config2_single_layer_decode_step(backend):
     assert_close(ra, rb, "rotated K")
     # the cached rows came back bit-exact (only row 511 is new)
     assert np.array_equal(ka[:511 * 512], kb[:511 * 512])
+
+
+def test_config2_repeated_steps_replay_the_recorded_layer(backend):
+    """plamo_cuda_layer records each layer's launches once and replays them:
+    the cache position and the KV page of every later step are read on the
+    device, so consecutive steps (rows 511..515, new input states) must each
+    match the oracle, which appends the same rows."""
+    pkg = load_package()
+    a, b, _ = config2_pair(pkg, seed=1)
+    backend.preload_model(a)
+    backend.prepare(a)
+    rng = np.random.default_rng(77)
+    for step in range(5):
+        state = rng.normal(0, 1, size=2048).astype(np.float32)
+        got = state.copy()
+        assert backend.lib.plamo_cuda_layer(backend.ctx, a.ptr, 0, got.ctypes.data) == 1
+        want = oracle_layer(b, state)
+        assert_close(got, want, f"layer output, step {step}")
+        assert a.caches[0].count == b.caches[0].count == 512 + step
+    assert backend.info().graph_launches >= 5
+    assert backend.lib.plamo_cuda_sync_host(backend.ctx, a.ptr) == 1
+    ka, va, _ = a.kv_arrays(0)
+    kb, vb, _ = b.kv_arrays(0)
+    assert_close(ka, kb, "K")
+    assert_close(va, vb, "V")
